@@ -1,0 +1,340 @@
+#!/usr/bin/env python3
+"""Decode throughput of the B200 GPT-2 engine -- BASELINE.json's metric.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1|c3|c4|c5] [--impl ours|reference]
+
+Workload (default ``c1``, BASELINE.json configs[0] -- the configuration the
+north star's B=1 target is quoted on): GPT-2 small, fp32, random N(0, 0.02)
+weights, batch 1, a 64-token seeded prompt, then 128 greedy decode steps.
+One *step* is one such generation per GPU (prefill + 128 decode steps, all
+on the device).  ``value`` is decode tokens per second over all GPUs:
+sum(decode steps) / device time of the decode phases, timed with CUDA
+events on the engine's stream and taken as the max over ranks; prefill time
+is reported beside it.  N GPUs run N independent sequences (replicas of the
+weights, no collective on the data path): weak scaling.
+
+``e2e`` times the same workload through the C ABI as a host program drives
+it -- g2_prefill, then per token g2_decode (token + position copied from
+pinned host memory) and g2_argmax (the token read back) -- wall-clock.
+
+``--impl reference`` runs the reference's own prefill()/decode()/
+sample_next_token() (main.c + math.cl compiled for the host CPU,
+oracle/_ref) on this machine's cores, for a bounded sample of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "gpt2-opencl-1.1_b200")
+for _p in (PKG, os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+CONFIGS = {
+    # name: shape, dtype, sequences per GPU, prompt, decode steps
+    "c1": dict(shape="SMALL", dtype="f32", batch=1, prompt=64, steps=128, desc="GPT-2 small fp32 B=1 prompt 64 + 128 greedy decode steps"),
+    "c3": dict(shape="SMALL", dtype="f32", batch=1, prompt=512, steps=511, desc="GPT-2 small fp32 B=1 prompt 512 + 511 greedy decode steps (fills ctx 1024)"),
+    "c4": dict(shape="MEDIUM", dtype="f16", batch=32, prompt=256, steps=256, desc="GPT-2 medium fp16, 32 sequences, prompt 256 + 256 greedy steps"),
+    "c5": dict(shape="XL", dtype="f32", batch=32, prompt=128, steps=384, desc="GPT-2 XL fp32, 32 sequences per GPU, prompt 128 + 384 greedy steps"),
+}
+README_DECODE_MS = 40.2   # reference, GT 730, GPT-2 small fp32 B=1 (README.md:59)
+MODEL_CACHE = os.environ.get("G2_MODEL_CACHE", os.path.join(ROOT, "_work", "models"))
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    return ws, int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.path = os.path.join(ROOT, "_work", f"clocks_{os.getpid()}.csv")
+        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        self.p = None
+
+    def start(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.close()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            c = [x.strip() for x in line.split(",")]
+            if len(c) < 9:
+                continue
+            try:
+                sm.append(float(c[1]))
+                mx = max(mx, float(c[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, c[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def model_for(cfg):
+    from gpt2b200 import synth
+    shape = getattr(synth, cfg["shape"])
+    name = f"{cfg['shape'].lower()}_{cfg['dtype']}_s0"
+    return synth.ensure_model(os.path.join(MODEL_CACHE, name), shape, seed=0, dtype=cfg["dtype"]), shape
+
+
+def kv_bytes(shape, elem, prompt, steps, batch):
+    """KV read + write bytes of `steps` decode steps after a `prompt`-token prefill (per sequence x batch)."""
+    L, E = shape.n_layer, shape.n_embd
+    rd = sum(elem * L * 2 * E * (prompt + s + 1) for s in range(steps))
+    wr = elem * L * 2 * E * steps
+    return (rd + wr) * batch
+
+
+def cpu_sample(cfg, seconds=12.0, force_reference=False):
+    """The reference's own code (oracle/_ref) on this host's cores for a bounded sample:
+    prefill of the prompt, then decode steps until ~`seconds` have passed."""
+    import oracle
+    d, shape = model_for(cfg)
+    from gpt2b200 import synth
+    prompt = synth.prompt_ids(0, cfg["prompt"])
+    if (oracle.ref_available() and oracle.ref_fast()) or force_reference:
+        ref, kind = oracle.RefMain(d), "reference"
+        cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    else:
+        ref, kind = oracle.RefModel(d), "port"
+        cores = oracle.cpu_lib().ref_num_threads()
+    t0 = time.perf_counter()
+    ref.prefill(prompt)
+    t_pre = time.perf_counter() - t0
+    ids = [int(t) for t in prompt]
+    lg = ref.logits()
+    tok = int(np.argmax(np.where(np.arange(len(lg)) == 50256, -np.inf, lg[:len(lg)])[:shape.vocab_size]))
+    n, t0 = 0, time.perf_counter()
+    while n < cfg["steps"] and (time.perf_counter() - t0 < seconds or n < 2):
+        ids.append(tok)
+        ref.decode(tok, len(ids) - 1)
+        lg = ref.logits()[:shape.vocab_size]
+        lg[50256] = -np.inf
+        tok = int(np.argmax(lg))
+        n += 1
+    t_dec = time.perf_counter() - t0
+    ref.close()
+    return {"value": round(n / t_dec, 4), "unit": "tok/s", "cores": cores, "kind": kind,
+            "sample": f"prefill {cfg['prompt']} tokens ({t_pre:.1f} s) + {n} greedy decode steps of the {cfg['shape']} "
+                      f"workload, batch 1 (per-sequence rate)", "prefill_s": round(t_pre, 3)}
+
+
+def run_reference(args, cfg):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    try:
+        import oracle
+        if not oracle.ref_available():
+            raise RuntimeError("oracle/_ref not built")
+    except Exception as ex:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU build missing: {ex}"}))
+        return
+    per = []
+    total_steps = args.warmup + args.steps
+    budget = max(4.0, 150.0 / max(total_steps, 1))
+    for i in range(total_steps):
+        r = cpu_sample(cfg, seconds=budget)
+        if i >= args.warmup:
+            per.append(r)
+    val = statistics.mean(p["value"] for p in per)
+    line = {"metric": "decode tok/s (B=1 ms/token; batched) + HBM GB/s % of peak", "value": round(val, 4),
+            "unit": "tok/s", "impl": "reference", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1000.0 / val, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": round(val / (1000.0 / README_DECODE_MS), 4), "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.config, "description": cfg["desc"], "sequences_per_gpu": 1},
+            "cpu_baseline": {k: per[-1][k] for k in ("kind", "cores", "sample")} | {"value": round(val, 4), "unit": "tok/s"},
+            "e2e": {"value": round(val, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_ours(args, cfg):
+    import torch
+    ws, rank, local = dist_env()
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    import gpt2b200 as g2
+    from gpt2b200 import synth
+    d, shape = model_for(cfg)
+    B = cfg["batch"]
+    dtype = g2.G2_F16 if cfg["dtype"] == "f16" else g2.G2_F32
+    eng = g2.Engine(d, device=local if ws > 1 else 0, max_batch=B, dtype=dtype)
+    n_new = cfg["steps"] + 1
+    prompts = [synth.prompt_ids(1000 * rank + i, cfg["prompt"]) for i in range(B)]
+
+    def one_step():
+        if B == 1:
+            eng.generate(prompts[0], n_new)
+        else:
+            eng.generate_batch(prompts, n_new)
+        pre, dec, nd = eng.last_timing()
+        return pre, dec, nd
+
+    for _ in range(args.warmup):
+        one_step()
+    barrier = (lambda: (dist.barrier(), torch.cuda.synchronize())) if ws > 1 else torch.cuda.synchronize
+    clocks = Clocks(local)
+    barrier()
+    clocks.start()
+    l0 = eng.launch_count()
+    t0 = time.perf_counter()
+    pre_ms = dec_ms = 0.0
+    dec_steps = 0
+    for _ in range(args.steps):
+        p, dm, nd = one_step()
+        pre_ms += p
+        dec_ms += dm
+        dec_steps += nd
+    eng.synchronize()
+    wall = time.perf_counter() - t0
+    barrier()
+    clk = clocks.stop()
+    launches = eng.launch_count() - l0
+    # e2e: the same workload through the host-driven C ABI calls
+    e2e_t = 0.0
+    e2e_tokens = 0
+    h2d = d2h = 0
+    if B == 1:
+        for _ in range(max(1, min(args.steps, 3))):
+            t1 = time.perf_counter()
+            eng.prefill(prompts[0])
+            tok, _ = eng.argmax(forbid_eos=True)
+            pos = cfg["prompt"]
+            for s in range(cfg["steps"]):
+                eng.decode(tok, pos + s)
+                tok, _ = eng.argmax(forbid_eos=True)
+            e2e_t += time.perf_counter() - t1
+            e2e_tokens += cfg["steps"]
+        h2d = 3 * 4 * cfg["prompt"] + 32 * cfg["steps"]
+        d2h = 8 * (cfg["steps"] + 1)
+    elif args.steps > 0:
+        t1 = time.perf_counter()
+        eng.generate_batch(prompts, n_new)
+        e2e_t = time.perf_counter() - t1
+        e2e_tokens = cfg["steps"] * B
+        h2d = 4 * B * cfg["prompt"] * 3 + 12 * B
+        d2h = 4 * B * n_new
+    cfgd = eng.cfg
+    elem = 2 if cfg["dtype"] == "f16" else 4
+    per_seq_kv = kv_bytes(shape, elem, cfg["prompt"], cfg["steps"], 1)
+    bytes_per_step = cfgd.weight_bytes + per_seq_kv * B / cfg["steps"] + B * (2 * shape.n_embd * elem + 4 * shape.padded_vocab)
+    t_local = torch.tensor([dec_ms, pre_ms, wall], dtype=torch.float64, device="cuda")
+    if ws > 1:
+        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
+    dec_max, pre_max, wall_max = [float(x) for x in t_local.tolist()]
+    e2e_local = torch.tensor([e2e_t], dtype=torch.float64, device="cuda")
+    if ws > 1:
+        dist.all_reduce(e2e_local, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        total_tokens = dec_steps * B * ws
+        value = total_tokens / (dec_max / 1000.0)
+        step_s = dec_max / 1000.0 / max(dec_steps, 1)            # seconds per decode step (all B rows)
+        achieved = bytes_per_step / step_s / 1e9
+        peak, peak_kind = peaks()
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", f"traffic_{args.config}.json")
+        if os.path.exists(tp):
+            traffic = json.load(open(tp)).get("bytes_per_decode_step")
+        line = {
+            "metric": "decode tok/s (B=1 ms/token; batched) + HBM GB/s % of peak",
+            "value": round(value, 3), "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round((dec_max + pre_max) / max(args.steps, 1), 4),
+            "ms_per_token": round(1000.0 * step_s, 5),
+            "prefill_ms": round(pre_max / max(args.steps, 1), 4),
+            "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": round((value / ws) / (1000.0 / README_DECODE_MS), 2) if args.config in ("c1", "c3") else None,
+            "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,0.02) weights, seeded uniform prompt ids)",
+            "config": {"workload": args.config, "description": cfg["desc"], "sequences_per_gpu": B,
+                       "decode_steps_per_step": cfg["steps"], "parallelism": f"replicas x{ws} (independent sequences)",
+                       "l2": f"weights {cfgd.weight_bytes / 1e6:.0f} MB per decode step > 126 MB L2 (no flush needed)"},
+            "roofline": {"bound": "hbm", "kernel": "decode step (embed + 5 kernels/layer + lm_head, CUDA graph)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "bytes_per_step": int(bytes_per_step), "traffic": traffic},
+            "e2e": {"value": round(e2e_tokens * ws / e2e_local.item(), 3) if e2e_t > 0 else None, "unit": "tok/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "g2_prefill + per-token g2_decode/g2_argmax (C ABI, host buffers)" if B == 1 else "g2_generate_batch"},
+            "gpu_launches": int(launches) * ws,
+            "wall_s": round(wall_max, 4),
+        }
+        if clk:
+            line["clocks"] = clk
+        if ws == 1 and not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_sample(cfg)
+            except Exception as ex:   # reported, never fatal
+                line["cpu_baseline"] = {"error": str(ex)}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = dict(CONFIGS[args.config])
+    ws, _, _ = dist_env()
+    if args.config == "c4":
+        cfg["batch"] = max(1, 32 // ws)   # 32 sequences in total: strong scaling across GPUs
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,898 @@
+// g2_engine.cu -- the C ABI (include/gpt2b200.h): model loading, KV caches,
+// prefill / decode orchestration, CUDA-graph decode steps, device greedy loop.
+//
+// Orchestration follows the reference's prefill() and decode()
+// (main.c:1739-1833), with its 147 launches per decoded token replaced by
+// 2 + 5 * n_layer fused kernels captured once in a CUDA graph; the token and
+// position live in device memory (StepState) so one graph serves every step,
+// and greedy generation runs with no host round trip per token.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "g2_internal.h"
+#include "g2_loader.h"
+#include "gpt2b200.h"
+
+using namespace g2;
+
+// ------------------------------------------------------------------------------
+// errors
+// ------------------------------------------------------------------------------
+static thread_local std::string t_err;
+
+static int set_err(int code, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_err = buf;
+    return code;
+}
+
+extern "C" const char *g2_last_error(void) { return t_err.c_str(); }
+
+#define CK(call)                                                                                              \
+    do {                                                                                                      \
+        cudaError_t e_ = (call);                                                                              \
+        if (e_ != cudaSuccess)                                                                                \
+            return set_err(e_ == cudaErrorMemoryAllocation ? G2_ERR_OOM : G2_ERR_CUDA, "%s: %s (%s:%d)", #call, \
+                           cudaGetErrorString(e_), __FILE__, __LINE__);                                       \
+    } while (0)
+#define CKL()                                                                                        \
+    do {                                                                                             \
+        cudaError_t e_ = cudaGetLastError();                                                         \
+        if (e_ != cudaSuccess)                                                                       \
+            return set_err(G2_ERR_CUDA, "kernel launch: %s (%s:%d)", cudaGetErrorString(e_), __FILE__, \
+                           __LINE__);                                                                \
+    } while (0)
+
+// ------------------------------------------------------------------------------
+// engine state
+// ------------------------------------------------------------------------------
+struct LayerOff {
+    size_t ln1_g, ln1_b, qkv_w, qkv_b, proj_w, proj_b, ln2_g, ln2_b, fc_w, fc_b, fc2_w, fc2_b;
+};
+
+struct g2_engine {
+    int device = 0, dtype = G2_F32, max_batch = 1, sms = 148;
+    ModelConfig c;
+    cudaStream_t st = nullptr;
+    // weights: one allocation, element offsets per tensor
+    void *wbuf = nullptr;
+    size_t welem = 0, esize = 4;
+    size_t wte = 0, wpe = 0, lnf_g = 0, lnf_b = 0, lm = 0;
+    std::vector<LayerOff> L;
+    size_t stream_bytes = 0, device_bytes = 0;
+    // KV caches
+    void *kbuf = nullptr, *vbuf = nullptr;
+    KVLayout kv{};
+    // workspaces
+    int R = 0;   // rows capacity
+    float *h = nullptr, *xln = nullptr, *qkv = nullptr, *attn = nullptr, *ffn = nullptr;
+    float *logits = nullptr, *logits_rows = nullptr;
+    float *gemv_partial = nullptr, *attn_partial = nullptr, *lm_partial = nullptr;
+    unsigned *gemv_ctr = nullptr, *attn_ctr = nullptr, *lm_ctr = nullptr;
+    int *rows_tok = nullptr, *rows_pos = nullptr, *rows_slot = nullptr;
+    int *result = nullptr, *argmax_out = nullptr, *batch_step = nullptr, *out_tokens = nullptr;
+    StepState *state = nullptr;
+    // pinned staging
+    int *h_rows = nullptr;          // [3][R]
+    StepState *h_state = nullptr;   // ring
+    int h_state_i = 0;
+    int *h_small = nullptr;         // results
+    cudaEvent_t staged = nullptr;
+    GemvPlan plan_qkv{}, plan_proj{}, plan_fc{}, plan_fc2{};
+    std::vector<int> filled;        // positions present in each slot's cache
+    int result_slot = -1;           // slot whose lm_head argmax is in `result`
+    // graphs
+    std::vector<cudaGraphExec_t> dec_graph;
+    int dec_graph_kernels = 0;
+    cudaGraphExec_t batch_graph = nullptr;
+    int batch_graph_n = 0, batch_graph_kernels = 0;
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    float last_prefill_ms = 0, last_decode_ms = 0;
+    int last_decode_steps = 0;
+    long long launches = 0;
+
+    template <typename WT>
+    const WT *w(size_t off) const {
+        return reinterpret_cast<const WT *>(wbuf) + off;
+    }
+};
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+static uint16_t f2h_bits(float f) {
+    __half h = __float2half_rn(f);
+    uint16_t u;
+    memcpy(&u, &h, 2);
+    return u;
+}
+
+// ------------------------------------------------------------------------------
+// open / close
+// ------------------------------------------------------------------------------
+static void free_engine(g2_engine *e) {
+    if (!e) return;
+    cudaSetDevice(e->device);
+    if (e->st) cudaStreamSynchronize(e->st);
+    for (auto g : e->dec_graph)
+        if (g) cudaGraphExecDestroy(g);
+    if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
+    void *dev_ptrs[] = {e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
+                        e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
+                        e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
+                        e->argmax_out, e->batch_step, e->out_tokens, e->state};
+    for (void *p : dev_ptrs)
+        if (p) cudaFree(p);
+    if (e->h_rows) cudaFreeHost(e->h_rows);
+    if (e->h_state) cudaFreeHost(e->h_state);
+    if (e->h_small) cudaFreeHost(e->h_small);
+    if (e->staged) cudaEventDestroy(e->staged);
+    for (auto &ev : e->ev)
+        if (ev) cudaEventDestroy(ev);
+    if (e->st) cudaStreamDestroy(e->st);
+    delete e;
+}
+
+template <typename T>
+static int dalloc(g2_engine *e, T **p, size_t count) {
+    const size_t bytes = align_up(count * sizeof(T), 256);
+    cudaError_t r = cudaMalloc((void **)p, bytes);
+    if (r != cudaSuccess)
+        return set_err(G2_ERR_OOM, "cudaMalloc(%zu bytes): %s", bytes, cudaGetErrorString(r));
+    e->device_bytes += bytes;
+    r = cudaMemset(*p, 0, bytes);
+    if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(r));
+    return G2_OK;
+}
+
+// Load every tensor into one device buffer, converted to the engine dtype.
+static int load_weights(g2_engine *e, const std::string &dir) {
+    std::string err;
+    SafeTensors sf;
+    int rc = sf.open(dir + "/model.safetensors", err);
+    if (rc) return set_err(rc, "%s", err.c_str());
+    const ModelConfig &c = e->c;
+    const int E = c.n_embd, F = c.ffn_dim, V = c.vocab_size;
+    // detect_weight_layout (main.c:1234-1250)
+    const StTensor *probe = sf.find("h.0.attn.c_attn.weight");
+    if (!probe || probe->shape.size() != 2) return set_err(G2_ERR_FORMAT, "cannot find h.0.attn.c_attn.weight");
+    bool conv1d;
+    if (probe->shape[0] == E && probe->shape[1] == 3 * E) conv1d = true;
+    else if (probe->shape[0] == 3 * E && probe->shape[1] == E) conv1d = false;
+    else return set_err(G2_ERR_FORMAT, "h.0.attn.c_attn.weight: unexpected shape [%lld,%lld]",
+                        (long long)probe->shape[0], (long long)probe->shape[1]);
+    const StTensor *lmt = sf.find("lm_head.weight");
+
+    // layout plan
+    struct Item {
+        std::string name;
+        size_t *off;
+        int rows, cols;      // as stored on the device: [rows][cols]
+        int kind;            // 0 vector/plain, 1 linear weight [in][out], 2 lm_head
+    };
+    std::vector<Item> items;
+    e->L.resize(c.n_layer);
+    items.push_back({"wte.weight", &e->wte, V, E, 0});
+    items.push_back({"wpe.weight", &e->wpe, c.n_ctx, E, 0});
+    for (int l = 0; l < c.n_layer; ++l) {
+        LayerOff &o = e->L[l];
+        const std::string p = "h." + std::to_string(l) + ".";
+        items.push_back({p + "ln_1.weight", &o.ln1_g, 1, E, 0});
+        items.push_back({p + "ln_1.bias", &o.ln1_b, 1, E, 0});
+        items.push_back({p + "attn.c_attn.weight", &o.qkv_w, E, 3 * E, 1});
+        items.push_back({p + "attn.c_attn.bias", &o.qkv_b, 1, 3 * E, 0});
+        items.push_back({p + "attn.c_proj.weight", &o.proj_w, E, E, 1});
+        items.push_back({p + "attn.c_proj.bias", &o.proj_b, 1, E, 0});
+        items.push_back({p + "ln_2.weight", &o.ln2_g, 1, E, 0});
+        items.push_back({p + "ln_2.bias", &o.ln2_b, 1, E, 0});
+        items.push_back({p + "mlp.c_fc.weight", &o.fc_w, E, F, 1});
+        items.push_back({p + "mlp.c_fc.bias", &o.fc_b, 1, F, 0});
+        items.push_back({p + "mlp.c_proj.weight", &o.fc2_w, F, E, 1});
+        items.push_back({p + "mlp.c_proj.bias", &o.fc2_b, 1, E, 0});
+    }
+    items.push_back({"ln_f.weight", &e->lnf_g, 1, E, 0});
+    items.push_back({"ln_f.bias", &e->lnf_b, 1, E, 0});
+    if (lmt) items.push_back({"lm_head.weight", &e->lm, V, E, 2});
+    size_t off = 0;
+    for (auto &it : items) {
+        *it.off = off;
+        off = align_up(off + (size_t)it.rows * it.cols, 128);
+    }
+    if (!lmt) e->lm = e->wte;   // tied head (main.c:1374-1386)
+    e->welem = off;
+    const size_t bytes = off * e->esize;
+    cudaError_t r = cudaMalloc(&e->wbuf, bytes);
+    if (r != cudaSuccess) return set_err(G2_ERR_OOM, "cudaMalloc weights (%zu bytes): %s", bytes, cudaGetErrorString(r));
+    e->device_bytes += bytes;
+
+    std::vector<float> tmp, tr;
+    std::vector<uint16_t> hv;
+    for (auto &it : items) {
+        const StTensor *t = sf.find(it.name);
+        if (!t) return set_err(G2_ERR_FORMAT, "tensor '%s' not found", it.name.c_str());
+        const size_t n = (size_t)it.rows * it.cols;
+        if ((size_t)t->numel() != n) return set_err(G2_ERR_FORMAT, "tensor '%s': %lld elements, expected %zu",
+                                                    it.name.c_str(), (long long)t->numel(), n);
+        tmp.resize(n);
+        rc = sf.read_f32(*t, tmp.data(), err);
+        if (rc) return set_err(rc, "%s", err.c_str());
+        const float *src = tmp.data();
+        if (it.kind == 1) {
+            // Conv1D [in,out] is kept; nn.Linear [out,in] is transposed (main.c:1252-1300)
+            const int in = it.rows, out = it.cols;
+            if (t->shape.size() != 2) return set_err(G2_ERR_FORMAT, "tensor '%s' is not 2-D", it.name.c_str());
+            if (conv1d) {
+                if (t->shape[0] != in || t->shape[1] != out)
+                    return set_err(G2_ERR_FORMAT, "tensor '%s': expected [%d,%d]", it.name.c_str(), in, out);
+            } else {
+                if (t->shape[0] != out || t->shape[1] != in)
+                    return set_err(G2_ERR_FORMAT, "tensor '%s': expected [%d,%d]", it.name.c_str(), out, in);
+                tr.resize(n);
+                for (int o = 0; o < out; ++o)
+                    for (int i = 0; i < in; ++i) tr[(size_t)i * out + o] = tmp[(size_t)o * in + i];
+                src = tr.data();
+            }
+        } else if (it.kind == 2) {
+            // lm_head.weight [V,E] is kept; [E,V] is transposed (main.c:1387-1410)
+            if (t->shape.size() != 2) return set_err(G2_ERR_FORMAT, "lm_head.weight is not 2-D");
+            if (t->shape[0] == E && t->shape[1] == V) {
+                tr.resize(n);
+                for (int k = 0; k < E; ++k)
+                    for (int v = 0; v < V; ++v) tr[(size_t)v * E + k] = tmp[(size_t)k * V + v];
+                src = tr.data();
+            } else if (!(t->shape[0] == V && t->shape[1] == E)) {
+                return set_err(G2_ERR_FORMAT, "lm_head.weight: unexpected shape");
+            }
+        }
+        void *dst = (char *)e->wbuf + *it.off * e->esize;
+        if (e->dtype == G2_F32) {
+            r = cudaMemcpy(dst, src, n * 4, cudaMemcpyHostToDevice);
+        } else {
+            hv.resize(n);
+            for (size_t i = 0; i < n; ++i) hv[i] = f2h_bits(src[i]);
+            r = cudaMemcpy(dst, hv.data(), n * 2, cudaMemcpyHostToDevice);
+        }
+        if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "upload '%s': %s", it.name.c_str(), cudaGetErrorString(r));
+    }
+    // Algorithmic bytes streamed per decode step (weights + biases + LN + lm head).
+    const size_t es = e->esize;
+    e->stream_bytes = es * ((size_t)c.n_layer * ((size_t)4 * E * E + (size_t)2 * E * F) + (size_t)E * c.padded_vocab) +
+                      es * ((size_t)c.n_layer * (9 * (size_t)E + F) + 2 * (size_t)E);
+    return G2_OK;
+}
+
+extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dtype, g2_engine **out) {
+    if (!model_dir || !out) return set_err(G2_ERR_ARG, "g2_open: null argument");
+    *out = nullptr;
+    if (max_batch < 1 || max_batch > 4096) return set_err(G2_ERR_ARG, "g2_open: max_batch out of range");
+    if (dtype != G2_F32 && dtype != G2_F16) return set_err(G2_ERR_ARG, "g2_open: dtype must be G2_F32 or G2_F16");
+    {
+        // Validate the files before touching a device (format errors are reported first).
+        ModelConfig c;
+        std::string err;
+        int rc = load_config(model_dir, c, err);
+        if (!rc) rc = validate_gpt2(model_dir, c, err);
+        if (rc) return set_err(rc, "%s", err.c_str());
+    }
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return set_err(G2_ERR_CUDA, "g2_open: no CUDA device");
+    if (device < 0 || device >= ndev) return set_err(G2_ERR_ARG, "g2_open: device %d of %d", device, ndev);
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) return set_err(G2_ERR_CUDA, "g2_open: device %d is sm_%d%d; this build targets sm_100a",
+                                        device, prop.major, prop.minor);
+    auto *e = new g2_engine;
+    e->device = device;
+    e->dtype = dtype;
+    e->esize = dtype == G2_F32 ? 4 : 2;
+    e->max_batch = max_batch;
+    e->sms = prop.multiProcessorCount;
+    int rc;
+    std::string err;
+    if ((rc = load_config(model_dir, e->c, err))) {
+        delete e;
+        return set_err(rc, "%s", err.c_str());
+    }
+#define TRY(x)                \
+    do {                      \
+        if ((rc = (x))) {     \
+            free_engine(e);   \
+            return rc;        \
+        }                     \
+    } while (0)
+    {
+        cudaError_t r = cudaSetDevice(device);
+        if (r != cudaSuccess) {
+            delete e;
+            return set_err(G2_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(r));
+        }
+        r = cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking);
+        if (r != cudaSuccess) {
+            delete e;
+            return set_err(G2_ERR_CUDA, "cudaStreamCreate: %s", cudaGetErrorString(r));
+        }
+    }
+    TRY(load_weights(e, model_dir));
+    const ModelConfig &c = e->c;
+    const int E = c.n_embd, F = c.ffn_dim, NH = c.n_head, S = c.n_ctx, Vp = c.padded_vocab;
+    // KV caches [slot][layer][head][pos][64]
+    e->kv.max_seq = S;
+    e->kv.n_head = NH;
+    e->kv.layer_stride = (long long)NH * S * kHeadDim;
+    e->kv.slot_stride = e->kv.layer_stride * c.n_layer;
+    const size_t kv_elems = (size_t)e->kv.slot_stride * max_batch;
+    {
+        const size_t bytes = kv_elems * e->esize;
+        cudaError_t r1 = cudaMalloc(&e->kbuf, bytes);
+        cudaError_t r2 = r1 == cudaSuccess ? cudaMalloc(&e->vbuf, bytes) : r1;
+        if (r2 != cudaSuccess) {
+            free_engine(e);
+            return set_err(G2_ERR_OOM, "KV cache (%zu bytes x 2): %s", bytes, cudaGetErrorString(r2));
+        }
+        e->device_bytes += 2 * bytes;
+        e->kv.k = e->kbuf;
+        e->kv.v = e->vbuf;
+    }
+    e->R = S > max_batch ? S : max_batch;
+    const int R = e->R;
+    TRY(dalloc(e, &e->h, (size_t)R * E));
+    TRY(dalloc(e, &e->xln, (size_t)R * E));
+    TRY(dalloc(e, &e->qkv, (size_t)R * 3 * E));
+    TRY(dalloc(e, &e->attn, (size_t)R * E));
+    TRY(dalloc(e, &e->ffn, (size_t)R * F));
+    TRY(dalloc(e, &e->logits, (size_t)max_batch * Vp));
+    TRY(dalloc(e, &e->logits_rows, (size_t)max_batch * Vp));
+    if (dtype == G2_F32) {
+        e->plan_qkv = gemv_plan<float>(3 * E, E, e->sms);
+        e->plan_proj = gemv_plan<float>(E, E, e->sms);
+        e->plan_fc = gemv_plan<float>(F, E, e->sms);
+        e->plan_fc2 = gemv_plan<float>(E, F, e->sms);
+    } else {
+        e->plan_qkv = gemv_plan<__half>(3 * E, E, e->sms);
+        e->plan_proj = gemv_plan<__half>(E, E, e->sms);
+        e->plan_fc = gemv_plan<__half>(F, E, e->sms);
+        e->plan_fc2 = gemv_plan<__half>(E, F, e->sms);
+    }
+    size_t gp = 0, gt = 0;
+    const GemvPlan plans[4] = {e->plan_qkv, e->plan_proj, e->plan_fc, e->plan_fc2};
+    const int Ns[4] = {3 * E, E, F, E};
+    for (int i = 0; i < 4; ++i) {
+        gp = std::max(gp, (size_t)plans[i].ksplit * Ns[i]);
+        gt = std::max(gt, (size_t)plans[i].tiles);
+    }
+    TRY(dalloc(e, &e->gemv_partial, gp));
+    TRY(dalloc(e, &e->gemv_ctr, gt));
+    TRY(dalloc(e, &e->attn_partial, attn_partial_floats(R, NH, S)));
+    TRY(dalloc(e, &e->attn_ctr, attn_counter_count(R, NH)));
+    TRY(dalloc(e, &e->lm_partial, (size_t)2 * lm_head_blocks()));
+    TRY(dalloc(e, &e->lm_ctr, 1));
+    TRY(dalloc(e, &e->rows_tok, R));
+    TRY(dalloc(e, &e->rows_pos, R));
+    TRY(dalloc(e, &e->rows_slot, R));
+    TRY(dalloc(e, &e->result, 2));
+    TRY(dalloc(e, &e->argmax_out, 2 * (size_t)max_batch));
+    TRY(dalloc(e, &e->batch_step, 1));
+    TRY(dalloc(e, &e->out_tokens, (size_t)max_batch * S));
+    TRY(dalloc(e, &e->state, 1));
+    {
+        cudaError_t r = cudaMallocHost(&e->h_rows, sizeof(int) * 3 * (size_t)R);
+        if (r == cudaSuccess) r = cudaMallocHost(&e->h_state, sizeof(StepState) * 64);
+        if (r == cudaSuccess) r = cudaMallocHost(&e->h_small, sizeof(int) * 4 * (size_t)max_batch + 64);
+        if (r == cudaSuccess) r = cudaEventCreateWithFlags(&e->staged, cudaEventDisableTiming);
+        for (auto &ev : e->ev)
+            if (r == cudaSuccess) r = cudaEventCreate(&ev);
+        if (r != cudaSuccess) {
+            free_engine(e);
+            return set_err(G2_ERR_CUDA, "host staging: %s", cudaGetErrorString(r));
+        }
+    }
+    e->filled.assign(max_batch, 0);
+    e->dec_graph.assign(max_batch, nullptr);
+#undef TRY
+    *out = e;
+    return G2_OK;
+}
+
+extern "C" int g2_close(g2_engine *e) {
+    if (!e) return set_err(G2_ERR_ARG, "g2_close: null engine");
+    free_engine(e);
+    return G2_OK;
+}
+
+extern "C" int g2_get_config(const g2_engine *e, g2_config *out) {
+    if (!e || !out) return set_err(G2_ERR_ARG, "g2_get_config: null argument");
+    out->n_layer = e->c.n_layer;
+    out->n_embd = e->c.n_embd;
+    out->n_head = e->c.n_head;
+    out->n_ctx = e->c.n_ctx;
+    out->vocab_size = e->c.vocab_size;
+    out->ffn_dim = e->c.ffn_dim;
+    out->padded_vocab = e->c.padded_vocab;
+    out->dtype = e->dtype;
+    out->max_batch = e->max_batch;
+    out->device = e->device;
+    out->weight_bytes = e->stream_bytes;
+    out->device_bytes = e->device_bytes;
+    return G2_OK;
+}
+
+extern "C" long long g2_launch_count(const g2_engine *e) { return e ? e->launches : -1; }
+
+// ------------------------------------------------------------------------------
+// forward passes
+// ------------------------------------------------------------------------------
+
+// Stage row descriptors (tok, pos, slot) into the device row arrays.
+static int stage_rows(g2_engine *e, int n, const int *tok, const int *pos, const int *slot) {
+    CK(cudaEventSynchronize(e->staged));   // previous staging copy has been consumed
+    int *hr = e->h_rows;
+    memcpy(hr, tok, sizeof(int) * n);
+    memcpy(hr + e->R, pos, sizeof(int) * n);
+    memcpy(hr + 2 * e->R, slot, sizeof(int) * n);
+    CK(cudaMemcpyAsync(e->rows_tok, hr, sizeof(int) * n, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->rows_pos, hr + e->R, sizeof(int) * n, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->rows_slot, hr + 2 * e->R, sizeof(int) * n, cudaMemcpyHostToDevice, e->st));
+    CK(cudaEventRecord(e->staged, e->st));
+    return G2_OK;
+}
+
+// All layers over `nrows` rows described by the device row arrays (prefill of
+// one slot, or one decode token for each of several slots).  Leaves the
+// residual stream in e->h.
+template <typename WT>
+static int forward_rows(g2_engine *e, int nrows, int max_pos) {
+    const ModelConfig &c = e->c;
+    const int E = c.n_embd, F = c.ffn_dim;
+    cudaStream_t st = e->st;
+    Rows rows{e->rows_tok, e->rows_pos, e->rows_slot};
+    launch_embed<WT>(e->w<WT>(e->wte), e->w<WT>(e->wpe), rows, e->h, E, c.vocab_size, c.n_ctx, nrows, st);
+    for (int l = 0; l < c.n_layer; ++l) {
+        const LayerOff &o = e->L[l];
+        launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln1_g), e->w<WT>(o.ln1_b), E, nrows, st);
+        launch_gemm_rows<WT>(e->xln, e->w<WT>(o.qkv_w), e->w<WT>(o.qkv_b), nullptr, e->qkv, nrows, 3 * E, E,
+                             EPI_BIAS | EPI_KV, &e->kv, l, rows, st);
+        launch_attention<WT>(e->qkv, 3 * E, e->kv, l, rows, nrows, e->attn, E, e->attn_partial, e->attn_ctr, max_pos,
+                             st);
+        launch_gemm_rows<WT>(e->attn, e->w<WT>(o.proj_w), e->w<WT>(o.proj_b), e->h, e->h, nrows, E, E,
+                             EPI_BIAS | EPI_RESID, nullptr, l, rows, st);
+        launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln2_g), e->w<WT>(o.ln2_b), E, nrows, st);
+        launch_gemm_rows<WT>(e->xln, e->w<WT>(o.fc_w), e->w<WT>(o.fc_b), nullptr, e->ffn, nrows, F, E,
+                             EPI_BIAS | EPI_GELU, nullptr, l, rows, st);
+        launch_gemm_rows<WT>(e->ffn, e->w<WT>(o.fc2_w), e->w<WT>(o.fc2_b), e->h, e->h, nrows, E, F,
+                             EPI_BIAS | EPI_RESID, nullptr, l, rows, st);
+    }
+    e->launches += 1 + 7LL * c.n_layer;
+    CKL();
+    return G2_OK;
+}
+
+// LM head on row `row` of e->h for `slot`, optionally advancing the step state.
+template <typename WT>
+static int lm_head_row(g2_engine *e, int row, int slot, StepState *state) {
+    const ModelConfig &c = e->c;
+    launch_lm_head<WT>(e->h + (size_t)row * c.n_embd, e->w<WT>(e->lm), e->w<WT>(e->lnf_g), e->w<WT>(e->lnf_b),
+                       e->logits + (size_t)slot * c.padded_vocab, c.n_embd, c.vocab_size, c.padded_vocab, 0,
+                       e->lm_partial, e->lm_ctr, e->result, state,
+                       state ? e->out_tokens + (size_t)slot * c.n_ctx : nullptr, e->st);
+    e->launches += 1;
+    e->result_slot = slot;
+    CKL();
+    return G2_OK;
+}
+
+// One B = 1 decode step driven by e->state (kernels only; captured in a graph).
+template <typename WT>
+static void record_decode_step(g2_engine *e, int slot) {
+    const ModelConfig &c = e->c;
+    const int E = c.n_embd, F = c.ffn_dim;
+    cudaStream_t st = e->st;
+    StepState *s = e->state;
+    Rows rows{&s->token, &s->pos, &s->slot};
+    launch_embed<WT>(e->w<WT>(e->wte), e->w<WT>(e->wpe), rows, e->h, E, c.vocab_size, c.n_ctx, 1, st);
+    for (int l = 0; l < c.n_layer; ++l) {
+        const LayerOff &o = e->L[l];
+        launch_gemv<WT>(e->h, e->w<WT>(o.qkv_w), e->w<WT>(o.qkv_b), nullptr, e->qkv, 3 * E, E, EPI_BIAS | EPI_KV,
+                        e->w<WT>(o.ln1_g), e->w<WT>(o.ln1_b), e->gemv_partial, e->gemv_ctr, e->plan_qkv, &e->kv, l,
+                        &s->pos, &s->slot, st);
+        launch_attention<WT>(e->qkv, 3 * E, e->kv, l, rows, 1, e->attn, E, e->attn_partial, e->attn_ctr, -1, st);
+        launch_gemv<WT>(e->attn, e->w<WT>(o.proj_w), e->w<WT>(o.proj_b), e->h, e->h, E, E, EPI_BIAS | EPI_RESID,
+                        nullptr, nullptr, e->gemv_partial, e->gemv_ctr, e->plan_proj, nullptr, l, nullptr, nullptr,
+                        st);
+        launch_gemv<WT>(e->h, e->w<WT>(o.fc_w), e->w<WT>(o.fc_b), nullptr, e->ffn, F, E, EPI_BIAS | EPI_GELU,
+                        e->w<WT>(o.ln2_g), e->w<WT>(o.ln2_b), e->gemv_partial, e->gemv_ctr, e->plan_fc, nullptr, l,
+                        nullptr, nullptr, st);
+        launch_gemv<WT>(e->ffn, e->w<WT>(o.fc2_w), e->w<WT>(o.fc2_b), e->h, e->h, E, F, EPI_BIAS | EPI_RESID,
+                        nullptr, nullptr, e->gemv_partial, e->gemv_ctr, e->plan_fc2, nullptr, l, nullptr, nullptr,
+                        st);
+    }
+    launch_lm_head<WT>(e->h, e->w<WT>(e->lm), e->w<WT>(e->lnf_g), e->w<WT>(e->lnf_b),
+                       e->logits + (size_t)slot * c.padded_vocab, E, c.vocab_size, c.padded_vocab, 0, e->lm_partial,
+                       e->lm_ctr, e->result, s, e->out_tokens + (size_t)slot * c.n_ctx, st);
+}
+
+static int decode_graph(g2_engine *e, int slot, cudaGraphExec_t *out) {
+    if (e->dec_graph[slot]) {
+        *out = e->dec_graph[slot];
+        return G2_OK;
+    }
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+    if (e->dtype == G2_F32) record_decode_step<float>(e, slot);
+    else record_decode_step<__half>(e, slot);
+    cudaError_t le = cudaGetLastError();
+    cudaError_t r = cudaStreamEndCapture(e->st, &g);
+    if (le != cudaSuccess) return set_err(G2_ERR_CUDA, "decode capture launch: %s", cudaGetErrorString(le));
+    if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "decode capture: %s", cudaGetErrorString(r));
+    size_t nn = 0;
+    cudaGraphGetNodes(g, nullptr, &nn);
+    r = cudaGraphInstantiate(&e->dec_graph[slot], g, 0);
+    cudaGraphDestroy(g);
+    if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(r));
+    e->dec_graph_kernels = (int)nn;
+    *out = e->dec_graph[slot];
+    return G2_OK;
+}
+
+static int check_slot(const g2_engine *e, int slot) {
+    if (slot < 0 || slot >= e->max_batch) return set_err(G2_ERR_RANGE, "slot %d out of range [0,%d)", slot, e->max_batch);
+    return G2_OK;
+}
+
+static int check_ids(const g2_engine *e, const int *ids, int n) {
+    for (int i = 0; i < n; ++i)
+        if (ids[i] < 0 || ids[i] >= e->c.vocab_size)
+            return set_err(G2_ERR_RANGE, "token id %d at index %d out of range [0,%d)", ids[i], i, e->c.vocab_size);
+    return G2_OK;
+}
+
+static int prefill_impl(g2_engine *e, int slot, const int *ids, int n) {
+    int rc;
+    if ((rc = check_slot(e, slot))) return rc;
+    if (!ids || n <= 0 || n > e->c.n_ctx) return set_err(G2_ERR_RANGE, "prefill length %d out of range [1,%d]", n, e->c.n_ctx);
+    if ((rc = check_ids(e, ids, n))) return rc;
+    std::vector<int> pos(n), sl(n, slot);
+    for (int i = 0; i < n; ++i) pos[i] = i;
+    if ((rc = stage_rows(e, n, ids, pos.data(), sl.data()))) return rc;
+    rc = e->dtype == G2_F32 ? forward_rows<float>(e, n, n - 1) : forward_rows<__half>(e, n, n - 1);
+    if (rc) return rc;
+    e->filled[slot] = n;
+    return G2_OK;
+}
+
+extern "C" int g2_prefill(g2_engine *e, int slot, const int *ids, int n) {
+    if (!e) return set_err(G2_ERR_ARG, "null engine");
+    CK(cudaSetDevice(e->device));
+    int rc = prefill_impl(e, slot, ids, n);
+    if (rc) return rc;
+    return e->dtype == G2_F32 ? lm_head_row<float>(e, n - 1, slot, nullptr) : lm_head_row<__half>(e, n - 1, slot, nullptr);
+}
+
+extern "C" int g2_decode(g2_engine *e, int slot, int token, int pos) {
+    if (!e) return set_err(G2_ERR_ARG, "null engine");
+    int rc;
+    if ((rc = check_slot(e, slot))) return rc;
+    if (token < 0 || token >= e->c.vocab_size) return set_err(G2_ERR_RANGE, "token id %d out of range", token);
+    if (pos < 0 || pos >= e->c.n_ctx) return set_err(G2_ERR_RANGE, "position %d out of range [0,%d)", pos, e->c.n_ctx);
+    if (pos > e->filled[slot]) return set_err(G2_ERR_STATE, "position %d but slot %d holds %d positions", pos, slot, e->filled[slot]);
+    CK(cudaSetDevice(e->device));
+    cudaGraphExec_t g;
+    if ((rc = decode_graph(e, slot, &g))) return rc;
+    if (e->h_state_i == 0) CK(cudaStreamSynchronize(e->st));   // ring of pinned states wrapped
+    StepState *hs = e->h_state + e->h_state_i;
+    e->h_state_i = (e->h_state_i + 1) % 64;
+    *hs = StepState{token, pos, slot, 0, 0, {0, 0, 0}};
+    CK(cudaMemcpyAsync(e->state, hs, sizeof(StepState), cudaMemcpyHostToDevice, e->st));
+    CK(cudaGraphLaunch(g, e->st));
+    e->launches += e->dec_graph_kernels;
+    e->filled[slot] = pos + 1;
+    e->result_slot = slot;
+    return G2_OK;
+}
+
+extern "C" int g2_decode_batch(g2_engine *e, int n, const int *slots, const int *tokens, const int *pos) {
+    if (!e || !slots || !tokens || !pos) return set_err(G2_ERR_ARG, "g2_decode_batch: null argument");
+    if (n < 1 || n > e->max_batch) return set_err(G2_ERR_RANGE, "batch %d out of range [1,%d]", n, e->max_batch);
+    int rc, maxp = 0;
+    std::vector<int> seen(e->max_batch, 0);
+    for (int i = 0; i < n; ++i) {
+        if ((rc = check_slot(e, slots[i]))) return rc;
+        if (seen[slots[i]]++) return set_err(G2_ERR_ARG, "slot %d repeated in batch", slots[i]);
+        if (pos[i] < 0 || pos[i] >= e->c.n_ctx) return set_err(G2_ERR_RANGE, "position %d out of range", pos[i]);
+        if (pos[i] > e->filled[slots[i]]) return set_err(G2_ERR_STATE, "slot %d: position %d beyond %d filled", slots[i], pos[i], e->filled[slots[i]]);
+        maxp = std::max(maxp, pos[i]);
+    }
+    if ((rc = check_ids(e, tokens, n))) return rc;
+    CK(cudaSetDevice(e->device));
+    if ((rc = stage_rows(e, n, tokens, pos, slots))) return rc;
+    const ModelConfig &c = e->c;
+    if (e->dtype == G2_F32) {
+        if ((rc = forward_rows<float>(e, n, maxp))) return rc;
+        launch_layernorm<float>(e->h, e->xln, e->w<float>(e->lnf_g), e->w<float>(e->lnf_b), c.n_embd, n, e->st);
+        launch_lm_head_rows<float>(e->xln, e->w<float>(e->lm), e->logits_rows, c.n_embd, c.vocab_size, c.padded_vocab, n, e->st);
+    } else {
+        if ((rc = forward_rows<__half>(e, n, maxp))) return rc;
+        launch_layernorm<__half>(e->h, e->xln, e->w<__half>(e->lnf_g), e->w<__half>(e->lnf_b), c.n_embd, n, e->st);
+        launch_lm_head_rows<__half>(e->xln, e->w<__half>(e->lm), e->logits_rows, c.n_embd, c.vocab_size, c.padded_vocab, n, e->st);
+    }
+    for (int i = 0; i < n; ++i)
+        launch_copy_row(e->logits_rows + (size_t)i * c.padded_vocab, e->logits + (size_t)slots[i] * c.padded_vocab,
+                        c.vocab_size, e->st);
+    e->launches += 2 + n;
+    CKL();
+    for (int i = 0; i < n; ++i) e->filled[slots[i]] = pos[i] + 1;
+    e->result_slot = -1;
+    return G2_OK;
+}
+
+extern "C" int g2_logits(g2_engine *e, int slot, float *host, int n) {
+    if (!e || !host) return set_err(G2_ERR_ARG, "g2_logits: null argument");
+    int rc;
+    if ((rc = check_slot(e, slot))) return rc;
+    if (n < 0 || n > e->c.padded_vocab) return set_err(G2_ERR_RANGE, "g2_logits: n %d > padded_vocab", n);
+    CK(cudaSetDevice(e->device));
+    CK(cudaMemcpyAsync(host, e->logits + (size_t)slot * e->c.padded_vocab, sizeof(float) * n, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    return G2_OK;
+}
+
+extern "C" int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, float *value) {
+    if (!e || !token) return set_err(G2_ERR_ARG, "g2_argmax: null argument");
+    int rc;
+    if ((rc = check_slot(e, slot))) return rc;
+    CK(cudaSetDevice(e->device));
+    const int *src = e->result;
+    if (e->result_slot != slot || forbid_eos) {
+        launch_argmax_rows(e->logits + (size_t)slot * e->c.padded_vocab, e->c.vocab_size, e->c.padded_vocab, 1,
+                           forbid_eos, e->argmax_out, reinterpret_cast<float *>(e->argmax_out + 1), nullptr, nullptr,
+                           nullptr, 0, nullptr, e->st);
+        e->launches += 1;
+        CKL();
+        src = e->argmax_out;
+    }
+    CK(cudaMemcpyAsync(e->h_small, src, 2 * sizeof(int), cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    *token = e->h_small[0];
+    if (value) memcpy(value, &e->h_small[1], 4);
+    return G2_OK;
+}
+
+extern "C" int g2_synchronize(g2_engine *e) {
+    if (!e) return set_err(G2_ERR_ARG, "null engine");
+    CK(cudaSetDevice(e->device));
+    CK(cudaStreamSynchronize(e->st));
+    return G2_OK;
+}
+
+extern "C" int g2_last_timing(g2_engine *e, float *prefill_ms, float *decode_ms, int *decode_steps) {
+    if (!e) return set_err(G2_ERR_ARG, "null engine");
+    if (prefill_ms) *prefill_ms = e->last_prefill_ms;
+    if (decode_ms) *decode_ms = e->last_decode_ms;
+    if (decode_steps) *decode_steps = e->last_decode_steps;
+    return G2_OK;
+}
+
+extern "C" int g2_generate(g2_engine *e, int slot, const int *prompt, int n_prompt, int n_new, int min_new,
+                           int *out_tokens) {
+    if (!e || !prompt || !out_tokens) return set_err(G2_ERR_ARG, "g2_generate: null argument");
+    if (n_new < 1) return set_err(G2_ERR_ARG, "g2_generate: n_new must be >= 1");
+    int rc;
+    if ((rc = check_slot(e, slot))) return rc;
+    if (n_prompt < 1 || n_prompt >= e->c.n_ctx) return set_err(G2_ERR_RANGE, "prompt length %d out of range", n_prompt);
+    // main.c:2126: generation stops when the sequence reaches the context size
+    const int cap = e->c.n_ctx - n_prompt;
+    if (n_new > cap) n_new = cap;
+    CK(cudaSetDevice(e->device));
+    cudaGraphExec_t g;
+    if ((rc = decode_graph(e, slot, &g))) return rc;
+    CK(cudaStreamSynchronize(e->st));
+    StepState *hs = e->h_state + e->h_state_i;
+    e->h_state_i = (e->h_state_i + 1) % 64;
+    *hs = StepState{0, n_prompt - 1, slot, 0, min_new, {0, 0, 0}};
+    CK(cudaEventRecord(e->ev[0], e->st));
+    CK(cudaMemcpyAsync(e->state, hs, sizeof(StepState), cudaMemcpyHostToDevice, e->st));
+    if ((rc = prefill_impl(e, slot, prompt, n_prompt))) return rc;
+    rc = e->dtype == G2_F32 ? lm_head_row<float>(e, n_prompt - 1, slot, e->state)
+                            : lm_head_row<__half>(e, n_prompt - 1, slot, e->state);
+    if (rc) return rc;
+    CK(cudaEventRecord(e->ev[1], e->st));
+    for (int i = 1; i < n_new; ++i) CK(cudaGraphLaunch(g, e->st));
+    e->launches += (long long)(n_new - 1) * e->dec_graph_kernels;
+    CK(cudaEventRecord(e->ev[2], e->st));
+    CK(cudaMemcpyAsync(out_tokens, e->out_tokens + (size_t)slot * e->c.n_ctx, sizeof(int) * n_new,
+                       cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    CK(cudaEventElapsedTime(&e->last_prefill_ms, e->ev[0], e->ev[1]));
+    CK(cudaEventElapsedTime(&e->last_decode_ms, e->ev[1], e->ev[2]));
+    e->last_decode_steps = n_new - 1;
+    e->filled[slot] = n_prompt + n_new - 1;
+    e->result_slot = slot;
+    // EOS ends generation once it is allowed (main.c:2126, 2135)
+    for (int i = 0; i < n_new; ++i)
+        if (out_tokens[i] == kEos && i >= min_new) return i + 1;
+    return n_new;
+}
+
+// One batched greedy decode step for the rows in the device row arrays.
+template <typename WT>
+static int record_batch_step(g2_engine *e, int n) {
+    const ModelConfig &c = e->c;
+    int rc = forward_rows<WT>(e, n, -1);
+    if (rc) return rc;
+    launch_layernorm<WT>(e->h, e->xln, e->w<WT>(e->lnf_g), e->w<WT>(e->lnf_b), c.n_embd, n, e->st);
+    launch_lm_head_rows<WT>(e->xln, e->w<WT>(e->lm), e->logits_rows, c.n_embd, c.vocab_size, c.padded_vocab, n, e->st);
+    launch_argmax_rows(e->logits_rows, c.vocab_size, c.padded_vocab, n, 1, nullptr, nullptr, e->rows_tok,
+                       e->rows_pos, e->out_tokens, c.n_ctx, e->batch_step, e->st);
+    launch_step_advance(e->batch_step, e->st);
+    e->launches += 4;
+    return G2_OK;
+}
+
+extern "C" int g2_generate_batch(g2_engine *e, int n, const int *slots, const int *prompts, const int *prompt_lens,
+                                 int n_new, int *out_tokens) {
+    if (!e || !slots || !prompts || !prompt_lens || !out_tokens) return set_err(G2_ERR_ARG, "g2_generate_batch: null argument");
+    if (n < 1 || n > e->max_batch) return set_err(G2_ERR_RANGE, "batch %d out of range", n);
+    if (n_new < 1) return set_err(G2_ERR_ARG, "n_new must be >= 1");
+    int rc;
+    std::vector<int> seen(e->max_batch, 0);
+    for (int i = 0; i < n; ++i) {
+        if ((rc = check_slot(e, slots[i]))) return rc;
+        if (seen[slots[i]]++) return set_err(G2_ERR_ARG, "slot %d repeated", slots[i]);
+        if (prompt_lens[i] < 1 || prompt_lens[i] + n_new - 1 > e->c.n_ctx)
+            return set_err(G2_ERR_RANGE, "prompt %d: length %d + %d new exceeds context %d", i, prompt_lens[i], n_new, e->c.n_ctx);
+    }
+    CK(cudaSetDevice(e->device));
+    CK(cudaStreamSynchronize(e->st));
+    const ModelConfig &c = e->c;
+    CK(cudaEventRecord(e->ev[0], e->st));
+    // prefill each sequence; its greedy token goes to row i of the batch
+    size_t off = 0;
+    for (int i = 0; i < n; ++i) {
+        if ((rc = prefill_impl(e, slots[i], prompts + off, prompt_lens[i]))) return rc;
+        off += prompt_lens[i];
+        rc = e->dtype == G2_F32 ? lm_head_row<float>(e, prompt_lens[i] - 1, slots[i], nullptr)
+                                : lm_head_row<__half>(e, prompt_lens[i] - 1, slots[i], nullptr);
+        if (rc) return rc;
+        launch_argmax_rows(e->logits + (size_t)slots[i] * c.padded_vocab, c.vocab_size, c.padded_vocab, 1, 1,
+                           e->argmax_out + i, nullptr, nullptr, nullptr, nullptr, 0, nullptr, e->st);
+        e->launches += 1;
+    }
+    CKL();
+    // rows for the decode steps: tok from the prefill argmax, pos = prompt length
+    CK(cudaStreamSynchronize(e->st));
+    std::vector<int> tok(n), pos(n), sl(n);
+    CK(cudaMemcpy(tok.data(), e->argmax_out, sizeof(int) * n, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < n; ++i) {
+        pos[i] = prompt_lens[i];
+        sl[i] = slots[i];
+        out_tokens[(size_t)i * n_new] = tok[i];
+    }
+    if ((rc = stage_rows(e, n, tok.data(), pos.data(), sl.data()))) return rc;
+    int one = 1;
+    CK(cudaMemcpyAsync(e->batch_step, &one, sizeof(int), cudaMemcpyHostToDevice, e->st));
+    CK(cudaEventRecord(e->ev[1], e->st));
+    if (n_new > 1) {
+        if (!e->batch_graph || e->batch_graph_n != n) {
+            if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
+            e->batch_graph = nullptr;
+            cudaGraph_t g;
+            const long long before = e->launches;
+            CK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+            rc = e->dtype == G2_F32 ? record_batch_step<float>(e, n) : record_batch_step<__half>(e, n);
+            cudaError_t r = cudaStreamEndCapture(e->st, &g);
+            if (rc) return rc;
+            if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "batch capture: %s", cudaGetErrorString(r));
+            r = cudaGraphInstantiate(&e->batch_graph, g, 0);
+            cudaGraphDestroy(g);
+            if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "batch graph instantiate: %s", cudaGetErrorString(r));
+            e->batch_graph_kernels = (int)(e->launches - before);
+            e->launches = before;
+            e->batch_graph_n = n;
+        }
+        for (int s = 1; s < n_new; ++s) CK(cudaGraphLaunch(e->batch_graph, e->st));
+        e->launches += (long long)(n_new - 1) * e->batch_graph_kernels;
+    }
+    CK(cudaEventRecord(e->ev[2], e->st));
+    CK(cudaStreamSynchronize(e->st));
+    for (int i = 0; i < n; ++i) {
+        CK(cudaMemcpy(out_tokens + (size_t)i * n_new + 1, e->out_tokens + (size_t)i * c.n_ctx + 1,
+                      sizeof(int) * (n_new - 1), cudaMemcpyDeviceToHost));
+        e->filled[slots[i]] = prompt_lens[i] + n_new - 1;
+    }
+    CK(cudaEventElapsedTime(&e->last_prefill_ms, e->ev[0], e->ev[1]));
+    CK(cudaEventElapsedTime(&e->last_decode_ms, e->ev[1], e->ev[2]));
+    e->last_decode_steps = n_new - 1;
+    e->result_slot = -1;
+    return G2_OK;
+}
+
+// ------------------------------------------------------------------------------
+// single-kernel entry points (device pointers)
+// ------------------------------------------------------------------------------
+static int current_sms() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+extern "C" size_t g2k_matvec_workspace(int N, int K) {
+    if (N <= 0 || K <= 0) return 0;
+    GemvPlan p = gemv_plan<float>(N, K, current_sms());
+    return align_up((size_t)p.tiles * 4, 256) + align_up((size_t)p.ksplit * N * 4, 256);
+}
+
+extern "C" int g2k_matvec(const float *x, const float *W, const float *bias, const float *residual, float *y, int N,
+                          int K, int apply_gelu, const float *ln_gamma, const float *ln_beta, void *workspace,
+                          size_t workspace_bytes, void *stream) {
+    if (!x || !W || !y || !workspace) return set_err(G2_ERR_ARG, "g2k_matvec: null argument");
+    if (N <= 0 || K <= 0 || N % 4 || K % 16) return set_err(G2_ERR_ARG, "g2k_matvec: need N %% 4 == 0, K %% 16 == 0");
+    if ((ln_gamma == nullptr) != (ln_beta == nullptr)) return set_err(G2_ERR_ARG, "g2k_matvec: ln_gamma and ln_beta go together");
+    if (workspace_bytes < g2k_matvec_workspace(N, K)) return set_err(G2_ERR_ARG, "g2k_matvec: workspace too small");
+    if ((uintptr_t)workspace % 256) return set_err(G2_ERR_ARG, "g2k_matvec: workspace not 256-byte aligned");
+    GemvPlan p = gemv_plan<float>(N, K, current_sms());
+    unsigned *ctr = reinterpret_cast<unsigned *>(workspace);
+    float *partial = reinterpret_cast<float *>((char *)workspace + align_up((size_t)p.tiles * 4, 256));
+    const int epi = (bias ? EPI_BIAS : 0) | (apply_gelu ? EPI_GELU : 0) | (residual ? EPI_RESID : 0);
+    launch_gemv<float>(x, W, bias, residual, y, N, K, epi, ln_gamma, ln_beta, partial, ctr, p, nullptr, 0, nullptr,
+                       nullptr, (cudaStream_t)stream);
+    CKL();
+    return G2_OK;
+}
+
+extern "C" int g2k_matmul(const float *A, const float *B, const float *bias, const float *residual, float *C, int M,
+                          int N, int K, int apply_gelu, void *stream) {
+    if (!A || !B || !C) return set_err(G2_ERR_ARG, "g2k_matmul: null argument");
+    if (M <= 0 || N <= 0 || K <= 0 || K % 16) return set_err(G2_ERR_ARG, "g2k_matmul: need K %% 16 == 0");
+    const int epi = (bias ? EPI_BIAS : 0) | (apply_gelu ? EPI_GELU : 0) | (residual ? EPI_RESID : 0);
+    launch_gemm_rows<float>(A, B, bias, residual, C, M, N, K, epi, nullptr, 0, Rows{nullptr, nullptr, nullptr},
+                            (cudaStream_t)stream);
+    CKL();
+    return G2_OK;
+}
+
+extern "C" int g2k_layernorm(const float *x, float *out, const float *gamma, const float *beta, int n_embd, int rows,
+                             void *stream) {
+    if (!x || !out || !gamma || !beta) return set_err(G2_ERR_ARG, "g2k_layernorm: null argument");
+    if (n_embd <= 0 || rows <= 0) return set_err(G2_ERR_ARG, "g2k_layernorm: bad size");
+    launch_layernorm<float>(x, out, gamma, beta, n_embd, rows, (cudaStream_t)stream);
+    CKL();
+    return G2_OK;
+}
+
+extern "C" size_t g2k_attention_workspace(int n_head, int max_seq) {
+    if (n_head <= 0 || max_seq <= 0) return 0;
+    return 256 + align_up(attn_counter_count(1, n_head) * 4, 256) + align_up(attn_partial_floats(1, n_head, max_seq) * 4, 256);
+}
+
+extern "C" int g2k_attention(const float *q, const float *K, const float *V, float *out, int n_head, int max_seq,
+                             int T_kv, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!q || !K || !V || !out || !workspace) return set_err(G2_ERR_ARG, "g2k_attention: null argument");
+    if (n_head <= 0 || max_seq <= 0 || max_seq > kMaxSeq || T_kv < 1 || T_kv > max_seq)
+        return set_err(G2_ERR_RANGE, "g2k_attention: need 1 <= T_kv <= max_seq <= %d", kMaxSeq);
+    if (workspace_bytes < g2k_attention_workspace(n_head, max_seq)) return set_err(G2_ERR_ARG, "g2k_attention: workspace too small");
+    if ((uintptr_t)workspace % 256) return set_err(G2_ERR_ARG, "g2k_attention: workspace not 256-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;
+    int *rowinfo = reinterpret_cast<int *>(workspace);   // [0] = pos, [1] = slot, [2] = token
+    unsigned *ctr = reinterpret_cast<unsigned *>((char *)workspace + 256);
+    float *partial = reinterpret_cast<float *>((char *)workspace + 256 + align_up(attn_counter_count(1, n_head) * 4, 256));
+    const int info[4] = {T_kv - 1, 0, 0, 0};
+    CK(cudaMemcpyAsync(rowinfo, info, sizeof info, cudaMemcpyHostToDevice, st));
+    KVLayout kv;
+    kv.k = const_cast<float *>(K);
+    kv.v = const_cast<float *>(V);
+    kv.slot_stride = 0;
+    kv.layer_stride = 0;
+    kv.max_seq = max_seq;
+    kv.n_head = n_head;
+    launch_attention<float>(q, n_head * kHeadDim, kv, 0, Rows{rowinfo + 2, rowinfo, rowinfo + 1}, 1, out,
+                            n_head * kHeadDim, partial, ctr, T_kv - 1, st);
+    CKL();
+    return G2_OK;
+}

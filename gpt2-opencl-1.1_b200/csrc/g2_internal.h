@@ -1,0 +1,106 @@
+// g2_internal.h -- device-side types and kernel launchers shared by the
+// engine (g2_engine.cu) and the kernels (g2_kernels.cu).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace g2 {
+
+constexpr int kHeadDim = 64;        // GPT-2 head size (all family members)
+constexpr int kAttnChunk = 64;      // keys per attention CTA (flash-decoding split)
+constexpr int kMaxSeq = 1024;       // KV positions per slot (main.c:51)
+constexpr int kEos = 50256;         // main.c:58
+
+// Per-token decode state in device memory.  The B=1 decode graph reads the
+// token and position from here and its last kernel writes the next greedy
+// token back, so one captured graph serves every step.
+struct StepState {
+    int token;       // token to embed this step
+    int pos;         // its position
+    int slot;        // KV slot
+    int step;        // tokens generated so far (index into out_tokens)
+    int min_new;     // EOS is excluded from the argmax while step < min_new
+    int pad[3];
+};
+
+// KV cache addressing: element (slot, layer, head, pos, d) of K (or V) is at
+// base + slot*slot_stride + layer*layer_stride + (head*max_seq + pos)*64 + d.
+struct KVLayout {
+    void *k, *v;                 // cache bases (float or __half)
+    long long slot_stride;       // elements
+    long long layer_stride;      // elements
+    int max_seq;
+    int n_head;
+};
+
+// Row descriptors of a batched pass: row r embeds tok[r] at pos[r] of slot[r].
+struct Rows {
+    const int *tok;
+    const int *pos;
+    const int *slot;
+};
+
+enum Epilogue { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_RESID = 4, EPI_KV = 8 };
+
+// ---- launchers (g2_kernels.cu); all asynchronous on `st` ------------------------
+template <typename WT>
+void launch_embed(const WT *wte, const WT *wpe, Rows rows, float *h, int E, int V, int n_pos, int nrows,
+                  cudaStream_t st);
+
+template <typename WT>
+void launch_layernorm(const float *x, float *out, const WT *g, const WT *b, int E, int nrows, cudaStream_t st);
+
+// B=1 GEMV: y = x' W (+bias)(GELU)(+resid)(KV append), x' = LN(x) if ln_g.
+// partial: [ksplit][N] floats, counters: [N / cols-per-CTA] zeroed uints.
+struct GemvPlan {
+    int ksplit;
+    int tiles;
+};
+template <typename WT>
+GemvPlan gemv_plan(int N, int K, int sms);
+template <typename WT>
+void launch_gemv(const float *x, const WT *W, const WT *bias, const float *resid, float *y, int N, int K,
+                 int epi, const WT *ln_g, const WT *ln_b, float *partial, unsigned *counters, GemvPlan plan,
+                 const KVLayout *kv, int layer, const int *pos_ptr, const int *slot_ptr, cudaStream_t st);
+
+// Rows GEMM: C[M][N] = A[M][K] W[K][N] with the same epilogues (KV append per row).
+template <typename WT>
+void launch_gemm_rows(const float *A, const WT *W, const WT *bias, const float *resid, float *C, int M, int N,
+                      int K, int epi, const KVLayout *kv, int layer, Rows rows, cudaStream_t st);
+
+// Single-query attention for nrows rows: row r attends to positions
+// 0..pos[r] of its slot. partial/counters: scratch (see attn_workspace_*).
+size_t attn_partial_floats(int nrows, int n_head, int max_seq);
+size_t attn_counter_count(int nrows, int n_head);
+template <typename KT>
+void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
+                      float *out, int out_stride, float *partial, unsigned *counters, int max_pos_hint,
+                      cudaStream_t st);
+
+// LM head on one row x (fp32 [E]) with the final LayerNorm fused:
+// logits[v] = LN_f(x) . wte[v]; argmax over v < V (first index on ties,
+// EOS excluded while state->step < state->min_new when state != NULL, or
+// when forbid_eos).  Writes logits[0..Vp), best (token, value) to result[0..1]
+// and, if state, appends the token to out_tokens and advances state.
+template <typename WT>
+void launch_lm_head(const float *x, const WT *wte, const WT *lnf_g, const WT *lnf_b, float *logits, int E,
+                    int V, int Vp, int forbid_eos, float *partial, unsigned *counter, int *result,
+                    StepState *state, int *out_tokens, cudaStream_t st);
+int lm_head_blocks();
+
+// Batched LM head: logits[r][v] = x_r . wte[v] for rows of x (already
+// normalised), then argmax per row into tokens[r] (and optional state update).
+template <typename WT>
+void launch_lm_head_rows(const float *x, const WT *wte, float *logits, int E, int V, int Vp, int nrows,
+                         cudaStream_t st);
+void launch_argmax_rows(const float *logits, int V, int Vp, int nrows, int forbid_eos, int *tokens, float *values,
+                        int *tok_next, int *pos_next, int *out_tokens, int out_stride, const int *step_ptr,
+                        cudaStream_t st);
+
+void launch_copy_row(const float *src, float *dst, int n, cudaStream_t st);
+void launch_step_advance(int *step_ptr, cudaStream_t st);
+
+}  // namespace g2

@@ -1,0 +1,809 @@
+// g2_kernels.cu -- sm_100a kernels of the GPT-2 decode/prefill path.
+//
+// Each kernel replaces one or more of the reference's OpenCL kernels
+// (math.cl) with the neighbouring element-wise work fused in:
+//
+//   gemv_kernel       matvec4 / matvec4_sk + reduce_partial (math.cl:185-280)
+//                     with layernorm (math.cl:283) fused as a prologue and
+//                     bias / GELU / residual / split_kv (math.cl:367) as the
+//                     epilogue.  B = 1 decode.
+//   gemm_kernel       the prefill matmul (main.c:593-684) + gelu / add_inplace /
+//                     split_kv epilogues, for any number of rows (prefill and
+//                     batched decode).
+//   attn_kernel       attn_scores_1q + attn_softmax_1q + attn_out_1q
+//                     (math.cl:388-476): one query per row, keys split over
+//                     CTAs (flash-decoding), online softmax, deterministic
+//                     in-order combine by the last CTA of each head.
+//   lm_head_kernel    final layernorm + lm_head matvec (main.c:1828-1832) +
+//                     the greedy argmax of sample_next_token (main.c:1898-1904).
+//   embed_kernel      embed (math.cl:333).
+//
+// Arithmetic is fp32 with fp32 accumulation (fp16 weights are widened on
+// load).  Summation orders differ from the reference (parallel reductions);
+// parity is checked against the oracle within the stated tolerances.
+#include <cfloat>
+#include <climits>
+
+#include "g2_internal.h"
+
+namespace g2 {
+
+// ------------------------------------------------------------------------------
+// helpers
+// ------------------------------------------------------------------------------
+__device__ __forceinline__ float tof(float v) { return v; }
+__device__ __forceinline__ float tof(__half v) { return __half2float(v); }
+template <typename T>
+__device__ __forceinline__ T fromf(float v);
+template <>
+__device__ __forceinline__ float fromf<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half fromf<__half>(float v) { return __float2half_rn(v); }
+
+// tanh-form GELU (math.cl:21-23, HF "gelu_new").
+__device__ __forceinline__ float gelu_f(float v) {
+    return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// Block-wide sum; `sh` holds >= 32 floats.  All threads get the result.
+__device__ __forceinline__ float block_sum(float v, float *sh) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (l == 0) sh[w] = v;
+    __syncthreads();
+    float t = (l < nw) ? sh[l] : 0.0f;
+    t = warp_sum(t);
+    return t;
+}
+__device__ __forceinline__ float block_max(float v, float *sh) {
+    v = warp_max(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (l == 0) sh[w] = v;
+    __syncthreads();
+    float t = (l < nw) ? sh[l] : -FLT_MAX;
+    return warp_max(t);
+}
+
+// Two-pass LayerNorm statistics of x[0..n) (math.cl:297-308), block-wide.
+__device__ __forceinline__ void ln_stats(const float *x, int n, float *sh, float &mean, float &rstd) {
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+    mean = block_sum(s, sh) / (float)n;
+    float v = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float d = x[i] - mean;
+        v += d * d;
+    }
+    const float var = block_sum(v, sh) / (float)n;
+    rstd = 1.0f / sqrtf(var + 1e-5f);
+}
+
+// 16-byte streaming load of weights (read once per step: no L1 allocation).
+__device__ __forceinline__ uint4 ld_stream(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+template <typename WT>
+struct Vec;
+template <>
+struct Vec<float> {
+    static constexpr int n = 4;
+};
+template <>
+struct Vec<__half> {
+    static constexpr int n = 8;
+};
+
+// acc[0..n) += x * w[0..n), w packed in 16 bytes.
+__device__ __forceinline__ void fma_vec(float *acc, uint4 w, float x, float) {
+    acc[0] = fmaf(x, __uint_as_float(w.x), acc[0]);
+    acc[1] = fmaf(x, __uint_as_float(w.y), acc[1]);
+    acc[2] = fmaf(x, __uint_as_float(w.z), acc[2]);
+    acc[3] = fmaf(x, __uint_as_float(w.w), acc[3]);
+}
+__device__ __forceinline__ void fma_vec(float *acc, uint4 w, float x, __half) {
+    const __half2 *h = reinterpret_cast<const __half2 *>(&w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 f = __half22float2(h[i]);
+        acc[2 * i] = fmaf(x, f.x, acc[2 * i]);
+        acc[2 * i + 1] = fmaf(x, f.y, acc[2 * i + 1]);
+    }
+}
+// dot of 16 bytes of weights with xs[0..n)
+__device__ __forceinline__ float dot_vec(uint4 w, const float *xs, float) {
+    return __uint_as_float(w.x) * xs[0] + __uint_as_float(w.y) * xs[1] + __uint_as_float(w.z) * xs[2] +
+           __uint_as_float(w.w) * xs[3];
+}
+__device__ __forceinline__ float dot_vec(uint4 w, const float *xs, __half) {
+    const __half2 *h = reinterpret_cast<const __half2 *>(&w);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 f = __half22float2(h[i]);
+        s = fmaf(f.x, xs[2 * i], s);
+        s = fmaf(f.y, xs[2 * i + 1], s);
+    }
+    return s;
+}
+
+// Epilogue shared by gemv and gemm: v = acc (+bias) (GELU) (+resid), stored to
+// out[r][n]; with EPI_KV the K and V thirds of a qkv row are also appended to
+// the cache at (slot[r], layer, head, pos[r]) -- split_kv (math.cl:367-383).
+template <typename WT>
+struct Epi {
+    const WT *bias;
+    const float *resid;
+    float *out;
+    int N, epi;
+    KVLayout kv;
+    int layer;
+    const int *pos;
+    const int *slot;
+    int E;
+
+    __device__ __forceinline__ void apply(int r, int n, float v) const {
+        if (epi & EPI_BIAS) v += tof(bias[n]);
+        if (epi & EPI_GELU) v = gelu_f(v);
+        if (epi & EPI_RESID) v = resid[(size_t)r * N + n] + v;
+        out[(size_t)r * N + n] = v;
+        if ((epi & EPI_KV) && n >= E) {
+            int m = n - E;
+            const bool isv = m >= E;
+            if (isv) m -= E;
+            const int h = m >> 6, d = m & 63;
+            const int p = pos[r];
+            if (p < 0 || p >= kv.max_seq) return;   // positions are validated on the host; never write outside
+            const long long off = (long long)slot[r] * kv.slot_stride + (long long)layer * kv.layer_stride +
+                                  ((long long)h * kv.max_seq + p) * kHeadDim + d;
+            WT *base = reinterpret_cast<WT *>(isv ? kv.v : kv.k);
+            base[off] = fromf<WT>(v);
+        }
+    }
+};
+
+// ------------------------------------------------------------------------------
+// embed (math.cl:333-350)
+// ------------------------------------------------------------------------------
+template <typename WT>
+__global__ void embed_kernel(const WT *wte, const WT *wpe, Rows rows, float *h, int E, int V, int n_pos) {
+    const int r = blockIdx.x;
+    // ids and positions are validated on the host; clamp so that a bad value
+    // can never address outside the tables
+    const int tok = min(max(rows.tok[r], 0), V - 1), pos = min(max(rows.pos[r], 0), n_pos - 1);
+    for (int i = threadIdx.x; i < E; i += blockDim.x)
+        h[(size_t)r * E + i] = tof(wte[(size_t)tok * E + i]) + tof(wpe[(size_t)pos * E + i]);
+}
+
+// layernorm (math.cl:283-311), one CTA per row.
+template <typename WT>
+__global__ void __launch_bounds__(256) layernorm_kernel(const float *x, float *out, const WT *g, const WT *b, int E) {
+    __shared__ float sh[32];
+    const float *xr = x + (size_t)blockIdx.x * E;
+    float mean, rstd;
+    ln_stats(xr, E, sh, mean, rstd);
+    for (int i = threadIdx.x; i < E; i += blockDim.x)
+        out[(size_t)blockIdx.x * E + i] = (xr[i] - mean) * rstd * tof(g[i]) + tof(b[i]);
+}
+
+// ------------------------------------------------------------------------------
+// B = 1 GEMV with split-K across CTAs and an in-order last-CTA reduction
+// ------------------------------------------------------------------------------
+template <typename WT>
+struct GemvArgs {
+    const float *x;
+    const WT *W;
+    const WT *ln_g, *ln_b;
+    float *partial;
+    unsigned *counters;
+    int N, K;
+    Epi<WT> e;
+};
+
+template <typename WT>
+__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs<WT> a) {
+    constexpr int VN = Vec<WT>::n, BN = 16 * VN;
+    extern __shared__ float smem[];
+    __shared__ float sh[32];
+    __shared__ int s_last;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int tile = blockIdx.x, ks = blockIdx.y, ksplit = gridDim.y;
+    const int kchunk = a.K / ksplit, k0 = ks * kchunk;
+    float *xs = smem;
+    float *red = smem + kchunk;
+
+    float mean = 0.0f, rstd = 1.0f;
+    if (a.ln_g) ln_stats(a.x, a.K, sh, mean, rstd);
+    for (int i = tid; i < kchunk; i += 256) {
+        float v = a.x[k0 + i];
+        if (a.ln_g) v = (v - mean) * rstd * tof(a.ln_g[k0 + i]) + tof(a.ln_b[k0 + i]);
+        xs[i] = v;
+    }
+    __syncthreads();
+
+    const int n0 = tile * BN + tx * VN;
+    float acc[VN];
+#pragma unroll
+    for (int c = 0; c < VN; ++c) acc[c] = 0.0f;
+    if (n0 < a.N) {
+        const WT *wp = a.W + (size_t)(k0 + ty) * a.N + n0;
+        const size_t step = (size_t)16 * a.N;
+        const int iters = kchunk >> 4;
+        int it = 0;
+        for (; it + 4 <= iters; it += 4) {
+            uint4 w0 = ld_stream(wp), w1 = ld_stream(wp + step), w2 = ld_stream(wp + 2 * step),
+                  w3 = ld_stream(wp + 3 * step);
+            wp += 4 * step;
+            fma_vec(acc, w0, xs[ty + (it + 0) * 16], WT());
+            fma_vec(acc, w1, xs[ty + (it + 1) * 16], WT());
+            fma_vec(acc, w2, xs[ty + (it + 2) * 16], WT());
+            fma_vec(acc, w3, xs[ty + (it + 3) * 16], WT());
+        }
+        for (; it < iters; ++it) {
+            uint4 w0 = ld_stream(wp);
+            wp += step;
+            fma_vec(acc, w0, xs[ty + it * 16], WT());
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < VN; ++c) red[ty * BN + tx * VN + c] = acc[c];
+    __syncthreads();
+    float colsum = 0.0f;
+    const int n = tile * BN + tid;
+    if (tid < BN) {
+        for (int t = 0; t < 16; ++t) colsum += red[t * BN + tid];
+    }
+    if (ksplit == 1) {
+        if (tid < BN && n < a.N) a.e.apply(0, n, colsum);
+        return;
+    }
+    if (tid < BN && n < a.N) a.partial[(size_t)ks * a.N + n] = colsum;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(&a.counters[tile], 1u) == (unsigned)(ksplit - 1));
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid < BN && n < a.N) {
+        float s = 0.0f;
+        for (int k = 0; k < ksplit; ++k) s += __ldcg(&a.partial[(size_t)k * a.N + n]);
+        a.e.apply(0, n, s);
+    }
+    if (tid == 0) a.counters[tile] = 0u;
+}
+
+// ------------------------------------------------------------------------------
+// Rows GEMM (SIMT fp32): C[M][N] = A[M][K] * W, W either [K][N] or (BT) [N][K]
+// ------------------------------------------------------------------------------
+template <typename WT>
+struct GemmArgs {
+    const float *A;
+    const WT *W;
+    int M, N, K;
+    Epi<WT> e;
+};
+
+template <typename WT, int BM, bool BT>
+__global__ void __launch_bounds__(256) gemm_kernel(GemmArgs<WT> a) {
+    constexpr int BN = 64, BK = 16, TM = BM / 16;
+    __shared__ __align__(16) float As[BK][BM + 4];
+    __shared__ __align__(16) float Bs[BK][BN + 4];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    float acc[TM][4];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+
+    for (int k0 = 0; k0 < a.K; k0 += BK) {
+        // A tile: BM rows x 16 k as float4 (BM*4 vectors)
+        for (int idx = tid; idx < BM * 4; idx += 256) {
+            const int row = idx >> 2, c4 = idx & 3;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (m0 + row < a.M) v = *reinterpret_cast<const float4 *>(a.A + (size_t)(m0 + row) * a.K + k0 + c4 * 4);
+            As[c4 * 4 + 0][row] = v.x;
+            As[c4 * 4 + 1][row] = v.y;
+            As[c4 * 4 + 2][row] = v.z;
+            As[c4 * 4 + 3][row] = v.w;
+        }
+        if (!BT) {
+            // W [K][N]: 16 rows x 64 columns
+            for (int idx = tid; idx < BK * BN; idx += 256) {
+                const int row = idx >> 6, col = idx & 63;
+                const int n = n0 + col;
+                Bs[row][col] = n < a.N ? tof(a.W[(size_t)(k0 + row) * a.N + n]) : 0.0f;
+            }
+        } else {
+            // W [N][K]: 64 rows (outputs) x 16 k
+            for (int idx = tid; idx < BK * BN; idx += 256) {
+                const int col = idx >> 4, kk = idx & 15;
+                const int n = n0 + col;
+                Bs[kk][col] = n < a.N ? tof(a.W[(size_t)n * a.K + k0 + kk]) : 0.0f;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            float av[TM];
+#pragma unroll
+            for (int i = 0; i < TM; ++i) av[i] = As[kk][ty * TM + i];
+            const float4 bv = *reinterpret_cast<const float4 *>(&Bs[kk][tx * 4]);
+#pragma unroll
+            for (int i = 0; i < TM; ++i) {
+                acc[i][0] = fmaf(av[i], bv.x, acc[i][0]);
+                acc[i][1] = fmaf(av[i], bv.y, acc[i][1]);
+                acc[i][2] = fmaf(av[i], bv.z, acc[i][2]);
+                acc[i][3] = fmaf(av[i], bv.w, acc[i][3]);
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const int r = m0 + ty * TM + i;
+        if (r >= a.M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = n0 + tx * 4 + j;
+            if (n < a.N) a.e.apply(r, n, acc[i][j]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------
+// Single-query attention, flash-decoding split over keys
+// ------------------------------------------------------------------------------
+template <typename KT>
+struct AttnArgs {
+    const float *qkv;
+    int qkv_stride;
+    KVLayout kv;
+    int layer;
+    Rows rows;
+    float *out;
+    int out_stride;
+    float *partial;      // [rows][heads][max_splits][66]
+    unsigned *counters;  // [rows][heads]
+    int max_splits;
+};
+
+template <typename KT>
+__global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
+    constexpr int CH = kAttnChunk;
+    __shared__ float q[kHeadDim];
+    __shared__ float p[CH];
+    __shared__ float accs[2][kHeadDim];
+    __shared__ float sh[32];
+    __shared__ int s_last;
+    const int h = blockIdx.x, sp = blockIdx.y, r = blockIdx.z, tid = threadIdx.x;
+    const int NH = a.kv.n_head;
+    const int T = a.rows.pos[r] + 1;
+    const int nsplit = (T + CH - 1) / CH;
+    if (sp >= nsplit) return;
+    const int slot = a.rows.slot[r];
+    if (tid < kHeadDim) q[tid] = a.qkv[(size_t)r * a.qkv_stride + h * kHeadDim + tid] * 0.125f;  // 1/sqrt(64)
+    __syncthreads();
+    const long long base = (long long)slot * a.kv.slot_stride + (long long)a.layer * a.kv.layer_stride +
+                           (long long)h * a.kv.max_seq * kHeadDim;
+    const KT *K = reinterpret_cast<const KT *>(a.kv.k) + base;
+    const KT *V = reinterpret_cast<const KT *>(a.kv.v) + base;
+    const int j0 = sp * CH;
+    const int nj = min(CH, T - j0);
+
+    // scores: two threads per key, 32 dims each
+    const int key = tid >> 1, half = tid & 1;
+    float s = -FLT_MAX;
+    if (key < nj) {
+        const KT *kr = K + (size_t)(j0 + key) * kHeadDim + half * 32;
+        const float *qh = q + half * 32;
+        float d = 0.0f;
+        constexpr int VN = 16 / sizeof(KT);
+#pragma unroll
+        for (int i = 0; i < 32; i += VN) d += dot_vec(*reinterpret_cast<const uint4 *>(kr + i), qh + i, KT());
+        s = d;
+    }
+    s += __shfl_xor_sync(0xffffffffu, key < nj ? s : 0.0f, 1) * (key < nj ? 1.0f : 0.0f);
+    const float m = block_max(s, sh);
+    const float e = key < nj ? expf(s - m) : 0.0f;
+    if (half == 0 && key < CH) p[key] = e;
+    const float l = block_sum(half == 0 ? e : 0.0f, sh);
+    __syncthreads();
+    // P.V: thread (d, part) sums keys part*32 .. part*32+31
+    const int d = tid & 63, part = tid >> 6;
+    float o = 0.0f;
+    const int jend = min(nj, part * 32 + 32);
+    for (int jj = part * 32; jj < jend; ++jj) o = fmaf(p[jj], tof(V[(size_t)(j0 + jj) * kHeadDim + d]), o);
+    accs[part][d] = o;
+    __syncthreads();
+    const float* none = nullptr;
+    (void)none;
+    if (nsplit == 1) {
+        if (tid < kHeadDim) a.out[(size_t)r * a.out_stride + h * kHeadDim + tid] = (accs[0][tid] + accs[1][tid]) / l;
+        return;
+    }
+    float *P = a.partial + (((size_t)r * NH + h) * a.max_splits + sp) * (kHeadDim + 2);
+    if (tid < kHeadDim) P[2 + tid] = accs[0][tid] + accs[1][tid];
+    if (tid == 0) {
+        P[0] = m;
+        P[1] = l;
+    }
+    __threadfence();
+    __syncthreads();
+    unsigned *ctr = a.counters + (size_t)r * NH + h;
+    if (tid == 0) s_last = (atomicAdd(ctr, 1u) == (unsigned)(nsplit - 1));
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid < kHeadDim) {
+        const float *P0 = a.partial + ((size_t)r * NH + h) * a.max_splits * (kHeadDim + 2);
+        float M = -FLT_MAX;
+        for (int i = 0; i < nsplit; ++i) M = fmaxf(M, __ldcg(P0 + (size_t)i * (kHeadDim + 2)));
+        float L = 0.0f, O = 0.0f;
+        for (int i = 0; i < nsplit; ++i) {
+            const float *Pi = P0 + (size_t)i * (kHeadDim + 2);
+            const float w = expf(__ldcg(Pi) - M);
+            L = fmaf(__ldcg(Pi + 1), w, L);
+            O = fmaf(__ldcg(Pi + 2 + tid), w, O);
+        }
+        a.out[(size_t)r * a.out_stride + h * kHeadDim + tid] = O / L;
+    }
+    if (tid == 0) *ctr = 0u;
+}
+
+// ------------------------------------------------------------------------------
+// LM head (one row) with the final LayerNorm and greedy argmax fused
+// ------------------------------------------------------------------------------
+template <typename WT>
+struct LmArgs {
+    const float *x;
+    const WT *wte, *g, *b;
+    float *logits;
+    int E, V, Vp, forbid_eos;
+    float *pval;
+    int *pidx;
+    unsigned *counter;
+    int *result;
+    StepState *state;
+    int *out_tokens;
+};
+
+// (v1, i1) beats (v2, i2): larger value, or equal value and smaller index.
+__device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
+    return v1 > v2 || (v1 == v2 && i1 < i2);
+}
+
+constexpr int kLmBlocks = 148 * 4;
+
+template <typename WT>
+__global__ void __launch_bounds__(256) lm_head_kernel(LmArgs<WT> a) {
+    constexpr int VN = Vec<WT>::n;
+    extern __shared__ float xs[];
+    __shared__ float sh[32];
+    __shared__ float wv[8];
+    __shared__ int wi[8];
+    __shared__ int s_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int forbid = a.forbid_eos || (a.state && a.state->step < a.state->min_new);
+    float mean, rstd;
+    ln_stats(a.x, a.E, sh, mean, rstd);
+    for (int i = tid; i < a.E; i += 256) xs[i] = (a.x[i] - mean) * rstd * tof(a.g[i]) + tof(a.b[i]);
+    __syncthreads();
+    float best = -FLT_MAX;
+    int besti = INT_MAX;
+    const int nw = gridDim.x * 8;
+    for (int v = blockIdx.x * 8 + warp; v < a.V; v += nw) {
+        const WT *row = a.wte + (size_t)v * a.E;
+        float s = 0.0f;
+        for (int i = lane * VN; i < a.E; i += 32 * VN) s += dot_vec(ld_stream(row + i), xs + i, WT());
+        s = warp_sum(s);
+        if (lane == 0) a.logits[v] = s;
+        if (!(forbid && v == kEos) && better(s, v, best, besti)) {
+            best = s;
+            besti = v;
+        }
+    }
+    if (blockIdx.x == 0)
+        for (int v = a.V + tid; v < a.Vp; v += 256) a.logits[v] = 0.0f;
+    if (lane == 0) {
+        wv[warp] = best;
+        wi[warp] = besti;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < 8; ++w)
+            if (better(wv[w], wi[w], best, besti)) {
+                best = wv[w];
+                besti = wi[w];
+            }
+        a.pval[blockIdx.x] = best;
+        a.pidx[blockIdx.x] = besti;
+        __threadfence();
+        s_last = (atomicAdd(a.counter, 1u) == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!s_last || tid != 0) return;
+    __threadfence();
+    float bv = -FLT_MAX;
+    int bi = INT_MAX;
+    for (int c = 0; c < (int)gridDim.x; ++c) {
+        const float v = __ldcg(a.pval + c);
+        const int i = __ldcg(a.pidx + c);
+        if (better(v, i, bv, bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+    if (bi == INT_MAX) bi = 0;   // every logit NaN: never hand an invalid id to the next step
+    a.result[0] = bi;
+    a.result[1] = __float_as_int(bv);
+    if (a.state) {
+        a.out_tokens[a.state->step] = bi;
+        a.state->token = bi;
+        a.state->pos += 1;
+        a.state->step += 1;
+    }
+    *a.counter = 0u;
+}
+
+// Argmax per row of logits [rows][Vp] (one CTA per row).
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const float *logits, int V, int Vp, int forbid_eos,
+                                                          int *tokens, float *values, int *tok_next, int *pos_next,
+                                                          int *out_tokens, int out_stride, const int *step_ptr) {
+    __shared__ float wv[8];
+    __shared__ int wi[8];
+    const int r = blockIdx.x, tid = threadIdx.x;
+    const float *L = logits + (size_t)r * Vp;
+    float best = -FLT_MAX;
+    int besti = INT_MAX;
+    for (int v = tid; v < V; v += 256) {
+        if (forbid_eos && v == kEos) continue;
+        const float s = L[v];
+        if (better(s, v, best, besti)) {
+            best = s;
+            besti = v;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+        if (better(ov, oi, best, besti)) {
+            best = ov;
+            besti = oi;
+        }
+    }
+    if ((tid & 31) == 0) {
+        wv[tid >> 5] = best;
+        wi[tid >> 5] = besti;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < 8; ++w)
+            if (better(wv[w], wi[w], best, besti)) {
+                best = wv[w];
+                besti = wi[w];
+            }
+        if (besti == INT_MAX) besti = 0;   // every logit NaN
+        if (tokens) tokens[r] = besti;
+        if (values) values[r] = best;
+        if (tok_next) tok_next[r] = besti;
+        if (pos_next) pos_next[r] += 1;
+        if (out_tokens) out_tokens[(size_t)r * out_stride + *step_ptr] = besti;
+    }
+}
+
+__global__ void copy_kernel(const float *src, float *dst, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) dst[i] = src[i];
+}
+__global__ void step_advance_kernel(int *step) { *step += 1; }
+
+// ------------------------------------------------------------------------------
+// launchers
+// ------------------------------------------------------------------------------
+template <typename WT>
+void launch_embed(const WT *wte, const WT *wpe, Rows rows, float *h, int E, int V, int n_pos, int nrows,
+                  cudaStream_t st) {
+    embed_kernel<WT><<<nrows, 256, 0, st>>>(wte, wpe, rows, h, E, V, n_pos);
+}
+
+template <typename WT>
+void launch_layernorm(const float *x, float *out, const WT *g, const WT *b, int E, int nrows, cudaStream_t st) {
+    layernorm_kernel<WT><<<nrows, 256, 0, st>>>(x, out, g, b, E);
+}
+
+template <typename WT>
+GemvPlan gemv_plan(int N, int K, int sms) {
+    constexpr int BN = 16 * Vec<WT>::n;
+    GemvPlan p;
+    p.tiles = (N + BN - 1) / BN;
+    const int target = sms * 4;
+    const int units = K / 16;  // ksplit must divide K/16
+    int best = 1;
+    for (int d = 1; d <= units; ++d) {
+        if (units % d) continue;
+        if (p.tiles * d <= target) best = d;
+    }
+    p.ksplit = best;
+    return p;
+}
+
+template <typename WT>
+void launch_gemv(const float *x, const WT *W, const WT *bias, const float *resid, float *y, int N, int K, int epi,
+                 const WT *ln_g, const WT *ln_b, float *partial, unsigned *counters, GemvPlan plan,
+                 const KVLayout *kv, int layer, const int *pos_ptr, const int *slot_ptr, cudaStream_t st) {
+    constexpr int BN = 16 * Vec<WT>::n;
+    GemvArgs<WT> a;
+    a.x = x;
+    a.W = W;
+    a.ln_g = ln_g;
+    a.ln_b = ln_b;
+    a.partial = partial;
+    a.counters = counters;
+    a.N = N;
+    a.K = K;
+    a.e.bias = bias;
+    a.e.resid = resid;
+    a.e.out = y;
+    a.e.N = N;
+    a.e.epi = epi;
+    if (kv) a.e.kv = *kv;
+    a.e.layer = layer;
+    a.e.pos = pos_ptr;
+    a.e.slot = slot_ptr;
+    a.e.E = N / 3;
+    const size_t smem = (size_t)(K / plan.ksplit + 16 * BN) * sizeof(float);
+    dim3 grid(plan.tiles, plan.ksplit);
+    gemv_kernel<WT><<<grid, 256, smem, st>>>(a);
+}
+
+template <typename WT>
+void launch_gemm_rows(const float *A, const WT *W, const WT *bias, const float *resid, float *C, int M, int N, int K,
+                      int epi, const KVLayout *kv, int layer, Rows rows, cudaStream_t st) {
+    GemmArgs<WT> a;
+    a.A = A;
+    a.W = W;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.e.bias = bias;
+    a.e.resid = resid;
+    a.e.out = C;
+    a.e.N = N;
+    a.e.epi = epi;
+    if (kv) a.e.kv = *kv;
+    a.e.layer = layer;
+    a.e.pos = rows.pos;
+    a.e.slot = rows.slot;
+    a.e.E = N / 3;
+    if (M <= 32) {
+        dim3 grid((N + 63) / 64, (M + 31) / 32);
+        gemm_kernel<WT, 32, false><<<grid, 256, 0, st>>>(a);
+    } else {
+        dim3 grid((N + 63) / 64, (M + 63) / 64);
+        gemm_kernel<WT, 64, false><<<grid, 256, 0, st>>>(a);
+    }
+}
+
+size_t attn_partial_floats(int nrows, int n_head, int max_seq) {
+    const int ms = (max_seq + kAttnChunk - 1) / kAttnChunk;
+    return (size_t)nrows * n_head * ms * (kHeadDim + 2);
+}
+size_t attn_counter_count(int nrows, int n_head) { return (size_t)nrows * n_head; }
+
+template <typename KT>
+void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
+                      float *out, int out_stride, float *partial, unsigned *counters, int max_pos_hint,
+                      cudaStream_t st) {
+    AttnArgs<KT> a;
+    a.qkv = qkv;
+    a.qkv_stride = qkv_stride;
+    a.kv = kv;
+    a.layer = layer;
+    a.rows = rows;
+    a.out = out;
+    a.out_stride = out_stride;
+    a.partial = partial;
+    a.counters = counters;
+    a.max_splits = (kv.max_seq + kAttnChunk - 1) / kAttnChunk;
+    const int splits = max_pos_hint < 0 ? a.max_splits : (max_pos_hint + kAttnChunk) / kAttnChunk;
+    dim3 grid(kv.n_head, splits, nrows);
+    attn_kernel<KT><<<grid, 128, 0, st>>>(a);
+}
+
+int lm_head_blocks() { return kLmBlocks; }
+
+template <typename WT>
+void launch_lm_head(const float *x, const WT *wte, const WT *lnf_g, const WT *lnf_b, float *logits, int E, int V,
+                    int Vp, int forbid_eos, float *partial, unsigned *counter, int *result, StepState *state,
+                    int *out_tokens, cudaStream_t st) {
+    LmArgs<WT> a;
+    a.x = x;
+    a.wte = wte;
+    a.g = lnf_g;
+    a.b = lnf_b;
+    a.logits = logits;
+    a.E = E;
+    a.V = V;
+    a.Vp = Vp;
+    a.forbid_eos = forbid_eos;
+    a.pval = partial;
+    a.pidx = reinterpret_cast<int *>(partial + kLmBlocks);
+    a.counter = counter;
+    a.result = result;
+    a.state = state;
+    a.out_tokens = out_tokens;
+    lm_head_kernel<WT><<<kLmBlocks, 256, (size_t)E * sizeof(float), st>>>(a);
+}
+
+template <typename WT>
+void launch_lm_head_rows(const float *x, const WT *wte, float *logits, int E, int V, int Vp, int nrows,
+                         cudaStream_t st) {
+    GemmArgs<WT> a;
+    a.A = x;
+    a.W = wte;
+    a.M = nrows;
+    a.N = V;
+    a.K = E;
+    a.e.bias = nullptr;
+    a.e.resid = nullptr;
+    a.e.out = logits;
+    a.e.N = Vp;
+    a.e.epi = EPI_NONE;
+    a.e.E = 0;
+    if (nrows <= 32) {
+        dim3 grid((V + 63) / 64, (nrows + 31) / 32);
+        gemm_kernel<WT, 32, true><<<grid, 256, 0, st>>>(a);
+    } else {
+        dim3 grid((V + 63) / 64, (nrows + 63) / 64);
+        gemm_kernel<WT, 64, true><<<grid, 256, 0, st>>>(a);
+    }
+}
+
+void launch_argmax_rows(const float *logits, int V, int Vp, int nrows, int forbid_eos, int *tokens, float *values,
+                        int *tok_next, int *pos_next, int *out_tokens, int out_stride, const int *step_ptr,
+                        cudaStream_t st) {
+    argmax_rows_kernel<<<nrows, 256, 0, st>>>(logits, V, Vp, forbid_eos, tokens, values, tok_next, pos_next,
+                                              out_tokens, out_stride, step_ptr);
+}
+
+void launch_copy_row(const float *src, float *dst, int n, cudaStream_t st) {
+    copy_kernel<<<(n + 255) / 256, 256, 0, st>>>(src, dst, n);
+}
+void launch_step_advance(int *step_ptr, cudaStream_t st) { step_advance_kernel<<<1, 1, 0, st>>>(step_ptr); }
+
+// explicit instantiations
+#define G2_INST(WT)                                                                                                   \
+    template void launch_embed<WT>(const WT *, const WT *, Rows, float *, int, int, int, int, cudaStream_t);         \
+    template void launch_layernorm<WT>(const float *, float *, const WT *, const WT *, int, int, cudaStream_t);      \
+    template GemvPlan gemv_plan<WT>(int, int, int);                                                                    \
+    template void launch_gemv<WT>(const float *, const WT *, const WT *, const float *, float *, int, int, int,      \
+                                  const WT *, const WT *, float *, unsigned *, GemvPlan, const KVLayout *, int,     \
+                                  const int *, const int *, cudaStream_t);                                           \
+    template void launch_gemm_rows<WT>(const float *, const WT *, const WT *, const float *, float *, int, int, int, \
+                                       int, const KVLayout *, int, Rows, cudaStream_t);                              \
+    template void launch_attention<WT>(const float *, int, const KVLayout &, int, Rows, int, float *, int, float *,  \
+                                       unsigned *, int, cudaStream_t);                                                \
+    template void launch_lm_head<WT>(const float *, const WT *, const WT *, const WT *, float *, int, int, int, int, \
+                                     float *, unsigned *, int *, StepState *, int *, cudaStream_t);                  \
+    template void launch_lm_head_rows<WT>(const float *, const WT *, float *, int, int, int, int, cudaStream_t);
+G2_INST(float)
+G2_INST(__half)
+
+}  // namespace g2

@@ -168,6 +168,14 @@ def ref_available() -> bool:
     return os.path.exists(LIB_REF)
 
 
+def ref_fast() -> bool:
+    """Whether the reference build runs barrier kernels on fibers (fast enough
+    for GPT-2-small prefill); the thread-per-work-item executor is not."""
+    if not ref_available():
+        return False
+    return hasattr(ref_lib(), "refcl_fiber_executor")
+
+
 def ref_lib():
     """The reference's own code (libref_main.so)."""
     global _refmain
