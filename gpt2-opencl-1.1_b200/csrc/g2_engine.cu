@@ -35,6 +35,10 @@ static int set_err(int code, const char *fmt, ...) {
 
 extern "C" const char *g2_last_error(void) { return t_err.c_str(); }
 
+namespace g2 {
+int set_error(int code, const char *msg) { return set_err(code, "%s", msg); }
+}  // namespace g2
+
 #define CK(call)                                                                                              \
     do {                                                                                                      \
         cudaError_t e_ = (call);                                                                              \

@@ -101,6 +101,9 @@ void launch_argmax_rows(const float *logits, int V, int Vp, int nrows, int forbi
                         cudaStream_t st);
 
 void launch_copy_row(const float *src, float *dst, int n, cudaStream_t st);
+
+// Record `msg` as the calling thread's g2_last_error(); returns `code`.
+int set_error(int code, const char *msg);
 void launch_step_advance(int *step_ptr, cudaStream_t st);
 
 }  // namespace g2

@@ -58,6 +58,7 @@ def _load():
     L.g2k_matvec_workspace.argtypes = [C.c_int, C.c_int]
     L.g2k_matvec_workspace.restype = C.c_size_t
     L.g2k_matvec.argtypes = [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp, C.c_size_t, vp]
+    L.g2k_matvec_noalloc.argtypes = [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]
     L.g2k_matmul.argtypes = [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp]
     L.g2k_layernorm.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, vp]
     L.g2k_attention_workspace.argtypes = [C.c_int, C.c_int]
@@ -183,6 +184,12 @@ def matvec(x, W, y, N, K, bias=None, residual=None, gelu=False, ln_gamma=None, l
            workspace_bytes=0, stream=0):
     check(lib.g2k_matvec(_ptr(x), _ptr(W), _ptr(bias), _ptr(residual), _ptr(y), N, K, int(gelu), _ptr(ln_gamma),
                          _ptr(ln_beta), _ptr(workspace), workspace_bytes, C.c_void_p(stream)))
+
+
+def matvec_noalloc(x, W, y, N, K, bias=None, residual=None, gelu=False, ln_gamma=None, ln_beta=None, stream=0):
+    """g2k_matvec with the library's fixed scratch instead of a caller workspace."""
+    check(lib.g2k_matvec_noalloc(_ptr(x), _ptr(W), _ptr(bias), _ptr(residual), _ptr(y), N, K, int(gelu),
+                                 _ptr(ln_gamma), _ptr(ln_beta), C.c_void_p(stream)))
 
 
 def matmul(A, B, C_, M, N, K, bias=None, residual=None, gelu=False, stream=0):

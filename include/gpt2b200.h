@@ -130,6 +130,20 @@ int g2k_matvec(const float *x, const float *W, const float *bias, const float *r
                int N, int K, int apply_gelu, const float *ln_gamma, const float *ln_beta,
                void *workspace, size_t workspace_bytes, void *stream);
 
+/* g2k_matvec without a workspace argument, for callers that cannot allocate
+ * device memory (an FFI binding with no device allocator of its own, an
+ * application whose device memory belongs to another allocator, or a path
+ * that must not take cudaMalloc's implicit synchronisation).  This entry has
+ * no counterpart in the reference.  Its scratch is a fixed 256 KiB device
+ * array inside this library (held on every GPU that loads it until exit);
+ * shapes whose split-K scratch would exceed it return G2_ERR_RANGE.  The
+ * first call on a device looks the array up (make it before any stream
+ * capture); every call clears the array's counters before its kernel; calls
+ * that overlap on the GPU share the array and race, so serialise them.
+ * Same arguments and results as g2k_matvec otherwise. */
+int g2k_matvec_noalloc(const float *x, const float *W, const float *bias, const float *residual, float *y,
+                       int N, int K, int apply_gelu, const float *ln_gamma, const float *ln_beta, void *stream);
+
 /* launch_matmul (main.c:1518) + launch_gelu / launch_add (main.c:1635-1654):
  * C[m][n] = sum_k A[m][k] * B[k][n] (+bias[n]) (GELU if apply_gelu) (+residual[m][n]).
  * residual may alias C.  N % 4 == 0, K % 4 == 0. */
