@@ -14,6 +14,7 @@
 
 #include "g2_internal.h"
 #include "g2_loader.h"
+#include "g2_mega.h"
 #include "gpt2b200.h"
 
 using namespace g2;
@@ -101,6 +102,20 @@ struct g2_engine {
     float last_prefill_ms = 0, last_decode_ms = 0;
     int last_decode_steps = 0;
     long long launches = 0;
+    // persistent B = 1 decode kernel (fp32)
+    bool mega = false;
+    float *packed = nullptr;            // strip-packed projection weights
+    std::vector<long long> layer_off;   // [L][4] float offsets into packed
+    long long *d_layer_off = nullptr;
+    LayerPtrs *d_layers = nullptr;
+    unsigned long long *t_qkv = nullptr, *t_part = nullptr, *t_ha = nullptr, *t_hb = nullptr, *t_f = nullptr,
+                       *t_best = nullptr;
+    int *d_err = nullptr;
+    unsigned long long *d_trace = nullptr;   // phase trace, when G2_MEGA_TRACE names an output file
+    std::string trace_path;
+    unsigned mega_epoch = 0;
+    int mega_grid = 0;
+    size_t mega_smem = 0;
 
     template <typename WT>
     const WT *w(size_t off) const {
@@ -127,7 +142,8 @@ static void free_engine(g2_engine *e) {
     for (auto g : e->dec_graph)
         if (g) cudaGraphExecDestroy(g);
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
-    void *dev_ptrs[] = {e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
+    void *dev_ptrs[] = {e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f,
+                        e->t_best, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
                         e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
                         e->argmax_out, e->batch_step, e->out_tokens, e->state};
@@ -179,6 +195,7 @@ static int load_weights(g2_engine *e, const std::string &dir) {
         size_t *off;
         int rows, cols;      // as stored on the device: [rows][cols]
         int kind;            // 0 vector/plain, 1 linear weight [in][out], 2 lm_head
+        int layer, ph;       // linear weights: layer and phase (0 qkv, 1 proj, 2 fc, 3 fc2)
     };
     std::vector<Item> items;
     e->L.resize(c.n_layer);
@@ -189,15 +206,15 @@ static int load_weights(g2_engine *e, const std::string &dir) {
         const std::string p = "h." + std::to_string(l) + ".";
         items.push_back({p + "ln_1.weight", &o.ln1_g, 1, E, 0});
         items.push_back({p + "ln_1.bias", &o.ln1_b, 1, E, 0});
-        items.push_back({p + "attn.c_attn.weight", &o.qkv_w, E, 3 * E, 1});
+        items.push_back({p + "attn.c_attn.weight", &o.qkv_w, E, 3 * E, 1, l, 0});
         items.push_back({p + "attn.c_attn.bias", &o.qkv_b, 1, 3 * E, 0});
-        items.push_back({p + "attn.c_proj.weight", &o.proj_w, E, E, 1});
+        items.push_back({p + "attn.c_proj.weight", &o.proj_w, E, E, 1, l, 1});
         items.push_back({p + "attn.c_proj.bias", &o.proj_b, 1, E, 0});
         items.push_back({p + "ln_2.weight", &o.ln2_g, 1, E, 0});
         items.push_back({p + "ln_2.bias", &o.ln2_b, 1, E, 0});
-        items.push_back({p + "mlp.c_fc.weight", &o.fc_w, E, F, 1});
+        items.push_back({p + "mlp.c_fc.weight", &o.fc_w, E, F, 1, l, 2});
         items.push_back({p + "mlp.c_fc.bias", &o.fc_b, 1, F, 0});
-        items.push_back({p + "mlp.c_proj.weight", &o.fc2_w, F, E, 1});
+        items.push_back({p + "mlp.c_proj.weight", &o.fc2_w, F, E, 1, l, 3});
         items.push_back({p + "mlp.c_proj.bias", &o.fc2_b, 1, E, 0});
     }
     items.push_back({"ln_f.weight", &e->lnf_g, 1, E, 0});
@@ -214,8 +231,26 @@ static int load_weights(g2_engine *e, const std::string &dir) {
     cudaError_t r = cudaMalloc(&e->wbuf, bytes);
     if (r != cudaSuccess) return set_err(G2_ERR_OOM, "cudaMalloc weights (%zu bytes): %s", bytes, cudaGetErrorString(r));
     e->device_bytes += bytes;
+    // Strip-packed copy of the projections for the persistent decode kernel:
+    // unit u of a [K][N] matrix with strip width CW holds W[k][u*CW + c] at
+    // [u][k][c], so each unit is one contiguous run of K * CW floats.
+    const int cw_e = mega_cw_e(E), cw_f = mega_cw_f();
+    if (e->mega) {
+        e->layer_off.assign((size_t)c.n_layer * 4, 0);
+        long long po = 0;
+        for (int l = 0; l < c.n_layer; ++l) {
+            const long long sz[4] = {(long long)E * 3 * E, (long long)E * E, (long long)E * F, (long long)F * E};
+            for (int q = 0; q < 4; ++q) {
+                e->layer_off[(size_t)l * 4 + q] = po;
+                po += (sz[q] + 63) / 64 * 64;
+            }
+        }
+        r = cudaMalloc(&e->packed, (size_t)po * 4);
+        if (r != cudaSuccess) return set_err(G2_ERR_OOM, "cudaMalloc packed weights: %s", cudaGetErrorString(r));
+        e->device_bytes += (size_t)po * 4;
+    }
 
-    std::vector<float> tmp, tr;
+    std::vector<float> tmp, tr, pk;
     std::vector<uint16_t> hv;
     for (auto &it : items) {
         const StTensor *t = sf.find(it.name);
@@ -253,6 +288,15 @@ static int load_weights(g2_engine *e, const std::string &dir) {
             } else if (!(t->shape[0] == V && t->shape[1] == E)) {
                 return set_err(G2_ERR_FORMAT, "lm_head.weight: unexpected shape");
             }
+        }
+        if (it.kind == 1 && e->mega) {
+            const int K = it.rows, N = it.cols, CW = it.ph == 3 ? cw_f : cw_e;
+            pk.resize(n);
+            for (int u = 0; u < N / CW; ++u)
+                for (int k = 0; k < K; ++k)
+                    for (int cc = 0; cc < CW; ++cc) pk[((size_t)u * K + k) * CW + cc] = src[(size_t)k * N + u * CW + cc];
+            r = cudaMemcpy(e->packed + e->layer_off[(size_t)it.layer * 4 + it.ph], pk.data(), n * 4, cudaMemcpyHostToDevice);
+            if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "upload packed '%s': %s", it.name.c_str(), cudaGetErrorString(r));
         }
         void *dst = (char *)e->wbuf + *it.off * e->esize;
         if (e->dtype == G2_F32) {
@@ -322,6 +366,19 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
             delete e;
             return set_err(G2_ERR_CUDA, "cudaStreamCreate: %s", cudaGetErrorString(r));
         }
+    }
+    {
+        // The persistent B = 1 decode kernel: fp32, one co-resident CTA per SM,
+        // its shared-memory ring and input vector within the opt-in limit.
+        const char *off = getenv("G2_NO_MEGA");
+        int coop = 0, optin = 0;
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+        const size_t smem = mega_smem_bytes(e->c.n_embd, e->c.ffn_dim);
+        e->mega = dtype == G2_F32 && !(off && off[0] == '1') && coop && smem <= (size_t)optin && e->sms <= 256 &&
+                  e->c.n_embd % mega_cw_e(e->c.n_embd) == 0 && e->c.ffn_dim % mega_cw_e(e->c.n_embd) == 0 &&
+                  e->c.n_embd * 4 <= 24576;
+        e->mega_smem = smem;
     }
     TRY(load_weights(e, model_dir));
     const ModelConfig &c = e->c;
@@ -399,6 +456,44 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
     }
     e->filled.assign(max_batch, 0);
     e->dec_graph.assign(max_batch, nullptr);
+    if (e->mega) {
+        TRY(dalloc(e, &e->t_qkv, (size_t)3 * E));
+        TRY(dalloc(e, &e->t_part, (size_t)NH * 16 * 66));
+        TRY(dalloc(e, &e->t_ha, (size_t)E));
+        TRY(dalloc(e, &e->t_hb, (size_t)E));
+        TRY(dalloc(e, &e->t_f, (size_t)F));
+        TRY(dalloc(e, &e->t_best, (size_t)4 * e->sms));
+        TRY(dalloc(e, &e->d_err, 1));
+        TRY(dalloc(e, &e->d_layer_off, e->layer_off.size()));
+        TRY(dalloc(e, &e->d_layers, (size_t)c.n_layer));
+        std::vector<LayerPtrs> lp(c.n_layer);
+        for (int l = 0; l < c.n_layer; ++l) {
+            const LayerOff &o = e->L[l];
+            lp[l] = LayerPtrs{e->w<float>(o.ln1_g), e->w<float>(o.ln1_b), e->w<float>(o.qkv_b), e->w<float>(o.proj_b),
+                              e->w<float>(o.ln2_g), e->w<float>(o.ln2_b), e->w<float>(o.fc_b), e->w<float>(o.fc2_b)};
+        }
+        cudaError_t r = cudaMemcpy(e->d_layers, lp.data(), sizeof(LayerPtrs) * lp.size(), cudaMemcpyHostToDevice);
+        if (r == cudaSuccess)
+            r = cudaMemcpy(e->d_layer_off, e->layer_off.data(), sizeof(long long) * e->layer_off.size(),
+                           cudaMemcpyHostToDevice);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(mega_kernel_ptr(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->mega_smem);
+        int per_sm = 0;
+        if (r == cudaSuccess)
+            r = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mega_kernel_ptr(), mega_threads(), e->mega_smem);
+        if (r != cudaSuccess) {
+            free_engine(e);
+            return set_err(G2_ERR_CUDA, "decode kernel setup: %s", cudaGetErrorString(r));
+        }
+        if (per_sm < 1) {
+            e->mega = false;   // cannot be co-resident: keep the graph path
+        }
+        e->mega_grid = e->sms;
+        if (const char *tp = getenv("G2_MEGA_TRACE")) {
+            e->trace_path = tp;
+            TRY(dalloc(e, &e->d_trace, (size_t)e->mega_grid * kTraceSlots));
+        }
+    }
 #undef TRY
     *out = e;
     return G2_OK;
@@ -544,6 +639,89 @@ static int decode_graph(g2_engine *e, int slot, cudaGraphExec_t *out) {
     return G2_OK;
 }
 
+// The persistent decode kernel for n_steps greedy steps of `slot`, starting
+// from e->state (token, pos, step, min_new) and leaving it advanced.
+static int launch_mega(g2_engine *e, int slot, int n_steps) {
+    const ModelConfig &c = e->c;
+    if (e->mega_epoch > 0xF0000000u) {   // epochs are 32-bit: restart them on cleared buffers
+        unsigned long long *bufs[6] = {e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f, e->t_best};
+        const size_t n[6] = {(size_t)3 * c.n_embd, (size_t)c.n_head * 16 * 66, (size_t)c.n_embd, (size_t)c.n_embd,
+                             (size_t)c.ffn_dim, (size_t)4 * e->sms};
+        for (int i = 0; i < 6; ++i) CK(cudaMemsetAsync(bufs[i], 0, n[i] * 8, e->st));
+        e->mega_epoch = 0;
+    }
+    MegaParams P;
+    P.L = c.n_layer;
+    P.E = c.n_embd;
+    P.F = c.ffn_dim;
+    P.NH = c.n_head;
+    P.V = c.vocab_size;
+    P.max_seq = e->kv.max_seq;
+    P.cw_e = mega_cw_e(P.E);
+    P.cw_f = mega_cw_f();
+    P.lm_rows = mega_lm_rows(P.E);
+    P.n_steps = n_steps;
+    P.layer_stride = e->kv.layer_stride;
+    P.packed = e->packed;
+    P.layer_off = e->d_layer_off;
+    P.layers = e->d_layers;
+    P.wte = e->w<float>(e->wte);
+    P.wpe = e->w<float>(e->wpe);
+    P.lnf_g = e->w<float>(e->lnf_g);
+    P.lnf_b = e->w<float>(e->lnf_b);
+    P.lm = e->w<float>(e->lm);
+    P.kc = reinterpret_cast<float *>(e->kbuf) + (size_t)slot * e->kv.slot_stride;
+    P.vc = reinterpret_cast<float *>(e->vbuf) + (size_t)slot * e->kv.slot_stride;
+    P.t_qkv = e->t_qkv;
+    P.t_part = e->t_part;
+    P.t_ha = e->t_ha;
+    P.t_hb = e->t_hb;
+    P.t_f = e->t_f;
+    P.t_best = e->t_best;
+    P.logits = e->logits + (size_t)slot * c.padded_vocab;
+    P.out_tokens = e->out_tokens + (size_t)slot * c.n_ctx;
+    P.result = e->result;
+    P.state = e->state;
+    P.err = e->d_err;
+    P.trace = e->d_trace;
+    P.epoch0 = e->mega_epoch + 1;
+    e->mega_epoch += mega_epochs(c.n_layer, n_steps);
+    void *args[] = {&P};
+    CK(cudaLaunchCooperativeKernel(mega_kernel_ptr(), dim3(e->mega_grid), dim3(mega_threads()), args, e->mega_smem,
+                                   e->st));
+    e->launches += 1;
+    return G2_OK;
+}
+
+// After a synchronised traced launch: append the per-CTA phase trace as one JSON line.
+static void dump_trace(g2_engine *e, int n_steps) {
+    if (!e->d_trace) return;
+    std::vector<unsigned long long> t((size_t)e->mega_grid * kTraceSlots);
+    if (cudaMemcpy(t.data(), e->d_trace, t.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return;
+    FILE *f = fopen(e->trace_path.c_str(), "a");
+    if (!f) return;
+    fprintf(f, "{\"steps\": %d, \"ctas\": [", n_steps);
+    for (int c = 0; c < e->mega_grid; ++c) {
+        fprintf(f, "%s[", c ? "," : "");
+        for (int i = 0; i < kTraceSlots; ++i) fprintf(f, "%s%llu", i ? "," : "", t[(size_t)c * kTraceSlots + i]);
+        fprintf(f, "]");
+    }
+    fprintf(f, "]}\n");
+    fclose(f);
+}
+
+// After a synchronisation: report an expired device-side wait of the decode kernel.
+static int check_mega_err(g2_engine *e) {
+    if (!e->mega) return G2_OK;
+    int code = 0;
+    CK(cudaMemcpy(&code, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code) {
+        CK(cudaMemset(e->d_err, 0, sizeof(int)));
+        return set_err(G2_ERR_TIMEOUT, "decode kernel: a bounded device-side wait expired (site %d)", code);
+    }
+    return G2_OK;
+}
+
 static int check_slot(const g2_engine *e, int slot) {
     if (slot < 0 || slot >= e->max_batch) return set_err(G2_ERR_RANGE, "slot %d out of range [0,%d)", slot, e->max_batch);
     return G2_OK;
@@ -586,15 +764,19 @@ extern "C" int g2_decode(g2_engine *e, int slot, int token, int pos) {
     if (pos < 0 || pos >= e->c.n_ctx) return set_err(G2_ERR_RANGE, "position %d out of range [0,%d)", pos, e->c.n_ctx);
     if (pos > e->filled[slot]) return set_err(G2_ERR_STATE, "position %d but slot %d holds %d positions", pos, slot, e->filled[slot]);
     CK(cudaSetDevice(e->device));
-    cudaGraphExec_t g;
-    if ((rc = decode_graph(e, slot, &g))) return rc;
+    cudaGraphExec_t g = nullptr;
+    if (!e->mega && (rc = decode_graph(e, slot, &g))) return rc;
     if (e->h_state_i == 0) CK(cudaStreamSynchronize(e->st));   // ring of pinned states wrapped
     StepState *hs = e->h_state + e->h_state_i;
     e->h_state_i = (e->h_state_i + 1) % 64;
     *hs = StepState{token, pos, slot, 0, 0, {0, 0, 0}};
     CK(cudaMemcpyAsync(e->state, hs, sizeof(StepState), cudaMemcpyHostToDevice, e->st));
-    CK(cudaGraphLaunch(g, e->st));
-    e->launches += e->dec_graph_kernels;
+    if (e->mega) {
+        if ((rc = launch_mega(e, slot, 1))) return rc;
+    } else {
+        CK(cudaGraphLaunch(g, e->st));
+        e->launches += e->dec_graph_kernels;
+    }
     e->filled[slot] = pos + 1;
     e->result_slot = slot;
     return G2_OK;
@@ -643,7 +825,7 @@ extern "C" int g2_logits(g2_engine *e, int slot, float *host, int n) {
     CK(cudaSetDevice(e->device));
     CK(cudaMemcpyAsync(host, e->logits + (size_t)slot * e->c.padded_vocab, sizeof(float) * n, cudaMemcpyDeviceToHost, e->st));
     CK(cudaStreamSynchronize(e->st));
-    return G2_OK;
+    return check_mega_err(e);
 }
 
 extern "C" int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, float *value) {
@@ -651,17 +833,26 @@ extern "C" int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, flo
     int rc;
     if ((rc = check_slot(e, slot))) return rc;
     CK(cudaSetDevice(e->device));
-    const int *src = e->result;
-    if (e->result_slot != slot || forbid_eos) {
-        launch_argmax_rows(e->logits + (size_t)slot * e->c.padded_vocab, e->c.vocab_size, e->c.padded_vocab, 1,
-                           forbid_eos, e->argmax_out, reinterpret_cast<float *>(e->argmax_out + 1), nullptr, nullptr,
-                           nullptr, 0, nullptr, e->st);
-        e->launches += 1;
-        CKL();
-        src = e->argmax_out;
+    if (e->result_slot == slot) {
+        // the LM-head kernel's argmax (no EOS exclusion); it also answers the
+        // EOS-excluding query whenever its token is not EOS
+        CK(cudaMemcpyAsync(e->h_small, e->result, 2 * sizeof(int), cudaMemcpyDeviceToHost, e->st));
+        CK(cudaStreamSynchronize(e->st));
+        if ((rc = check_mega_err(e))) return rc;
+        if (!forbid_eos || e->h_small[0] != kEos) {
+            *token = e->h_small[0];
+            if (value) memcpy(value, &e->h_small[1], 4);
+            return G2_OK;
+        }
     }
-    CK(cudaMemcpyAsync(e->h_small, src, 2 * sizeof(int), cudaMemcpyDeviceToHost, e->st));
+    launch_argmax_rows(e->logits + (size_t)slot * e->c.padded_vocab, e->c.vocab_size, e->c.padded_vocab, 1, forbid_eos,
+                       e->argmax_out, reinterpret_cast<float *>(e->argmax_out + 1), nullptr, nullptr, nullptr, 0,
+                       nullptr, e->st);
+    e->launches += 1;
+    CKL();
+    CK(cudaMemcpyAsync(e->h_small, e->argmax_out, 2 * sizeof(int), cudaMemcpyDeviceToHost, e->st));
     CK(cudaStreamSynchronize(e->st));
+    if ((rc = check_mega_err(e))) return rc;
     *token = e->h_small[0];
     if (value) memcpy(value, &e->h_small[1], 4);
     return G2_OK;
@@ -671,7 +862,7 @@ extern "C" int g2_synchronize(g2_engine *e) {
     if (!e) return set_err(G2_ERR_ARG, "null engine");
     CK(cudaSetDevice(e->device));
     CK(cudaStreamSynchronize(e->st));
-    return G2_OK;
+    return check_mega_err(e);
 }
 
 extern "C" int g2_last_timing(g2_engine *e, float *prefill_ms, float *decode_ms, int *decode_steps) {
@@ -693,8 +884,8 @@ extern "C" int g2_generate(g2_engine *e, int slot, const int *prompt, int n_prom
     const int cap = e->c.n_ctx - n_prompt;
     if (n_new > cap) n_new = cap;
     CK(cudaSetDevice(e->device));
-    cudaGraphExec_t g;
-    if ((rc = decode_graph(e, slot, &g))) return rc;
+    cudaGraphExec_t g = nullptr;
+    if (!e->mega && (rc = decode_graph(e, slot, &g))) return rc;
     CK(cudaStreamSynchronize(e->st));
     StepState *hs = e->h_state + e->h_state_i;
     e->h_state_i = (e->h_state_i + 1) % 64;
@@ -706,12 +897,18 @@ extern "C" int g2_generate(g2_engine *e, int slot, const int *prompt, int n_prom
                             : lm_head_row<__half>(e, n_prompt - 1, slot, e->state);
     if (rc) return rc;
     CK(cudaEventRecord(e->ev[1], e->st));
-    for (int i = 1; i < n_new; ++i) CK(cudaGraphLaunch(g, e->st));
-    e->launches += (long long)(n_new - 1) * e->dec_graph_kernels;
+    if (e->mega) {
+        if (n_new > 1 && (rc = launch_mega(e, slot, n_new - 1))) return rc;
+    } else {
+        for (int i = 1; i < n_new; ++i) CK(cudaGraphLaunch(g, e->st));
+        e->launches += (long long)(n_new - 1) * e->dec_graph_kernels;
+    }
     CK(cudaEventRecord(e->ev[2], e->st));
     CK(cudaMemcpyAsync(out_tokens, e->out_tokens + (size_t)slot * e->c.n_ctx, sizeof(int) * n_new,
                        cudaMemcpyDeviceToHost, e->st));
     CK(cudaStreamSynchronize(e->st));
+    if ((rc = check_mega_err(e))) return rc;
+    if (e->mega && n_new > 1) dump_trace(e, n_new - 1);
     CK(cudaEventElapsedTime(&e->last_prefill_ms, e->ev[0], e->ev[1]));
     CK(cudaEventElapsedTime(&e->last_decode_ms, e->ev[1], e->ev[2]));
     e->last_decode_steps = n_new - 1;

@@ -129,6 +129,45 @@ def test_prefill_decode_vs_oracle_affine(g2, tiny_affine_model):
     ref.close()
 
 
+def test_persistent_and_graph_decode_agree(g2, tiny_affine_model, monkeypatch):
+    """The persistent decode kernel (default for fp32) and the per-kernel graph
+    path (G2_NO_MEGA=1) give the same greedy stream and matching logits, and
+    the persistent kernel runs one launch for a whole generation."""
+    prompt = synth.prompt_ids(21, 30)
+    out = {}
+    for mode in ("persistent", "graph"):
+        if mode == "graph":
+            monkeypatch.setenv("G2_NO_MEGA", "1")
+        with g2.Engine(tiny_affine_model) as eng:
+            l0 = eng.launch_count()
+            toks = eng.generate(prompt, 40)
+            launches = eng.launch_count() - l0
+            eng.prefill(prompt)
+            lg = [eng.logits()]
+            tok = int(np.argmax(lg[0][:50257]))
+            for s in range(5):
+                eng.decode(tok, 30 + s)
+                lg.append(eng.logits())
+                tok = int(np.argmax(lg[-1][:50257]))
+        out[mode] = (toks, lg, launches)
+    assert list(out["persistent"][0]) == list(out["graph"][0])
+    for a, b in zip(out["persistent"][1], out["graph"][1]):
+        assert rel(a, b) <= 1e-5
+    # 39 decode steps: one persistent launch vs 39 graph replays of 2 + 5 L kernels
+    assert out["persistent"][2] < out["graph"][2] - 30 * 12
+
+
+def test_long_context_persistent(g2, tiny_affine_model):
+    """Positions up to the end of the context (16 attention chunks) against the oracle."""
+    prompt = synth.prompt_ids(22, 900)
+    ref = oracle.RefModel(tiny_affine_model)
+    want = ref.generate(prompt, 124)
+    ref.close()
+    with g2.Engine(tiny_affine_model) as eng:
+        got = eng.generate(prompt, 124)
+    assert list(got) == list(want)
+
+
 def test_fp16_engine_vs_oracle_on_rounded_weights(g2, tmp_path):
     """fp16 weights + KV: within 2e-2 of the fp32 oracle run on the same fp16-rounded weights."""
     d = synth.make_model(str(tmp_path / "f16"), synth.TINY, seed=4, dtype="f16", affine=True)
