@@ -114,7 +114,9 @@ struct g2_engine {
     unsigned long long *d_trace = nullptr;   // phase trace, when G2_MEGA_TRACE names an output file
     std::string trace_path;
     unsigned mega_epoch = 0;
+    int mega_inflight = 3;   // outstanding bulk copies per CTA (G2_MEGA_INFLIGHT overrides)
     int mega_grid = 0;
+    int mega_cw[4] = {0, 0, 0, 0};   // strip widths of qkv, proj, fc, fc2
     size_t mega_smem = 0;
 
     template <typename WT>
@@ -169,6 +171,33 @@ static int dalloc(g2_engine *e, T **p, size_t count) {
     r = cudaMemset(*p, 0, bytes);
     if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(r));
     return G2_OK;
+}
+
+// One projection W [K][N] packed for the persistent decode kernel: unit u
+// (columns u*CW .. u*CW + CW - 1) is (K + 1) rows x CW, rows k < K holding
+// g[k] * W[k][n] and row K holding b[n] + sum_k beta[k] * W[k][n].  With g and
+// beta the preceding LayerNorm's parameters this folds the LayerNorm's affine
+// part into the projection: (norm(x) * g + beta) W + b = norm(x) (diag(g) W) +
+// (beta W + b).  Without a LayerNorm (g = beta = nullptr) the rows are W and b.
+static void pack_strips(const float *W, const float *b, const float *g, const float *beta, int K, int N, int CW,
+                        float *out) {
+    for (int u = 0; u < N / CW; ++u) {
+        float *o = out + (size_t)u * (K + 2) * CW;
+        for (int k = 0; k < K; ++k) {
+            const float gk = g ? g[k] : 1.0f;
+            for (int cc = 0; cc < CW; ++cc) o[(size_t)k * CW + cc] = gk * W[(size_t)k * N + u * CW + cc];
+        }
+        for (int cc = 0; cc < CW; ++cc) {
+            const int n = u * CW + cc;
+            double acc = b[n], cs = 0.0;
+            if (beta)
+                for (int k = 0; k < K; ++k) acc += (double)beta[k] * (double)W[(size_t)k * N + n];
+            if (g)   // sums of the stored (rounded) W' column: x W' - mean * sum_k W'[k] = (x - mean) W'
+                for (int k = 0; k < K; ++k) cs += (double)o[(size_t)k * CW + cc];
+            o[(size_t)K * CW + cc] = (float)acc;
+            o[(size_t)(K + 1) * CW + cc] = (float)cs;
+        }
+    }
 }
 
 // Load every tensor into one device buffer, converted to the engine dtype.
@@ -231,15 +260,15 @@ static int load_weights(g2_engine *e, const std::string &dir) {
     cudaError_t r = cudaMalloc(&e->wbuf, bytes);
     if (r != cudaSuccess) return set_err(G2_ERR_OOM, "cudaMalloc weights (%zu bytes): %s", bytes, cudaGetErrorString(r));
     e->device_bytes += bytes;
-    // Strip-packed copy of the projections for the persistent decode kernel:
-    // unit u of a [K][N] matrix with strip width CW holds W[k][u*CW + c] at
-    // [u][k][c], so each unit is one contiguous run of K * CW floats.
-    const int cw_e = mega_cw_e(E), cw_f = mega_cw_f();
+    // Strip-packed copy of the projections for the persistent decode kernel
+    // (pack_strips): each unit is one contiguous run of (K + 2) * CW floats.
+    const int *cw = e->mega_cw;
     if (e->mega) {
         e->layer_off.assign((size_t)c.n_layer * 4, 0);
         long long po = 0;
         for (int l = 0; l < c.n_layer; ++l) {
-            const long long sz[4] = {(long long)E * 3 * E, (long long)E * E, (long long)E * F, (long long)F * E};
+            const long long sz[4] = {mega_packed_floats(E, 3 * E), mega_packed_floats(E, E), mega_packed_floats(E, F),
+                                     mega_packed_floats(F, E)};
             for (int q = 0; q < 4; ++q) {
                 e->layer_off[(size_t)l * 4 + q] = po;
                 po += (sz[q] + 63) / 64 * 64;
@@ -249,6 +278,9 @@ static int load_weights(g2_engine *e, const std::string &dir) {
         if (r != cudaSuccess) return set_err(G2_ERR_OOM, "cudaMalloc packed weights: %s", cudaGetErrorString(r));
         e->device_bytes += (size_t)po * 4;
     }
+    // host copies of the current layer's tensors until all twelve are read
+    std::vector<std::vector<float>> layer_t(12);
+    int layer_have = 0;
 
     std::vector<float> tmp, tr, pk;
     std::vector<uint16_t> hv;
@@ -289,14 +321,30 @@ static int load_weights(g2_engine *e, const std::string &dir) {
                 return set_err(G2_ERR_FORMAT, "lm_head.weight: unexpected shape");
             }
         }
-        if (it.kind == 1 && e->mega) {
-            const int K = it.rows, N = it.cols, CW = it.ph == 3 ? cw_f : cw_e;
-            pk.resize(n);
-            for (int u = 0; u < N / CW; ++u)
-                for (int k = 0; k < K; ++k)
-                    for (int cc = 0; cc < CW; ++cc) pk[((size_t)u * K + k) * CW + cc] = src[(size_t)k * N + u * CW + cc];
-            r = cudaMemcpy(e->packed + e->layer_off[(size_t)it.layer * 4 + it.ph], pk.data(), n * 4, cudaMemcpyHostToDevice);
-            if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "upload packed '%s': %s", it.name.c_str(), cudaGetErrorString(r));
+        if (e->mega && it.name.compare(0, 2, "h.") == 0) {
+            // the layer's tensors arrive in the order ln_1.w/b, c_attn.w/b, attn.c_proj.w/b,
+            // ln_2.w/b, c_fc.w/b, mlp.c_proj.w/b; pack the four projections once all are here
+            layer_t[layer_have].assign(src, src + n);
+            if (++layer_have == 12) {
+                const int l = atoi(it.name.c_str() + 2);   // "h.<l>.mlp.c_proj.bias"
+                const std::vector<float> *T = layer_t.data();
+                struct P {
+                    const std::vector<float> &w, &b;
+                    const float *g, *beta;
+                    int K, N, CW, ph;
+                } proj[4] = {{T[2], T[3], T[0].data(), T[1].data(), E, 3 * E, cw[0], 0},
+                             {T[4], T[5], nullptr, nullptr, E, E, cw[1], 1},
+                             {T[8], T[9], T[6].data(), T[7].data(), E, F, cw[2], 2},
+                             {T[10], T[11], nullptr, nullptr, F, E, cw[3], 3}};
+                for (const P &q : proj) {
+                    pk.resize((size_t)mega_packed_floats(q.K, q.N));
+                    pack_strips(q.w.data(), q.b.data(), q.g, q.beta, q.K, q.N, q.CW, pk.data());
+                    r = cudaMemcpy(e->packed + e->layer_off[(size_t)l * 4 + q.ph], pk.data(), pk.size() * 4,
+                                   cudaMemcpyHostToDevice);
+                    if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "upload packed layer %d: %s", l, cudaGetErrorString(r));
+                }
+                layer_have = 0;
+            }
         }
         void *dst = (char *)e->wbuf + *it.off * e->esize;
         if (e->dtype == G2_F32) {
@@ -375,9 +423,17 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
         const size_t smem = mega_smem_bytes(e->c.n_embd, e->c.ffn_dim);
-        e->mega = dtype == G2_F32 && !(off && off[0] == '1') && coop && smem <= (size_t)optin && e->sms <= 256 &&
-                  e->c.n_embd % mega_cw_e(e->c.n_embd) == 0 && e->c.ffn_dim % mega_cw_e(e->c.n_embd) == 0 &&
-                  e->c.n_embd * 4 <= 24576;
+        const int G = e->sms, E = e->c.n_embd, F = e->c.ffn_dim;
+        int *cw = e->mega_cw;
+        cw[0] = mega_cw(3 * E, G);
+        cw[1] = mega_cw(E, G);
+        cw[2] = mega_cw(F, G);
+        cw[3] = mega_cw(E, G);
+        const bool widths = cw[0] && cw[1] && cw[2] && cw[3];
+        // residual values per CTA and phase must fit the kernel's 64-float buffer
+        const int res_c = widths ? (E / cw[1] + G - 1) / G * cw[1] : 0, res_e = widths ? (E / cw[3] + G - 1) / G * cw[3] : 0;
+        e->mega = dtype == G2_F32 && !(off && off[0] == '1') && coop && smem <= (size_t)optin && G <= 256 && widths &&
+                  E * 4 <= mega_slot_bytes() && res_c <= 64 && res_e <= 64;
         e->mega_smem = smem;
     }
     TRY(load_weights(e, model_dir));
@@ -489,6 +545,10 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
             e->mega = false;   // cannot be co-resident: keep the graph path
         }
         e->mega_grid = e->sms;
+        if (const char *fl = getenv("G2_MEGA_INFLIGHT")) {
+            const int v = atoi(fl);
+            if (v >= 1 && v <= 8) e->mega_inflight = v;
+        }
         if (const char *tp = getenv("G2_MEGA_TRACE")) {
             e->trace_path = tp;
             TRY(dalloc(e, &e->d_trace, (size_t)e->mega_grid * kTraceSlots));
@@ -657,8 +717,7 @@ static int launch_mega(g2_engine *e, int slot, int n_steps) {
     P.NH = c.n_head;
     P.V = c.vocab_size;
     P.max_seq = e->kv.max_seq;
-    P.cw_e = mega_cw_e(P.E);
-    P.cw_f = mega_cw_f();
+    for (int q = 0; q < 4; ++q) P.cw[q] = e->mega_cw[q];
     P.lm_rows = mega_lm_rows(P.E);
     P.n_steps = n_steps;
     P.layer_stride = e->kv.layer_stride;
@@ -684,6 +743,7 @@ static int launch_mega(g2_engine *e, int slot, int n_steps) {
     P.state = e->state;
     P.err = e->d_err;
     P.trace = e->d_trace;
+    P.max_inflight = e->mega_inflight;
     P.epoch0 = e->mega_epoch + 1;
     e->mega_epoch += mega_epochs(c.n_layer, n_steps);
     void *args[] = {&P};
