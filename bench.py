@@ -80,7 +80,7 @@ class Clocks:
         try:
             self.f = open(self.path, "w")
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                       "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.p = None
 
@@ -202,11 +202,16 @@ def run_ours(args, cfg):
     import gpt2b200 as g2
     from gpt2b200 import synth
     d, shape = model_for(cfg)
-    B = cfg["batch"]
+    from gpt2b200 import replicas
+    # sequences of this rank: c4 splits 32 in total over the ranks (strong), the others
+    # give every rank its own `batch` sequences (weak); prompts are seeded by global index
+    scaling = "strong" if args.config == "c4" else "weak"
+    mine = replicas.shard(cfg["batch"], ws, rank, scaling)
+    B = len(mine)
     dtype = g2.G2_F16 if cfg["dtype"] == "f16" else g2.G2_F32
     eng = g2.Engine(d, device=local if ws > 1 else 0, max_batch=B, dtype=dtype)
     n_new = cfg["steps"] + 1
-    prompts = [synth.prompt_ids(1000 * rank + i, cfg["prompt"]) for i in range(B)]
+    prompts = [synth.prompt_ids(i, cfg["prompt"]) for i in mine]
 
     def one_step():
         if B == 1:
@@ -236,12 +241,25 @@ def run_ours(args, cfg):
     barrier()
     clk = clocks.stop()
     launches = eng.launch_count() - l0
-    # e2e: the same workload through the host-driven C ABI calls
+    # e2e: the same workload through the C ABI with host buffers, wall-clock: g2_generate
+    # (prompt ids copied from host memory, generated ids copied back), and for B = 1 also
+    # the reference's host loop (g2_prefill, then per token g2_decode + g2_argmax).
     e2e_t = 0.0
     e2e_tokens = 0
-    h2d = d2h = 0
+    loop_t, loop_tokens = 0.0, 0
+    reps = max(1, min(args.steps, 3))
+    for _ in range(reps):
+        t1 = time.perf_counter()
+        if B == 1:
+            eng.generate(prompts[0], n_new)
+        else:
+            eng.generate_batch(prompts, n_new)
+        e2e_t += time.perf_counter() - t1
+        e2e_tokens += cfg["steps"] * B
+    h2d = 4 * B * cfg["prompt"] + 12 * B
+    d2h = 4 * B * n_new
     if B == 1:
-        for _ in range(max(1, min(args.steps, 3))):
+        for _ in range(reps):
             t1 = time.perf_counter()
             eng.prefill(prompts[0])
             tok, _ = eng.argmax(forbid_eos=True)
@@ -249,30 +267,17 @@ def run_ours(args, cfg):
             for s in range(cfg["steps"]):
                 eng.decode(tok, pos + s)
                 tok, _ = eng.argmax(forbid_eos=True)
-            e2e_t += time.perf_counter() - t1
-            e2e_tokens += cfg["steps"]
-        h2d = 3 * 4 * cfg["prompt"] + 32 * cfg["steps"]
-        d2h = 8 * (cfg["steps"] + 1)
-    elif args.steps > 0:
-        t1 = time.perf_counter()
-        eng.generate_batch(prompts, n_new)
-        e2e_t = time.perf_counter() - t1
-        e2e_tokens = cfg["steps"] * B
-        h2d = 4 * B * cfg["prompt"] * 3 + 12 * B
-        d2h = 4 * B * n_new
+            loop_t += time.perf_counter() - t1
+            loop_tokens += cfg["steps"]
     cfgd = eng.cfg
     elem = 2 if cfg["dtype"] == "f16" else 4
     per_seq_kv = kv_bytes(shape, elem, cfg["prompt"], cfg["steps"], 1)
     bytes_per_step = cfgd.weight_bytes + per_seq_kv * B / cfg["steps"] + B * (2 * shape.n_embd * elem + 4 * shape.padded_vocab)
-    t_local = torch.tensor([dec_ms, pre_ms, wall], dtype=torch.float64, device="cuda")
-    if ws > 1:
-        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
-    dec_max, pre_max, wall_max = [float(x) for x in t_local.tolist()]
-    e2e_local = torch.tensor([e2e_t], dtype=torch.float64, device="cuda")
-    if ws > 1:
-        dist.all_reduce(e2e_local, op=dist.ReduceOp.MAX)
+    dec_max, pre_max, wall_max = replicas.max_over_ranks([dec_ms, pre_ms, wall], device="cuda")
+    e2e_local = replicas.max_over_ranks([e2e_t, loop_t], device="cuda")
     if rank == 0:
-        total_tokens = dec_steps * B * ws
+        n_total = cfg["batch"] * (ws if scaling == "weak" else 1)    # sequences over all ranks
+        total_tokens = dec_steps * n_total
         value = total_tokens / (dec_max / 1000.0)
         step_s = dec_max / 1000.0 / max(dec_steps, 1)            # seconds per decode step (all B rows)
         achieved = bytes_per_step / step_s / 1e9
@@ -281,25 +286,34 @@ def run_ours(args, cfg):
         tp = os.path.join(ROOT, "profiles", f"traffic_{args.config}.json")
         if os.path.exists(tp):
             traffic = json.load(open(tp)).get("bytes_per_decode_step")
+        persistent = bool(cfgd.persistent) and B == 1
+        kernel = ("mega_decode_kernel (persistent: every layer, LM head and greedy argmax of all decode steps "
+                  "in one launch)" if persistent else
+                  "decode step kernels (embed, 5 per layer, LM head + argmax)" + (" in a CUDA graph" if B == 1 else ""))
+        e2e_max, loop_max = e2e_local
         line = {
             "metric": "decode tok/s (B=1 ms/token; batched) + HBM GB/s % of peak",
             "value": round(value, 3), "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round((dec_max + pre_max) / max(args.steps, 1), 4),
             "ms_per_token": round(1000.0 * step_s, 5),
             "prefill_ms": round(pre_max / max(args.steps, 1), 4),
-            "higher_is_better": True, "scaling": "weak",
+            "higher_is_better": True, "scaling": scaling,
             "vs_baseline": round((value / ws) / (1000.0 / README_DECODE_MS), 2) if args.config in ("c1", "c3") else None,
             "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,0.02) weights, seeded uniform prompt ids)",
             "config": {"workload": args.config, "description": cfg["desc"], "sequences_per_gpu": B,
                        "decode_steps_per_step": cfg["steps"], "parallelism": f"replicas x{ws} (independent sequences)",
                        "l2": f"weights {cfgd.weight_bytes / 1e6:.0f} MB per decode step > 126 MB L2 (no flush needed)"},
-            "roofline": {"bound": "hbm", "kernel": "decode step (embed + 5 kernels/layer + lm_head, CUDA graph)",
+            "roofline": {"bound": "hbm", "kernel": kernel,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "bytes_per_step": int(bytes_per_step), "traffic": traffic},
-            "e2e": {"value": round(e2e_tokens * ws / e2e_local.item(), 3) if e2e_t > 0 else None, "unit": "tok/s",
+            "e2e": {"value": round(e2e_tokens / B * n_total / e2e_max, 3) if e2e_max > 0 else None, "unit": "tok/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "g2_prefill + per-token g2_decode/g2_argmax (C ABI, host buffers)" if B == 1 else "g2_generate_batch"},
+                    "path": ("g2_generate" if B == 1 else "g2_generate_batch") + " (C ABI, host buffers, wall-clock, "
+                            "prefill included)",
+                    "host_loop": ({"value": round(loop_tokens * ws / loop_max, 3), "unit": "tok/s",
+                                   "path": "g2_prefill + per-token g2_decode/g2_argmax (the reference's host loop)"}
+                                  if loop_max > 0 else None)},
             "gpu_launches": int(launches) * ws,
             "wall_s": round(wall_max, 4),
         }
@@ -320,16 +334,18 @@ def run_ours(args, cfg):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-steps", type=int, default=0,
+                    help="override the workload's decode steps (short runs for profiler captures; not a bench number)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
+    if args.decode_steps > 0:
+        cfg["steps"] = args.decode_steps
     ws, _, _ = dist_env()
-    if args.config == "c4":
-        cfg["batch"] = max(1, 32 // ws)   # 32 sequences in total: strong scaling across GPUs
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

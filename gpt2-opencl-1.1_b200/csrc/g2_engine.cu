@@ -579,6 +579,7 @@ extern "C" int g2_get_config(const g2_engine *e, g2_config *out) {
     out->device = e->device;
     out->weight_bytes = e->stream_bytes;
     out->device_bytes = e->device_bytes;
+    out->persistent = e->mega ? 1 : 0;
     return G2_OK;
 }
 

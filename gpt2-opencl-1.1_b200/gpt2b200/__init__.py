@@ -30,7 +30,7 @@ class Config(C.Structure):
     _fields_ = [("n_layer", C.c_int), ("n_embd", C.c_int), ("n_head", C.c_int), ("n_ctx", C.c_int),
                 ("vocab_size", C.c_int), ("ffn_dim", C.c_int), ("padded_vocab", C.c_int), ("dtype", C.c_int),
                 ("max_batch", C.c_int), ("device", C.c_int), ("weight_bytes", C.c_size_t),
-                ("device_bytes", C.c_size_t)]
+                ("device_bytes", C.c_size_t), ("persistent", C.c_int)]
 
 
 def _load():

@@ -59,6 +59,8 @@ typedef struct g2_config {
     int device;
     size_t weight_bytes;   /* bytes of weights streamed per decode step (for GB/s) */
     size_t device_bytes;   /* device memory held by the engine */
+    int persistent;        /* 1: B = 1 decode runs the persistent kernel (one launch per
+                              g2_decode / g2_generate); 0: per-layer kernels in a CUDA graph */
 } g2_config;
 
 const char *g2_last_error(void);
