@@ -1,0 +1,59 @@
+// g2_device.cuh -- device helpers shared by the kernel files: element
+// conversion, the tanh GELU (math.cl:21-23) and the GEMM epilogue.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "g2_internal.h"
+
+namespace g2 {
+
+__device__ __forceinline__ float tof(float v) { return v; }
+__device__ __forceinline__ float tof(__half v) { return __half2float(v); }
+template <typename T>
+__device__ __forceinline__ T fromf(float v);
+template <>
+__device__ __forceinline__ float fromf<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half fromf<__half>(float v) { return __float2half_rn(v); }
+
+// tanh-form GELU (math.cl:21-23, HF "gelu_new").
+__device__ __forceinline__ float gelu_f(float v) {
+    return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
+}
+
+// Epilogue shared by gemv and gemm: v = acc (+bias) (GELU) (+resid), stored to
+// out[r][n]; with EPI_KV the K and V thirds of a qkv row are also appended to
+// the cache at (slot[r], layer, head, pos[r]) -- split_kv (math.cl:367-383).
+template <typename WT>
+struct Epi {
+    const WT *bias;
+    const float *resid;
+    float *out;
+    int N, epi;
+    KVLayout kv;
+    int layer;
+    const int *pos;
+    const int *slot;
+    int E;
+
+    __device__ __forceinline__ void apply(int r, int n, float v) const {
+        if (epi & EPI_BIAS) v += tof(bias[n]);
+        if (epi & EPI_GELU) v = gelu_f(v);
+        if (epi & EPI_RESID) v = resid[(size_t)r * N + n] + v;
+        out[(size_t)r * N + n] = v;
+        if ((epi & EPI_KV) && n >= E) {
+            int m = n - E;
+            const bool isv = m >= E;
+            if (isv) m -= E;
+            const int h = m >> 6, d = m & 63;
+            const int p = pos[r];
+            if (p < 0 || p >= kv.max_seq) return;   // positions are validated on the host; never write outside
+            const long long off = (long long)slot[r] * kv.slot_stride + (long long)layer * kv.layer_stride +
+                                  ((long long)h * kv.max_seq + p) * kHeadDim + d;
+            WT *base = reinterpret_cast<WT *>(isv ? kv.v : kv.k);
+            base[off] = fromf<WT>(v);
+        }
+    }
+};
+
+}  // namespace g2

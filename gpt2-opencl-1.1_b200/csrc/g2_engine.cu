@@ -15,6 +15,7 @@
 #include "g2_internal.h"
 #include "g2_loader.h"
 #include "g2_mega.h"
+#include "g2_tc.h"
 #include "gpt2b200.h"
 
 using namespace g2;
@@ -1115,6 +1116,66 @@ extern "C" int g2k_matmul(const float *A, const float *B, const float *bias, con
     const int epi = (bias ? EPI_BIAS : 0) | (apply_gelu ? EPI_GELU : 0) | (residual ? EPI_RESID : 0);
     launch_gemm_rows<float>(A, B, bias, residual, C, M, N, K, epi, nullptr, 0, Rows{nullptr, nullptr, nullptr},
                             (cudaStream_t)stream);
+    CKL();
+    return G2_OK;
+}
+
+// Workspace of g2k_matmul_tc: [err | A hi | A lo | B hi | B lo | partial sums], 256-byte aligned parts.
+static size_t tc_ws_layout(int M, int N, int K, int precision, int sms, size_t off[6]) {
+    const int kind = precision == G2_F16 ? TC_F16 : TC_TF32X3;
+    const size_t es = kind == TC_F16 ? 2 : 4;
+    const size_t sz[6] = {256, (size_t)M * K * es, kind == TC_F16 ? 0 : (size_t)M * K * 4, (size_t)K * N * es,
+                          kind == TC_F16 ? 0 : (size_t)K * N * 4, tc_partial_floats(M, N, K, kind, sms) * 4};
+    size_t o = 0;
+    for (int i = 0; i < 6; ++i) {
+        off[i] = o;
+        o += align_up(sz[i], 256);
+    }
+    return o;
+}
+static int device_sms() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+extern "C" size_t g2k_matmul_tc_workspace(int M, int N, int K, int precision) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    size_t off[6];
+    return tc_ws_layout(M, N, K, precision, device_sms(), off);
+}
+
+extern "C" int g2k_matmul_tc(const float *A, const float *B, const float *bias, const float *residual, float *C, int M,
+                             int N, int K, int apply_gelu, int precision, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+    if (!A || !B || !C || !workspace) return set_err(G2_ERR_ARG, "g2k_matmul_tc: null argument");
+    if (precision != G2_F32 && precision != G2_F16) return set_err(G2_ERR_ARG, "g2k_matmul_tc: bad precision");
+    if (M <= 0 || N <= 0 || K <= 0 || K % 64 || N % 8)
+        return set_err(G2_ERR_ARG, "g2k_matmul_tc: need K %% 64 == 0 and N %% 8 == 0");
+    if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)C) & 15) return set_err(G2_ERR_ARG, "g2k_matmul_tc: pointers not 16-byte aligned");
+    if ((uintptr_t)workspace % 256) return set_err(G2_ERR_ARG, "g2k_matmul_tc: workspace not 256-byte aligned");
+    const int sms = device_sms();
+    size_t off[6];
+    if (workspace_bytes < tc_ws_layout(M, N, K, precision, sms, off)) return set_err(G2_ERR_ARG, "g2k_matmul_tc: workspace too small");
+    const int kind = precision == G2_F16 ? TC_F16 : TC_TF32X3;
+    char *ws = static_cast<char *>(workspace);
+    cudaStream_t st = (cudaStream_t)stream;
+    int *err = reinterpret_cast<int *>(ws);
+    CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+    float *ahi = reinterpret_cast<float *>(ws + off[1]), *alo = reinterpret_cast<float *>(ws + off[2]);
+    float *bhi = reinterpret_cast<float *>(ws + off[3]), *blo = reinterpret_cast<float *>(ws + off[4]);
+    launch_tc_prep(kind, A, ahi, alo, reinterpret_cast<__half *>(ahi), (long long)M * K, st);
+    launch_tc_prep(kind, B, bhi, blo, reinterpret_cast<__half *>(bhi), (long long)K * N, st);
+    TcWeights w;
+    TcRowsOperand x;
+    int rc = tc_weights(&w, kind, bhi, blo, K, N);
+    if (!rc) rc = tc_rows_operand(&x, kind, ahi, alo, K, M);
+    if (rc) return set_err(rc, "g2k_matmul_tc: tensor map encoding failed");
+    const int epi = (bias ? EPI_BIAS : 0) | (apply_gelu ? EPI_GELU : 0) | (residual ? EPI_RESID : 0);
+    launch_tc_gemm<float>(kind, w, x, M, reinterpret_cast<float *>(ws + off[5]),
+                          tc_partial_floats(M, N, K, kind, sms), err, bias, residual, C, epi, nullptr, 0,
+                          Rows{nullptr, nullptr, nullptr}, sms, st);
     CKL();
     return G2_OK;
 }

@@ -1,0 +1,493 @@
+// g2_tc.cu -- tensor-core GEMM (tcgen05 + TMA) for many-row passes.
+//
+// out[r][n] = epilogue(sum_k X[r][k] W[k][n]) for the R rows of a prefill
+// (the runtime matmul of prefill, main.c:593-684 via launch_matmul
+// main.c:1518, with its bias / gelu / add_inplace / split_kv epilogues,
+// main.c:1759-1786) or of a batched decode step (one token of each of R
+// sequences).
+//
+// Mapping onto tcgen05.mma (cta_group::1, M = 128):
+//   * MMA A = W^T: 128 output features x K.  The Conv1D weights [K][N] are
+//     feature-contiguous, which is the MN-major operand layout, so they are
+//     used in place: TMA boxes of 128 bytes of features x BK rows, 128-byte
+//     swizzle.
+//   * MMA B = X^T: K x BN rows, K-major (X [R][K] rows are K-contiguous).
+//   * D (fp32) lives in tensor memory: 128 lanes (features) x BN columns
+//     (rows); the epilogue warps read it with tcgen05.ld and store
+//     feature-contiguous, coalesced rows.
+// One CTA computes a 128 x BN tile over a range of K (split-K when the tiles
+// alone cannot fill the SMs); partial tiles go to a scratch buffer and one
+// small kernel sums the splits in order and applies the epilogue, so results
+// do not depend on timing.
+//
+// Warp roles: warp 0 lane 0 issues the TMA loads of a STAGES-deep ring,
+// warp 1 lane 0 issues the MMAs (tcgen05.commit releases a stage when the
+// MMAs that read it complete), all four warps run the epilogue.  Every wait
+// is bounded; on expiry the kernel records G2_ERR_TIMEOUT in *err, drains its
+// own copies, frees its tensor memory and returns.
+#include <cstdio>
+
+#include "g2_device.cuh"
+#include "g2_tc.h"
+#include "gpt2b200.h"
+
+namespace g2 {
+
+namespace {
+
+constexpr int kThreads = 128;
+typedef unsigned long long u64;
+
+__device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ u64 gtime() {
+    u64 t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(u64 *b, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(u64 *b, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(u64 *b, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{ .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for the phase of parity `parity`, at most 1 s.
+__device__ __forceinline__ bool mbar_wait(u64 *b, unsigned parity) {
+    if (mbar_try(b, parity)) return true;
+    const u64 limit = gtime() + 1000000000ull;
+    for (;;) {
+        if (mbar_try(b, parity)) return true;
+        if (gtime() > limit) return false;
+    }
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, u64 *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<u64>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor (version 1) with a 128-byte swizzle: layout
+// type 2 (16-byte granules, 8-row atoms) or, for MN-major 32-bit operands, type 1
+// (128-byte swizzle of 32-byte granules, 4-row atoms).
+__device__ __forceinline__ u64 sw128_desc(unsigned saddr, unsigned lbo, unsigned sbo, unsigned layout = 2) {
+    return (u64)((saddr >> 4) & 0x3FFFu) | ((u64)((lbo >> 4) & 0x3FFFu) << 16) | ((u64)((sbo >> 4) & 0x3FFFu) << 32) |
+           (1ull << 46) | ((u64)layout << 61);
+}
+
+// Instruction descriptor: D f32; A, B tf32 or f16; A MN-major, B K-major; N = BN, M = 128.
+template <int KIND, int BN>
+__host__ __device__ constexpr unsigned make_idesc() {
+    return (1u << 4) | ((KIND == TC_TF32X3 ? 2u : 0u) << 7) | ((KIND == TC_TF32X3 ? 2u : 0u) << 10) | (1u << 15) |
+           ((unsigned)(BN >> 3) << 17) | ((unsigned)(kTcTileF >> 4) << 24);
+}
+
+template <int KIND>
+__device__ __forceinline__ void mma(unsigned tmem_d, u64 adesc, u64 bdesc, unsigned idesc, unsigned accum) {
+    if (KIND == TC_TF32X3) {
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+            " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
+    } else {
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+            " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
+    }
+}
+__device__ __forceinline__ void mma_commit(u64 *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this warp's 32 tensor-memory lanes.
+__device__ __forceinline__ void tmem_ld32(unsigned taddr, float (&v)[32]) {
+    unsigned r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+struct TcArgs {
+    int N, R;
+    int kb_total, kb_per;   // K blocks in total and per split
+    float *part;            // [splits][R][N]
+    int *err;
+};
+
+template <int KIND>
+struct TcShape {
+    static constexpr int NPASS = KIND == TC_TF32X3 ? 2 : 1;   // hi and lo copies
+    static constexpr int ELEM = KIND == TC_TF32X3 ? 4 : 2;
+    static constexpr int BK = 128 / ELEM;                      // K per stage: one 128-byte row
+    static constexpr int BOX_F = 128 / ELEM;                   // features per weight box
+    static constexpr int NBOX = kTcTileF / BOX_F;              // weight boxes per stage and copy
+    static constexpr int A_BYTES = kTcTileF * BK * ELEM;       // 16 KB
+    static constexpr int KSTEP = KIND == TC_TF32X3 ? 8 : 16;   // K per MMA
+    static constexpr int NSTEP = BK / KSTEP;
+    // the weights (MN-major A): tf32 needs the 32-byte-granule swizzle (4-row atoms of 512 B)
+    static constexpr unsigned A_LAYOUT = KIND == TC_TF32X3 ? 1u : 2u;
+    static constexpr unsigned A_SBO = KIND == TC_TF32X3 ? 512u : 1024u;
+};
+
+template <int KIND, int BN>
+struct TcCfg {
+    using S = TcShape<KIND>;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int STAGE = S::NPASS * (S::A_BYTES + B_BYTES);
+    static constexpr int STAGES = (196608 / STAGE) < 8 ? (196608 / STAGE) : 8;
+    static constexpr size_t SMEM = (size_t)STAGES * STAGE + 1024 + 256;
+};
+
+template <int KIND, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap mw_hi, const __grid_constant__ CUtensorMap mw_lo,
+                   const __grid_constant__ CUtensorMap mx_hi, const __grid_constant__ CUtensorMap mx_lo, TcArgs a) {
+    using S = TcShape<KIND>;
+    using C = TcCfg<KIND, BN>;
+    constexpr int STAGES = C::STAGES;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char *base =
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    u64 *full = reinterpret_cast<u64 *>(base + (size_t)STAGES * C::STAGE);
+    u64 *empty = full + STAGES;
+    u64 *done = empty + STAGES;
+    unsigned *tslot = reinterpret_cast<unsigned *>(done + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int f0 = blockIdx.x * kTcTileF, r0 = blockIdx.y * BN;
+    const int kb0 = blockIdx.z * a.kb_per;
+    const int nkb = min(a.kb_per, a.kb_total - kb0);   // >= 1 (the planner guarantees it)
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                     "r"((unsigned)BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const unsigned tmem = *tslot;
+
+    if (threadIdx.x == 0) {
+        // ---- TMA producer ----
+        int issued = 0;
+        for (int i = 0; i < nkb; ++i) {
+            const int s = i % STAGES;
+            if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) {
+                atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
+                break;
+            }
+            unsigned char *st = base + (size_t)s * C::STAGE;
+            const int k = (kb0 + i) * S::BK;
+            mbar_expect_tx(&full[s], C::STAGE);
+#pragma unroll
+            for (int p = 0; p < S::NPASS; ++p)
+#pragma unroll
+                for (int b = 0; b < S::NBOX; ++b)
+                    tma_load_2d(st + p * S::A_BYTES + b * (S::BK * 128), p ? &mw_lo : &mw_hi, f0 + b * S::BOX_F, k,
+                                &full[s]);
+#pragma unroll
+            for (int p = 0; p < S::NPASS; ++p)
+                tma_load_2d(st + S::NPASS * S::A_BYTES + p * C::B_BYTES, p ? &mx_lo : &mx_hi, k, r0, &full[s]);
+            ++issued;
+        }
+        // every copy issued must land before the CTA may exit
+        for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
+    } else if (threadIdx.x == 32) {
+        // ---- MMA issuer ----
+        constexpr unsigned idesc = make_idesc<KIND, BN>();
+        for (int i = 0; i < nkb; ++i) {
+            const int s = i % STAGES;
+            if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+                atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const unsigned a_hi = smem_u32(base + (size_t)s * C::STAGE);
+            const unsigned b_hi = a_hi + S::NPASS * S::A_BYTES;
+#pragma unroll
+            for (int j = 0; j < S::NSTEP; ++j) {
+                const unsigned ao = j * S::KSTEP * 128, bo = j * S::KSTEP * S::ELEM;
+                const u64 ad = sw128_desc(a_hi + ao, S::BK * 128, S::A_SBO, S::A_LAYOUT);
+                const u64 bd = sw128_desc(b_hi + bo, 16, 1024);
+                const unsigned acc = (i | j) != 0;
+                mma<KIND>(tmem, ad, bd, idesc, acc);
+                if (KIND == TC_TF32X3) {
+                    const u64 ad_lo = sw128_desc(a_hi + S::A_BYTES + ao, S::BK * 128, S::A_SBO, S::A_LAYOUT);
+                    const u64 bd_lo = sw128_desc(b_hi + C::B_BYTES + bo, 16, 1024);
+                    mma<KIND>(tmem, ad, bd_lo, idesc, 1u);
+                    mma<KIND>(tmem, ad_lo, bd, idesc, 1u);
+                }
+            }
+            mma_commit(&empty[s]);
+        }
+        mma_commit(done);
+    }
+    __syncwarp();
+
+    // ---- epilogue: tensor memory -> partial tile ----
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0));   // warp-uniform: tcgen05.ld is .sync.aligned
+    if (!ok && lane == 0) atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+        const int f = f0 + warp * 32 + lane;
+        float *dst = a.part + (size_t)blockIdx.z * a.R * a.N;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            float v[32];
+            tmem_ld32(tmem + ((unsigned)(warp * 32) << 16) + (unsigned)c0, v);
+            if (f < a.N) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int r = r0 + c0 + j;
+                    if (r < a.R) dst[(size_t)r * a.N + f] = v[j];
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((unsigned)BN));
+}
+
+// x -> (hi, lo) tf32 pair, or x -> fp16.
+__global__ void tc_prep_kernel(int kind, const float4 *x, float4 *hi, float4 *lo, __half2 *h16, long long n4) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const float4 v = x[i];
+        if (kind == TC_TF32X3) {
+            float h[4], l[4];
+            const float in[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                unsigned t;
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(in[j]));
+                h[j] = __uint_as_float(t);
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(in[j] - h[j]));
+                l[j] = __uint_as_float(t);
+            }
+            hi[i] = make_float4(h[0], h[1], h[2], h[3]);
+            lo[i] = make_float4(l[0], l[1], l[2], l[3]);
+        } else {
+            h16[2 * i] = __floats2half2_rn(v.x, v.y);
+            h16[2 * i + 1] = __floats2half2_rn(v.z, v.w);
+        }
+    }
+}
+
+// Ordered sum of the splits + epilogue, 4 outputs per thread (N % 4 == 0).
+template <typename WT>
+__global__ void tc_reduce_kernel(const float *part, int splits, int R, int N, Epi<WT> e) {
+    const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    const long long total = (long long)R * N;
+    if (i >= total) return;
+    float4 acc = *reinterpret_cast<const float4 *>(part + i);
+    for (int s = 1; s < splits; ++s) {
+        const float4 p = *reinterpret_cast<const float4 *>(part + (size_t)s * total + i);
+        acc.x += p.x;
+        acc.y += p.y;
+        acc.z += p.z;
+        acc.w += p.w;
+    }
+    const int r = (int)(i / N), n = (int)(i % N);
+    e.apply(r, n, acc.x);
+    e.apply(r, n + 1, acc.y);
+    e.apply(r, n + 2, acc.z);
+    e.apply(r, n + 3, acc.w);
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Row-tile height (BN) and split count for R rows x N outputs over kb_total K blocks.
+struct TcPlan {
+    int bn, splits, kb_per;
+};
+TcPlan plan(int R, int N, int kb_total, int sms) {
+    TcPlan p;
+    p.bn = R <= 32 ? 32 : R <= 64 ? 64 : 128;
+    const int tiles = ((N + kTcTileF - 1) / kTcTileF) * ((R + p.bn - 1) / p.bn);
+    int s = (sms + tiles - 1) / tiles;                     // one wave of CTAs
+    s = s < 1 ? 1 : s;
+    const int max_s = kb_total / 2 > 0 ? kb_total / 2 : 1;   // at least two K blocks per split
+    s = s > max_s ? max_s : s;
+    s = s > 32 ? 32 : s;
+    p.kb_per = (kb_total + s - 1) / s;
+    p.splits = (kb_total + p.kb_per - 1) / p.kb_per;       // no empty split
+    return p;
+}
+
+template <int KIND, int BN>
+void launch_kernel(const TcWeights &w, const TcRowsOperand &x, int bn_idx, const TcArgs &a, int splits,
+                   cudaStream_t st) {
+    using C = TcCfg<KIND, BN>;
+    static unsigned long long attr_set = 0;   // devices on which this instantiation's smem limit was raised
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !(__atomic_load_n(&attr_set, __ATOMIC_ACQUIRE) >> dev & 1ull)) {
+        cudaFuncSetAttribute(tc_gemm_kernel<KIND, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+        __atomic_fetch_or(&attr_set, 1ull << dev, __ATOMIC_RELEASE);
+    } else if (dev >= 64) {
+        cudaFuncSetAttribute(tc_gemm_kernel<KIND, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    }
+    dim3 grid((a.N + kTcTileF - 1) / kTcTileF, (a.R + BN - 1) / BN, splits);
+    tc_gemm_kernel<KIND, BN><<<grid, kThreads, C::SMEM, st>>>(w.hi, KIND == TC_TF32X3 ? w.lo : w.hi, x.hi[bn_idx],
+                                                            KIND == TC_TF32X3 ? x.lo[bn_idx] : x.hi[bn_idx], a);
+}
+
+}  // namespace
+
+int tc_encode(CUtensorMap *map, CUtensorMapDataType dt, const void *base, unsigned long long inner,
+              unsigned long long outer, unsigned box_inner, unsigned box_outer, bool atom32) {
+    EncodeTiledFn fn = encoder();
+    if (!fn) return G2_ERR_CUDA;
+    const unsigned elem = dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT16 ? 2 : 4;
+    if (box_inner * elem != 128 || ((uintptr_t)base & 15) || (inner * elem) % 16) return G2_ERR_ARG;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {inner * elem};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? G2_OK : G2_ERR_CUDA;
+}
+
+int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N) {
+    const bool t = kind == TC_TF32X3;
+    const CUtensorMapDataType dt = t ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const unsigned bf = t ? 32 : 64, bk = t ? 32 : 64;
+    w->K = K;
+    w->N = N;
+    int rc = tc_encode(&w->hi, dt, hi, N, K, bf, bk, t);
+    if (!rc && t) rc = tc_encode(&w->lo, dt, lo, N, K, bf, bk, t);
+    if (!t) w->lo = w->hi;
+    return rc;
+}
+
+int tc_rows_operand(TcRowsOperand *x, int kind, const void *hi, const void *lo, int K, int R) {
+    const bool t = kind == TC_TF32X3;
+    const CUtensorMapDataType dt = t ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const unsigned bk = t ? 32 : 64;
+    x->K = K;
+    x->R = R;
+    const unsigned bn[3] = {32, 64, 128};
+    for (int i = 0; i < 3; ++i) {
+        int rc = tc_encode(&x->hi[i], dt, hi, K, R, bk, bn[i], false);
+        if (!rc && t) rc = tc_encode(&x->lo[i], dt, lo, K, R, bk, bn[i], false);
+        if (rc) return rc;
+        if (!t) x->lo[i] = x->hi[i];
+    }
+    return G2_OK;
+}
+
+void launch_tc_prep(int kind, const float *x, float *hi, float *lo, __half *h16, long long n, cudaStream_t st) {
+    const long long n4 = n / 4;
+    const int blocks = (int)((n4 + 255) / 256 < 4096 ? (n4 + 255) / 256 : 4096);
+    tc_prep_kernel<<<blocks > 0 ? blocks : 1, 256, 0, st>>>(kind, reinterpret_cast<const float4 *>(x),
+                                                          reinterpret_cast<float4 *>(hi), reinterpret_cast<float4 *>(lo),
+                                                          reinterpret_cast<__half2 *>(h16), n4);
+}
+
+size_t tc_partial_floats(int R_max, int N, int K, int kind, int sms) {
+    const int kb_total = K / (kind == TC_TF32X3 ? 32 : 64);
+    size_t m = 0;
+    for (int R = 1; R <= R_max; ++R) {
+        const TcPlan p = plan(R, N, kb_total, sms);
+        const size_t f = (size_t)p.splits * R * N;
+        m = f > m ? f : m;
+    }
+    return m;
+}
+
+template <typename WT>
+int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, float *partial, size_t partial_floats,
+                   int *err, const WT *bias, const float *resid, float *out, int epi, const KVLayout *kv, int layer,
+                   Rows rows, int sms, cudaStream_t st) {
+    const int bk = kind == TC_TF32X3 ? 32 : 64;
+    const int kb_total = w.K / bk;
+    TcPlan p = plan(R, w.N, kb_total, sms);
+    // fewer splits if the scratch is smaller than the plan needs (one split always fits R x N)
+    while (p.splits > 1 && (size_t)p.splits * R * w.N > partial_floats) {
+        p.kb_per = (kb_total + p.splits - 2) / (p.splits - 1);
+        p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
+    }
+    TcArgs a;
+    a.N = w.N;
+    a.R = R;
+    a.kb_total = kb_total;
+    a.kb_per = p.kb_per;
+    a.part = partial;
+    a.err = err;
+    const int bi = p.bn == 32 ? 0 : p.bn == 64 ? 1 : 2;
+    if (kind == TC_TF32X3) {
+        if (p.bn == 32) launch_kernel<TC_TF32X3, 32>(w, x, bi, a, p.splits, st);
+        else if (p.bn == 64) launch_kernel<TC_TF32X3, 64>(w, x, bi, a, p.splits, st);
+        else launch_kernel<TC_TF32X3, 128>(w, x, bi, a, p.splits, st);
+    } else {
+        if (p.bn == 32) launch_kernel<TC_F16, 32>(w, x, bi, a, p.splits, st);
+        else if (p.bn == 64) launch_kernel<TC_F16, 64>(w, x, bi, a, p.splits, st);
+        else launch_kernel<TC_F16, 128>(w, x, bi, a, p.splits, st);
+    }
+    Epi<WT> e;
+    e.bias = bias;
+    e.resid = resid;
+    e.out = out;
+    e.N = w.N;
+    e.epi = epi;
+    if (kv) e.kv = *kv;
+    e.layer = layer;
+    e.pos = rows.pos;
+    e.slot = rows.slot;
+    e.E = w.N / 3;
+    const long long n4 = (long long)R * w.N / 4;
+    tc_reduce_kernel<WT><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(partial, p.splits, R, w.N, e);
+    return 2;
+}
+
+template int launch_tc_gemm<float>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, int *,
+                                   const float *, const float *, float *, int, const KVLayout *, int, Rows, int,
+                                   cudaStream_t);
+template int launch_tc_gemm<__half>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, int *,
+                                    const __half *, const float *, float *, int, const KVLayout *, int, Rows, int,
+                                    cudaStream_t);
+
+}  // namespace g2

@@ -1,0 +1,62 @@
+// g2_tc.h -- tensor-core GEMM (tcgen05) for many-row passes: prefill and
+// batched decode.  See g2_tc.cu.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "g2_internal.h"
+
+namespace g2 {
+
+// Operand precision of a tensor-core GEMM.
+//  TC_TF32X3: fp32 operands split as x = hi + lo (hi = x rounded to tf32, lo =
+//             the rest rounded to tf32); three tf32 products hi*hi + hi*lo +
+//             lo*hi with fp32 accumulation, which keeps fp32-level accuracy.
+//  TC_F16:    fp16 operands (fp16 weights of the fp16 engine; activations
+//             rounded to fp16), fp32 accumulation.
+enum TcKind { TC_F16 = 0, TC_TF32X3 = 1 };
+
+constexpr int kTcTileF = 128;   // output features per CTA (the MMA's M)
+
+// Encode a 2-D row-major tensor [outer][inner] of `dt` elements with a
+// 128-byte-swizzled box of box_inner x box_outer elements (box_inner * elem
+// must be 128 bytes); atom32 selects the swizzle of 32-byte granules that
+// MN-major tf32 operands need.  Returns 0 or a G2_ERR_* code.
+int tc_encode(CUtensorMap *map, CUtensorMapDataType dt, const void *base, unsigned long long inner,
+              unsigned long long outer, unsigned box_inner, unsigned box_outer, bool atom32);
+
+// Weight operand of one projection W [K][N]: tensor maps of its hi and lo
+// copies (TC_TF32X3) or of the fp16 weights (TC_F16, lo unused).
+struct TcWeights {
+    CUtensorMap hi, lo;
+    int K, N;
+};
+int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N);
+
+// Activation operand X [R][K] (hi / lo fp32 copies, or fp16): maps for every
+// row-tile height the planner may pick.
+struct TcRowsOperand {
+    CUtensorMap hi[3], lo[3];   // box heights 32, 64, 128
+    int K, R;
+};
+int tc_rows_operand(TcRowsOperand *x, int kind, const void *hi, const void *lo, int K, int R);
+
+// Split an fp32 [n] array into tf32 hi / lo copies (TC_TF32X3) or round it to
+// fp16 (TC_F16: h16 written, hi / lo unused).  n % 4 == 0.
+void launch_tc_prep(int kind, const float *x, float *hi, float *lo, __half *h16, long long n, cudaStream_t st);
+
+// Floats of partial-sum scratch the planner uses for up to R_max rows of an
+// N x K projection on `sms` SMs.
+size_t tc_partial_floats(int R_max, int N, int K, int kind, int sms);
+
+// out[r][n] = epilogue(sum_k X[r][k] W[k][n]) for r < R: the tensor-core pass
+// into `partial`, then an ordered split-K reduction with the epilogue
+// (bias / GELU / residual / K,V append of g2_device.cuh).  `err` receives an
+// error code if a wait inside the kernel expires.  Returns the launch count.
+template <typename WT>
+int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, float *partial, size_t partial_floats,
+                   int *err, const WT *bias, const float *resid, float *out, int epi, const KVLayout *kv, int layer,
+                   Rows rows, int sms, cudaStream_t st);
+
+}  // namespace g2

@@ -60,6 +60,9 @@ def _load():
     L.g2k_matvec.argtypes = [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp, C.c_size_t, vp]
     L.g2k_matvec_noalloc.argtypes = [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]
     L.g2k_matmul.argtypes = [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp]
+    L.g2k_matmul_tc_workspace.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
+    L.g2k_matmul_tc_workspace.restype = C.c_size_t
+    L.g2k_matmul_tc.argtypes = [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp, C.c_size_t, vp]
     L.g2k_layernorm.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, vp]
     L.g2k_attention_workspace.argtypes = [C.c_int, C.c_int]
     L.g2k_attention_workspace.restype = C.c_size_t
@@ -195,6 +198,17 @@ def matvec_noalloc(x, W, y, N, K, bias=None, residual=None, gelu=False, ln_gamma
 def matmul(A, B, C_, M, N, K, bias=None, residual=None, gelu=False, stream=0):
     check(lib.g2k_matmul(_ptr(A), _ptr(B), _ptr(bias), _ptr(residual), _ptr(C_), M, N, K, int(gelu),
                          C.c_void_p(stream)))
+
+
+def matmul_tc_workspace(M: int, N: int, K: int, precision: int = G2_F32) -> int:
+    return lib.g2k_matmul_tc_workspace(M, N, K, precision)
+
+
+def matmul_tc(A, B, C_, M, N, K, bias=None, residual=None, gelu=False, precision=G2_F32, workspace=None,
+              workspace_bytes=0, stream=0):
+    """Tensor-core matmul (tcgen05): G2_F32 = 3xTF32 split operands, G2_F16 = fp16 operands."""
+    check(lib.g2k_matmul_tc(_ptr(A), _ptr(B), _ptr(bias), _ptr(residual), _ptr(C_), M, N, K, int(gelu), precision,
+                            _ptr(workspace), workspace_bytes, C.c_void_p(stream)))
 
 
 def layernorm(x, out, gamma, beta, n_embd, rows, stream=0):

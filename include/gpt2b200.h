@@ -152,6 +152,18 @@ int g2k_matvec_noalloc(const float *x, const float *W, const float *bias, const 
 int g2k_matmul(const float *A, const float *B, const float *bias, const float *residual, float *C,
                int M, int N, int K, int apply_gelu, void *stream);
 
+/* The same product on the tensor cores (tcgen05): the runtime matmul of
+ * prefill (main.c:593-684) for many rows.  precision G2_F32 splits every
+ * operand into tf32 hi + lo and sums three tf32 products (fp32-level
+ * accuracy); G2_F16 rounds both operands to fp16.  fp32 accumulation either
+ * way.  K % 64 == 0, N % 8 == 0, A / B / C 16-byte aligned.  `workspace`
+ * (256-byte aligned) holds g2k_matmul_tc_workspace() bytes; its first int
+ * becomes G2_ERR_TIMEOUT if a wait inside the kernel expired. */
+size_t g2k_matmul_tc_workspace(int M, int N, int K, int precision);
+int g2k_matmul_tc(const float *A, const float *B, const float *bias, const float *residual, float *C,
+                  int M, int N, int K, int apply_gelu, int precision, void *workspace,
+                  size_t workspace_bytes, void *stream);
+
 /* launch_layernorm (main.c:1620): rows of n_embd, eps 1e-5. */
 int g2k_layernorm(const float *x, float *out, const float *gamma, const float *beta, int n_embd,
                   int rows, void *stream);
