@@ -119,6 +119,16 @@ struct g2_engine {
     int mega_grid = 0;
     int mega_cw[4] = {0, 0, 0, 0};   // strip widths of qkv, proj, fc, fc2
     size_t mega_smem = 0;
+    // tensor-core GEMMs of the many-row passes (prefill, batched decode)
+    bool tc = false;
+    int tc_kind = TC_TF32X3;
+    float *tc_w = nullptr;                    // fp32 engine: tf32 hi / lo copies of the projections
+    float *tc_xhi = nullptr, *tc_xlo = nullptr;   // GEMM input rows: hi / lo (fp32) or fp16 (in tc_xhi)
+    float *tc_part = nullptr;                 // split-K partial sums
+    size_t tc_part_floats = 0;
+    int *tc_err = nullptr;
+    std::vector<TcWeights> tc_maps;           // [L][4]: qkv, proj, fc, fc2
+    TcRowsOperand tc_x_e{}, tc_x_f{};         // input rows with K = E and K = F
 
     template <typename WT>
     const WT *w(size_t off) const {
@@ -145,7 +155,7 @@ static void free_engine(g2_engine *e) {
     for (auto g : e->dec_graph)
         if (g) cudaGraphExecDestroy(g);
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
-    void *dev_ptrs[] = {e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f,
+    void *dev_ptrs[] = {e->tc_w, e->tc_xhi, e->tc_xlo, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f,
                         e->t_best, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
                         e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
@@ -555,6 +565,59 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
             TRY(dalloc(e, &e->d_trace, (size_t)e->mega_grid * kTraceSlots));
         }
     }
+    {
+        // Tensor-core GEMMs for prefill and batched decode: every K a multiple of
+        // 64 and every N of 8 (the projections of all GPT-2 sizes qualify).
+        const char *notc = getenv("G2_NO_TC");
+        e->tc = !(notc && notc[0] == '1') && E % 64 == 0 && F % 64 == 0 && E % 8 == 0;
+        if (e->tc) {
+            e->tc_kind = dtype == G2_F32 ? TC_TF32X3 : TC_F16;
+            const int Ks[4] = {E, E, E, F}, Ns[4] = {3 * E, E, F, E};
+            size_t per_layer = 0;
+            for (int q = 0; q < 4; ++q) per_layer += align_up((size_t)Ks[q] * Ns[q], 64);
+            if (e->tc_kind == TC_TF32X3) TRY(dalloc(e, &e->tc_w, 2 * per_layer * c.n_layer));
+            e->tc_maps.resize((size_t)c.n_layer * 4);
+            size_t o = 0;
+            for (int l = 0; l < c.n_layer; ++l) {
+                const LayerOff &lo = e->L[l];
+                const size_t wo[4] = {lo.qkv_w, lo.proj_w, lo.fc_w, lo.fc2_w};
+                for (int q = 0; q < 4; ++q) {
+                    const size_t n = (size_t)Ks[q] * Ns[q];
+                    int rc;
+                    if (e->tc_kind == TC_TF32X3) {
+                        float *hi = e->tc_w + o, *lo_ = e->tc_w + per_layer * c.n_layer + o;
+                        launch_tc_prep(TC_TF32X3, e->w<float>(wo[q]), hi, lo_, nullptr, (long long)n, e->st);
+                        rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_TF32X3, hi, lo_, Ks[q], Ns[q]);
+                    } else {
+                        rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_F16, e->w<__half>(wo[q]), nullptr, Ks[q], Ns[q]);
+                    }
+                    if (rc) {
+                        free_engine(e);
+                        return set_err(rc, "tensor map of layer %d projection %d", l, q);
+                    }
+                    o += align_up(n, 64);
+                }
+            }
+            const size_t xr = (size_t)R * (E > F ? E : F);
+            TRY(dalloc(e, &e->tc_xhi, xr));
+            if (e->tc_kind == TC_TF32X3) TRY(dalloc(e, &e->tc_xlo, xr));
+            int rc = tc_rows_operand(&e->tc_x_e, e->tc_kind, e->tc_xhi, e->tc_xlo, E, R);
+            if (!rc) rc = tc_rows_operand(&e->tc_x_f, e->tc_kind, e->tc_xhi, e->tc_xlo, F, R);
+            if (rc) {
+                free_engine(e);
+                return set_err(rc, "tensor maps of the GEMM input rows");
+            }
+            for (int q = 0; q < 4; ++q)
+                e->tc_part_floats = std::max(e->tc_part_floats, tc_partial_floats(R, Ns[q], Ks[q], e->tc_kind, e->sms));
+            TRY(dalloc(e, &e->tc_part, e->tc_part_floats));
+            TRY(dalloc(e, &e->tc_err, 1));
+            cudaError_t r = cudaStreamSynchronize(e->st);
+            if (r != cudaSuccess) {
+                free_engine(e);
+                return set_err(G2_ERR_CUDA, "tensor-core weight split: %s", cudaGetErrorString(r));
+            }
+        }
+    }
 #undef TRY
     *out = e;
     return G2_OK;
@@ -607,6 +670,27 @@ static int stage_rows(g2_engine *e, int n, const int *tok, const int *pos, const
 // All layers over `nrows` rows described by the device row arrays (prefill of
 // one slot, or one decode token for each of several slots).  Leaves the
 // residual stream in e->h.
+// One projection of a many-row pass: out[r] = epilogue(X[r] W) on the tensor
+// cores (X split / rounded into the GEMM input rows first), or the SIMT GEMM.
+template <typename WT>
+static void rows_gemm(g2_engine *e, int l, int q, const float *X, int nrows, const WT *W, const WT *bias,
+                      const float *resid, float *out, int N, int K, int epi, const KVLayout *kv, Rows rows) {
+    cudaStream_t st = e->st;
+    if (e->tc) {
+        launch_tc_prep(e->tc_kind, X, e->tc_xhi, e->tc_xlo, reinterpret_cast<__half *>(e->tc_xhi),
+                       (long long)nrows * K, st);
+        e->launches += 1 + launch_tc_gemm<WT>(e->tc_kind, e->tc_maps[(size_t)l * 4 + q], K == e->c.n_embd ? e->tc_x_e : e->tc_x_f,
+                                              nrows, e->tc_part, e->tc_part_floats, e->tc_err, bias, resid, out, epi, kv,
+                                              l, rows, e->sms, st);
+    } else {
+        launch_gemm_rows<WT>(X, W, bias, resid, out, nrows, N, K, epi, kv, l, rows, st);
+        e->launches += 1;
+    }
+}
+
+// All layers over `nrows` rows described by the device row arrays (prefill of
+// one slot, or one decode token for each of several slots).  Leaves the
+// residual stream in e->h.
 template <typename WT>
 static int forward_rows(g2_engine *e, int nrows, int max_pos) {
     const ModelConfig &c = e->c;
@@ -617,19 +701,19 @@ static int forward_rows(g2_engine *e, int nrows, int max_pos) {
     for (int l = 0; l < c.n_layer; ++l) {
         const LayerOff &o = e->L[l];
         launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln1_g), e->w<WT>(o.ln1_b), E, nrows, st);
-        launch_gemm_rows<WT>(e->xln, e->w<WT>(o.qkv_w), e->w<WT>(o.qkv_b), nullptr, e->qkv, nrows, 3 * E, E,
-                             EPI_BIAS | EPI_KV, &e->kv, l, rows, st);
+        rows_gemm<WT>(e, l, 0, e->xln, nrows, e->w<WT>(o.qkv_w), e->w<WT>(o.qkv_b), nullptr, e->qkv, 3 * E, E,
+                      EPI_BIAS | EPI_KV, &e->kv, rows);
         launch_attention<WT>(e->qkv, 3 * E, e->kv, l, rows, nrows, e->attn, E, e->attn_partial, e->attn_ctr, max_pos,
                              st);
-        launch_gemm_rows<WT>(e->attn, e->w<WT>(o.proj_w), e->w<WT>(o.proj_b), e->h, e->h, nrows, E, E,
-                             EPI_BIAS | EPI_RESID, nullptr, l, rows, st);
+        rows_gemm<WT>(e, l, 1, e->attn, nrows, e->w<WT>(o.proj_w), e->w<WT>(o.proj_b), e->h, e->h, E, E,
+                      EPI_BIAS | EPI_RESID, nullptr, rows);
         launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln2_g), e->w<WT>(o.ln2_b), E, nrows, st);
-        launch_gemm_rows<WT>(e->xln, e->w<WT>(o.fc_w), e->w<WT>(o.fc_b), nullptr, e->ffn, nrows, F, E,
-                             EPI_BIAS | EPI_GELU, nullptr, l, rows, st);
-        launch_gemm_rows<WT>(e->ffn, e->w<WT>(o.fc2_w), e->w<WT>(o.fc2_b), e->h, e->h, nrows, E, F,
-                             EPI_BIAS | EPI_RESID, nullptr, l, rows, st);
+        rows_gemm<WT>(e, l, 2, e->xln, nrows, e->w<WT>(o.fc_w), e->w<WT>(o.fc_b), nullptr, e->ffn, F, E,
+                      EPI_BIAS | EPI_GELU, nullptr, rows);
+        rows_gemm<WT>(e, l, 3, e->ffn, nrows, e->w<WT>(o.fc2_w), e->w<WT>(o.fc2_b), e->h, e->h, E, F,
+                      EPI_BIAS | EPI_RESID, nullptr, rows);
     }
-    e->launches += 1 + 7LL * c.n_layer;
+    e->launches += 1 + 3LL * c.n_layer;
     CKL();
     return G2_OK;
 }
@@ -774,8 +858,15 @@ static void dump_trace(g2_engine *e, int n_steps) {
 
 // After a synchronisation: report an expired device-side wait of the decode kernel.
 static int check_mega_err(g2_engine *e) {
-    if (!e->mega) return G2_OK;
     int code = 0;
+    if (e->tc) {
+        CK(cudaMemcpy(&code, e->tc_err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (code) {
+            CK(cudaMemset(e->tc_err, 0, sizeof(int)));
+            return set_err(G2_ERR_TIMEOUT, "tensor-core GEMM: a bounded device-side wait expired");
+        }
+    }
+    if (!e->mega) return G2_OK;
     CK(cudaMemcpy(&code, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code) {
         CK(cudaMemset(e->d_err, 0, sizeof(int)));
