@@ -127,6 +127,10 @@ struct g2_engine {
     float *tc_part = nullptr;                 // split-K partial sums
     size_t tc_part_floats = 0;
     int *tc_err = nullptr;
+    // device sampler
+    float *sample_work = nullptr;   // [padded_vocab]
+    int *sample_ctx = nullptr;      // [n_ctx] context ids
+    int *h_ctx = nullptr;           // pinned staging of the context ids
     std::vector<TcWeights> tc_maps;           // [L][4]: qkv, proj, fc, fc2
     TcRowsOperand tc_x_e{}, tc_x_f{};         // input rows with K = E and K = F
 
@@ -155,7 +159,7 @@ static void free_engine(g2_engine *e) {
     for (auto g : e->dec_graph)
         if (g) cudaGraphExecDestroy(g);
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
-    void *dev_ptrs[] = {e->tc_w, e->tc_xhi, e->tc_xlo, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f,
+    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_xhi, e->tc_xlo, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f,
                         e->t_best, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
                         e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
@@ -165,6 +169,7 @@ static void free_engine(g2_engine *e) {
     if (e->h_rows) cudaFreeHost(e->h_rows);
     if (e->h_state) cudaFreeHost(e->h_state);
     if (e->h_small) cudaFreeHost(e->h_small);
+    if (e->h_ctx) cudaFreeHost(e->h_ctx);
     if (e->staged) cudaEventDestroy(e->staged);
     for (auto &ev : e->ev)
         if (ev) cudaEventDestroy(ev);
@@ -509,10 +514,13 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
     TRY(dalloc(e, &e->batch_step, 1));
     TRY(dalloc(e, &e->out_tokens, (size_t)max_batch * S));
     TRY(dalloc(e, &e->state, 1));
+    TRY(dalloc(e, &e->sample_work, (size_t)Vp));
+    TRY(dalloc(e, &e->sample_ctx, (size_t)S));
     {
         cudaError_t r = cudaMallocHost(&e->h_rows, sizeof(int) * 3 * (size_t)R);
         if (r == cudaSuccess) r = cudaMallocHost(&e->h_state, sizeof(StepState) * 64);
         if (r == cudaSuccess) r = cudaMallocHost(&e->h_small, sizeof(int) * 4 * (size_t)max_batch + 64);
+        if (r == cudaSuccess) r = cudaMallocHost(&e->h_ctx, sizeof(int) * (size_t)S);
         if (r == cudaSuccess) r = cudaEventCreateWithFlags(&e->staged, cudaEventDisableTiming);
         for (auto &ev : e->ev)
             if (r == cudaSuccess) r = cudaEventCreate(&ev);
@@ -1008,6 +1016,31 @@ extern "C" int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, flo
     if ((rc = check_mega_err(e))) return rc;
     *token = e->h_small[0];
     if (value) memcpy(value, &e->h_small[1], 4);
+    return G2_OK;
+}
+
+extern "C" int g2_sample_device(g2_engine *e, int slot, const int *context_ids, int n_context, int forbid_eos,
+                                float temperature, int top_k, float rep_penalty, double u01, int *out_token) {
+    if (!e || !out_token || n_context < 0 || (n_context > 0 && !context_ids))
+        return set_err(G2_ERR_ARG, "g2_sample_device: bad argument");
+    int rc;
+    if ((rc = check_slot(e, slot))) return rc;
+    if (n_context > e->c.n_ctx) return set_err(G2_ERR_RANGE, "g2_sample_device: %d context ids > n_ctx %d", n_context, e->c.n_ctx);
+    if (!(u01 >= 0.0 && u01 < 1.0)) return set_err(G2_ERR_ARG, "g2_sample_device: u01 must be in [0, 1)");
+    if (e->filled[slot] == 0) return set_err(G2_ERR_STATE, "g2_sample_device: slot %d has no logits yet", slot);
+    CK(cudaSetDevice(e->device));
+    if (n_context > 0) {
+        memcpy(e->h_ctx, context_ids, sizeof(int) * n_context);
+        CK(cudaMemcpyAsync(e->sample_ctx, e->h_ctx, sizeof(int) * n_context, cudaMemcpyHostToDevice, e->st));
+    }
+    launch_sample(e->logits + (size_t)slot * e->c.padded_vocab, e->sample_work, e->c.vocab_size, e->sample_ctx,
+                  n_context, forbid_eos, temperature, top_k, rep_penalty, u01, e->argmax_out, e->st);
+    e->launches += 1;
+    CKL();
+    CK(cudaMemcpyAsync(e->h_small, e->argmax_out, sizeof(int), cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    if ((rc = check_mega_err(e))) return rc;
+    *out_token = e->h_small[0];
     return G2_OK;
 }
 

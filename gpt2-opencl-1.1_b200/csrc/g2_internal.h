@@ -46,6 +46,10 @@ struct Rows {
 enum Epilogue { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_RESID = 4, EPI_KV = 8 };
 
 // ---- launchers (g2_kernels.cu); all asynchronous on `st` ------------------------
+// sample_next_token on the device (g2_sample_dev.cu): token -> out[0].
+void launch_sample(const float *logits, float *work, int V, const int *ctx, int n_ctx, int forbid_eos,
+                   float temperature, int top_k, float rep_penalty, double u, int *out, cudaStream_t st);
+
 template <typename WT>
 void launch_embed(const WT *wte, const WT *wpe, Rows rows, float *h, int E, int V, int n_pos, int nrows,
                   cudaStream_t st);

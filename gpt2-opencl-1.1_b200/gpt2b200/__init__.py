@@ -49,6 +49,7 @@ def _load():
     L.g2_logits.argtypes = [vp, C.c_int, fp, C.c_int]
     L.g2_argmax.argtypes = [vp, C.c_int, C.c_int, ip, fp]
     L.g2_sample.argtypes = [fp, C.c_int, ip, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, ip]
+    L.g2_sample_device.argtypes = [vp, C.c_int, ip, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, C.c_double, ip]
     L.g2_generate.argtypes = [vp, C.c_int, ip, C.c_int, C.c_int, C.c_int, ip]
     L.g2_generate_batch.argtypes = [vp, C.c_int, ip, ip, ip, C.c_int, ip]
     L.g2_synchronize.argtypes = [vp]
@@ -133,6 +134,15 @@ class Engine:
         t, v = C.c_int(), C.c_float()
         check(lib.g2_argmax(self.h, slot, int(forbid_eos), C.byref(t), C.byref(v)))
         return t.value, v.value
+
+    def sample_device(self, context, forbid_eos: bool = False, temperature: float = 0.0, top_k: int = 0,
+                      rep_penalty: float = 1.0, u: float = 0.0, slot: int = 0) -> int:
+        """sample_next_token on the device with the uniform draw `u` in [0, 1)."""
+        a, p = _i32(context)
+        t = C.c_int()
+        check(lib.g2_sample_device(self.h, slot, p, len(a), int(forbid_eos), temperature, top_k, rep_penalty, u,
+                                   C.byref(t)))
+        return t.value
 
     def generate(self, prompt, n_new: int, min_new: int = None, slot: int = 0) -> np.ndarray:
         a, p = _i32(prompt)

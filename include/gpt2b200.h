@@ -94,6 +94,17 @@ int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, float *value);
 int g2_sample(const float *logits, int vocab_size, const int *context_ids, int n_context,
               int forbid_eos, float temperature, int top_k, float rep_penalty, int *out_token);
 
+/* sample_next_token (main.c:1872-1939) on the device, on the logits of `slot`
+ * (left unchanged): the same EOS mask, repetition penalty over the unique ids
+ * context_ids[0..n_context) (host array, n_context <= n_ctx), greedy first
+ * maximum for temperature <= 0, else 1/temperature scaling, the top-k
+ * threshold (k-th largest; k clamped to G2_MAX_TOPK) and the inverse-CDF draw
+ * at u01 * sum.  The caller supplies the uniform draw u01 in [0, 1) -- the
+ * reference uses rand() / (RAND_MAX + 1.0).  Only the token comes back to the
+ * host (4 bytes instead of the vocab_size logits). */
+int g2_sample_device(g2_engine *e, int slot, const int *context_ids, int n_context, int forbid_eos,
+                     float temperature, int top_k, float rep_penalty, double u01, int *out_token);
+
 /* Greedy generation on the device (main.c:2106-2150 with --greedy,
  * --rep-penalty 1): prefill `prompt`, then argmax/decode until n_new tokens
  * (the prefill's token included) are in out_tokens.  EOS is excluded from the
