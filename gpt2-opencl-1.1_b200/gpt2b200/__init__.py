@@ -50,6 +50,12 @@ def _load():
     L.g2_argmax.argtypes = [vp, C.c_int, C.c_int, ip, fp]
     L.g2_sample.argtypes = [fp, C.c_int, ip, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, ip]
     L.g2_sample_device.argtypes = [vp, C.c_int, ip, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, C.c_double, ip]
+    L.g2_tokenizer_load.argtypes = [C.c_char_p, C.POINTER(vp)]
+    L.g2_tokenizer_free.argtypes = [vp]
+    L.g2_tokenizer_free.restype = None
+    L.g2_tokenizer_vocab_size.argtypes = [vp]
+    L.g2_tok_encode.argtypes = [vp, C.c_char_p, ip, C.c_int]
+    L.g2_tok_decode.argtypes = [vp, ip, C.c_int, C.c_char_p, C.c_int]
     L.g2_generate.argtypes = [vp, C.c_int, ip, C.c_int, C.c_int, C.c_int, ip]
     L.g2_generate_batch.argtypes = [vp, C.c_int, ip, ip, ip, C.c_int, ip]
     L.g2_synchronize.argtypes = [vp]
@@ -180,6 +186,45 @@ def sample(logits, ctx, forbid_eos=False, temperature=0.0, top_k=40, rep_penalty
     check(lib.g2_sample(lg.ctypes.data_as(C.POINTER(C.c_float)), len(lg) if vocab_size is None else vocab_size,
                         cp, len(c), int(forbid_eos), temperature, top_k, rep_penalty, C.byref(out)))
     return out.value
+
+
+class Tokenizer:
+    """GPT-2 byte-level BPE (g2_tokenizer_*; tokenizer.c semantics) from vocab.json + merges.txt."""
+
+    def __init__(self, directory: str):
+        self.h = C.c_void_p()
+        rc = lib.g2_tokenizer_load(directory.encode(), C.byref(self.h))
+        if rc < 0:
+            raise G2Error(rc, f"cannot load vocab.json / merges.txt from {directory}")
+
+    def close(self):
+        if self.h:
+            lib.g2_tokenizer_free(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def vocab_size(self) -> int:
+        return lib.g2_tokenizer_vocab_size(self.h)
+
+    def encode(self, text, max_ids: int = None) -> list:
+        b = text.encode() if isinstance(text, str) else bytes(text)
+        cap = max_ids if max_ids is not None else len(b) + 1
+        out = (C.c_int * max(cap, 1))()
+        n = check(lib.g2_tok_encode(self.h, b, out, max(cap, 1)))
+        return list(out[:n])
+
+    def decode(self, ids, max_bytes: int = None) -> bytes:
+        a, p = _i32(ids)
+        cap = max_bytes if max_bytes is not None else 16 * len(a) + 1
+        buf = C.create_string_buffer(max(cap, 1))
+        n = check(lib.g2_tok_decode(self.h, p, len(a), buf, max(cap, 1)))
+        return buf.raw[:n]
 
 
 # ---- single kernels on device pointers (ints = device addresses) ---------------------

@@ -105,6 +105,18 @@ int g2_sample(const float *logits, int vocab_size, const int *context_ids, int n
 int g2_sample_device(g2_engine *e, int slot, const int *context_ids, int n_context, int forbid_eos,
                      float temperature, int top_k, float rep_penalty, double u01, int *out_token);
 
+/* ---- tokenizer (tokenizer.c:442-579): GPT-2 byte-level BPE ----
+ * vocab.json + merges.txt from `dir`; the same pre-tokenization, merges and
+ * byte mapping as the reference, so the same ids and bytes. */
+typedef struct g2_tokenizer g2_tokenizer;
+int g2_tokenizer_load(const char *dir, g2_tokenizer **out);
+void g2_tokenizer_free(g2_tokenizer *t);
+int g2_tokenizer_vocab_size(const g2_tokenizer *t);
+/* UTF-8 text -> at most max_ids ids; returns the count (or a negative code). */
+int g2_tok_encode(const g2_tokenizer *t, const char *text, int *ids, int max_ids);
+/* ids -> bytes, NUL-terminated within max_bytes; returns the bytes written. */
+int g2_tok_decode(const g2_tokenizer *t, const int *ids, int n, char *out, int max_bytes);
+
 /* Greedy generation on the device (main.c:2106-2150 with --greedy,
  * --rep-penalty 1): prefill `prompt`, then argmax/decode until n_new tokens
  * (the prefill's token included) are in out_tokens.  EOS is excluded from the

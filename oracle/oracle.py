@@ -274,3 +274,39 @@ def run_ref_kernel(name: str, gws, lws, args, program_kind: int = 0) -> None:
     rc = L.refcl_run_kernel(name.encode(), program_kind, len(gws), g, l, raw, len(args))
     if rc:
         raise RuntimeError(f"refcl_run_kernel({name}) = {rc}")
+
+
+class RefTokenizer:
+    """The reference's own tokenizer.c (in libref_main.so): gpt2_tokenizer_load /
+    gpt2_encode / gpt2_decode."""
+
+    def __init__(self, directory: str):
+        L = ref_lib()
+        L.gpt2_tokenizer_load.restype = C.c_void_p
+        L.gpt2_tokenizer_load.argtypes = [C.c_char_p]
+        L.gpt2_tokenizer_free.argtypes = [C.c_void_p]
+        L.gpt2_encode.argtypes = [C.c_void_p, C.c_char_p, _ip, C.c_int]
+        L.gpt2_decode.argtypes = [C.c_void_p, _ip, C.c_int, C.c_char_p, C.c_int]
+        L.gpt2_tokenizer_vocab_size.argtypes = [C.c_void_p]
+        self.L = L
+        self.h = L.gpt2_tokenizer_load(directory.encode())
+        if not self.h:
+            raise RuntimeError(f"reference tokenizer failed to load {directory}")
+
+    def close(self):
+        if self.h:
+            self.L.gpt2_tokenizer_free(self.h)
+            self.h = None
+
+    def encode(self, data: bytes, max_ids: int = None) -> list:
+        cap = max_ids if max_ids is not None else len(data) + 1
+        out = (C.c_int * max(cap, 1))()
+        n = self.L.gpt2_encode(self.h, data, out, max(cap, 1))
+        return list(out[:n])
+
+    def decode(self, ids, max_bytes: int = None) -> bytes:
+        a = np.ascontiguousarray(ids, dtype=np.int32)
+        cap = max_bytes if max_bytes is not None else 16 * len(a) + 1
+        buf = C.create_string_buffer(max(cap, 1))
+        n = self.L.gpt2_decode(self.h, iptr(a), len(a), buf, max(cap, 1))
+        return buf.raw[:n]
