@@ -162,6 +162,105 @@ def cpu_sample(cfg, seconds=12.0, force_reference=False):
                       f"workload, batch 1 (per-sequence rate)", "prefill_s": round(t_pre, 3)}
 
 
+def run_c2(args):
+    """C2: per-kernel microbench on the device pointers entry points (g2k_*), weights rotating
+    over a pool larger than L2 so HBM is what is measured; one JSON line with every case."""
+    import torch
+    import gpt2b200 as g2
+    peak_gbs, _ = peaks()
+    try:
+        bf16 = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
+    except Exception:
+        bf16 = 1590.0
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    dev = torch.device("cuda")
+    L2 = 126 * 2**20
+    cases = []
+
+    stream = torch.cuda.Stream()
+
+    def timed(fn, reps):
+        """Device time per call: `reps` calls captured in a CUDA graph (no host launch
+        overhead in the timed region), replayed between events."""
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                fn(i, stream.cuda_stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(reps):
+                fn(i, stream.cuda_stream)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record()
+            g.replay()
+            b.record()
+        torch.cuda.synchronize()
+        del g
+        return a.elapsed_time(b) * 1000.0 / reps   # us per call
+
+    shapes = [("qkv", 2304, 768), ("attn_proj", 768, 768), ("ffn1", 3072, 768), ("ffn2", 768, 3072),
+              ("lm_head", 50260, 768)]
+    for name, N, K in shapes:
+        wbytes = 4 * N * K
+        pool = max(2, -(-3 * L2 // wbytes))
+        W = torch.randn(pool, K, N, generator=gen, device=dev) * 0.02
+        x = torch.randn(K, generator=gen, device=dev)
+        y = torch.zeros(N, device=dev)
+        wsb = g2.matvec_workspace(N, K)
+        ws = torch.zeros(wsb // 4 + 64, device=dev)
+        us = timed(lambda i, st: g2.matvec(x, W[i % pool], y, N, K, workspace=ws, workspace_bytes=wsb, stream=st),
+                   4 * pool)
+        gbs = (wbytes + 4 * (N + K)) / us / 1e3
+        cases.append({"kernel": "gemv_kernel (g2k_matvec)", "case": f"{name} {K}->{N}, B=1 fp32", "us": round(us, 2),
+                      "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peak_gbs, 3)})
+        del W
+    for M in (64, 256, 1024):
+        for name, N, K in shapes[:4]:
+            for prec, pname in ((g2.G2_F32, "3xTF32"), (g2.G2_F16, "fp16")):
+                pool = max(2, -(-3 * L2 // (4 * N * K)))
+                W = torch.randn(pool, K, N, generator=gen, device=dev) * 0.02
+                A = torch.randn(M, K, generator=gen, device=dev)
+                Cm = torch.zeros(M, N, device=dev)
+                wsb = g2.matmul_tc_workspace(M, N, K, prec)
+                ws = torch.zeros(wsb // 4 + 64, device=dev)
+                us = timed(lambda i, st: g2.matmul_tc(A, W[i % pool], Cm, M, N, K, precision=prec, workspace=ws,
+                                                      workspace_bytes=wsb, stream=st), 2 * pool)
+                tf = 2.0 * M * N * K / us / 1e6
+                cases.append({"kernel": "tc_gemm_kernel (g2k_matmul_tc, incl. operand split + reduce)",
+                              "case": f"{name} M={M} {K}->{N} {pname}", "us": round(us, 2), "TFLOP/s": round(tf, 2),
+                              "frac_bf16": round(tf / bf16, 4)})
+                del W
+            if M == 64:
+                W = torch.randn(K, N, generator=gen, device=dev) * 0.02
+                A = torch.randn(M, K, generator=gen, device=dev)
+                Cm = torch.zeros(M, N, device=dev)
+                us = timed(lambda i, st: g2.matmul(A, W, Cm, M, N, K, stream=st), 10)
+                cases.append({"kernel": "gemm_kernel (g2k_matmul, SIMT fp32)", "case": f"{name} M={M} {K}->{N}",
+                              "us": round(us, 2), "TFLOP/s": round(2.0 * M * N * K / us / 1e6, 2)})
+    H, S = 12, 1024
+    for T in (64, 128, 256, 512, 1024):
+        pool = 8
+        Kc = torch.randn(pool, H, S, 64, generator=gen, device=dev)
+        Vc = torch.randn(pool, H, S, 64, generator=gen, device=dev)
+        q = torch.randn(H * 64, generator=gen, device=dev)
+        out = torch.zeros(H * 64, device=dev)
+        wsb = g2.attention_workspace(H, S)
+        ws = torch.zeros(wsb // 4 + 64, device=dev)
+        us = timed(lambda i, st: g2.attention(q, Kc[i % pool], Vc[i % pool], out, H, S, T, ws, wsb, stream=st),
+                   4 * pool)
+        by = 2 * H * T * 64 * 4
+        cases.append({"kernel": "attn_kernel (g2k_attention)", "case": f"12 heads x 64, T_kv={T}", "us": round(us, 2),
+                      "GB/s": round(by / us / 1e3, 1), "frac_hbm": round(by / us / 1e3 / peak_gbs, 3)})
+        del Kc, Vc
+    line = {"metric": "C2 kernel microbench (device us per call from CUDA-graph replay; GB/s or TFLOP/s)", "value": None, "unit": "per case",
+            "n_gpus": 1, "higher_is_better": True, "config": {"workload": "c2", "pool": "weights rotate over > 3x L2"},
+            "peaks": {"hbm_gbs": peak_gbs, "bf16_tflops": bf16}, "cases": cases}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, cfg):
     ws, rank, _ = dist_env()
     if rank != 0:
@@ -336,12 +435,18 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["c2"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-steps", type=int, default=0,
                     help="override the workload's decode steps (short runs for profiler captures; not a bench number)")
     args = ap.parse_args()
+    if args.config == "c2":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "c2 is a per-kernel device microbench"}))
+        else:
+            run_c2(args)
+        return
     cfg = dict(CONFIGS[args.config])
     if args.decode_steps > 0:
         cfg["steps"] = args.decode_steps

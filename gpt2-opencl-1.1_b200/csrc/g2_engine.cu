@@ -1329,8 +1329,7 @@ extern "C" int g2k_attention(const float *q, const float *K, const float *V, flo
     int *rowinfo = reinterpret_cast<int *>(workspace);   // [0] = pos, [1] = slot, [2] = token
     unsigned *ctr = reinterpret_cast<unsigned *>((char *)workspace + 256);
     float *partial = reinterpret_cast<float *>((char *)workspace + 256 + align_up(attn_counter_count(1, n_head) * 4, 256));
-    const int info[4] = {T_kv - 1, 0, 0, 0};
-    CK(cudaMemcpyAsync(rowinfo, info, sizeof info, cudaMemcpyHostToDevice, st));
+    launch_set_ints(rowinfo, T_kv - 1, 0, 0, 0, st);   // pos, slot, token (no host copy: graph-capturable)
     KVLayout kv;
     kv.k = const_cast<float *>(K);
     kv.v = const_cast<float *>(V);

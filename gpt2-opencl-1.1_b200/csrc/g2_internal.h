@@ -46,6 +46,8 @@ struct Rows {
 enum Epilogue { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_RESID = 4, EPI_KV = 8 };
 
 // ---- launchers (g2_kernels.cu); all asynchronous on `st` ------------------------
+// p[0..4) = a, b, c, d on the device (g2_kernels.cu).
+void launch_set_ints(int *p, int a, int b, int c, int d, cudaStream_t st);
 // sample_next_token on the device (g2_sample_dev.cu): token -> out[0].
 void launch_sample(const float *logits, float *work, int V, const int *ctx, int n_ctx, int forbid_eos,
                    float temperature, int top_k, float rep_penalty, double u, int *out, cudaStream_t st);

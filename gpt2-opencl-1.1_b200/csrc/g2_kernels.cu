@@ -680,6 +680,16 @@ void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int 
 
 int lm_head_blocks() { return kLmBlocks; }
 
+// Four ints written on the device (row descriptors of single-query calls), so
+// that no host-memory copy is needed and the call can be captured in a graph.
+__global__ void set_ints_kernel(int *p, int a, int b, int c, int d) {
+    p[0] = a;
+    p[1] = b;
+    p[2] = c;
+    p[3] = d;
+}
+void launch_set_ints(int *p, int a, int b, int c, int d, cudaStream_t st) { set_ints_kernel<<<1, 1, 0, st>>>(p, a, b, c, d); }
+
 template <typename WT>
 void launch_lm_head(const float *x, const WT *wte, const WT *lnf_g, const WT *lnf_b, float *logits, int E, int V,
                     int Vp, int forbid_eos, float *partial, unsigned *counter, int *result, StepState *state,
