@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <map>
 #include <vector>
 
 #include "g2_internal.h"
@@ -98,6 +99,15 @@ struct g2_engine {
     std::vector<cudaGraphExec_t> dec_graph;
     int dec_graph_kernels = 0;
     cudaGraphExec_t batch_graph = nullptr;
+    // prefill graphs by prompt length: a length is run eagerly on first use and
+    // captured on the second (G2_NO_PREFILL_GRAPH=1 keeps it eager)
+    struct PrefillGraph {
+        cudaGraphExec_t exec = nullptr;
+        long long kernels = 0;
+        int uses = 0;
+    };
+    std::map<int, PrefillGraph> prefill_graphs;
+    bool prefill_graph_on = true;
     int batch_graph_n = 0, batch_graph_kernels = 0;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     float last_prefill_ms = 0, last_decode_ms = 0;
@@ -159,6 +169,8 @@ static void free_engine(g2_engine *e) {
     for (auto g : e->dec_graph)
         if (g) cudaGraphExecDestroy(g);
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
+    for (auto &kv : e->prefill_graphs)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_xhi, e->tc_xlo, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f,
                         e->t_best, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
@@ -576,6 +588,8 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
     {
         // Tensor-core GEMMs for prefill and batched decode: every K a multiple of
         // 64 and every N of 8 (the projections of all GPT-2 sizes qualify).
+        const char *npg = getenv("G2_NO_PREFILL_GRAPH");
+        e->prefill_graph_on = !(npg && npg[0] == '1');
         const char *notc = getenv("G2_NO_TC");
         e->tc = !(notc && notc[0] == '1') && E % 64 == 0 && F % 64 == 0 && E % 8 == 0;
         if (e->tc) {
@@ -903,8 +917,34 @@ static int prefill_impl(g2_engine *e, int slot, const int *ids, int n) {
     std::vector<int> pos(n), sl(n, slot);
     for (int i = 0; i < n; ++i) pos[i] = i;
     if ((rc = stage_rows(e, n, ids, pos.data(), sl.data()))) return rc;
-    rc = e->dtype == G2_F32 ? forward_rows<float>(e, n, n - 1) : forward_rows<__half>(e, n, n - 1);
-    if (rc) return rc;
+    // The forward reads its rows (tokens, positions, slot) from device arrays,
+    // so one graph per length serves every slot and prompt.
+    auto run = [&]() { return e->dtype == G2_F32 ? forward_rows<float>(e, n, n - 1) : forward_rows<__half>(e, n, n - 1); };
+    g2_engine::PrefillGraph *pg = nullptr;
+    if (e->prefill_graph_on && n > 1) {
+        pg = &e->prefill_graphs[n];
+        if (!pg->exec && pg->uses >= 1 && e->prefill_graphs.size() <= 64) {
+            cudaGraph_t g;
+            const long long before = e->launches;
+            CK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+            rc = run();
+            cudaError_t r = cudaStreamEndCapture(e->st, &g);
+            if (rc) return rc;
+            if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "prefill capture: %s", cudaGetErrorString(r));
+            r = cudaGraphInstantiate(&pg->exec, g, 0);
+            cudaGraphDestroy(g);
+            if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "prefill graph instantiate: %s", cudaGetErrorString(r));
+            pg->kernels = e->launches - before;
+            e->launches = before;
+        }
+        ++pg->uses;
+    }
+    if (pg && pg->exec) {
+        CK(cudaGraphLaunch(pg->exec, e->st));
+        e->launches += pg->kernels;
+    } else if ((rc = run())) {
+        return rc;
+    }
     e->filled[slot] = n;
     return G2_OK;
 }
