@@ -297,7 +297,7 @@ def run_ours(args, cfg):
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     import gpt2b200 as g2
     from gpt2b200 import synth
     d, shape = model_for(cfg)
