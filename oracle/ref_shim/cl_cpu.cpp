@@ -11,9 +11,13 @@
 //
 // Work-items: kernels without barriers run one work-item per call with the
 // work-item ids in thread-local storage, spread over OpenMP threads.
-// Kernels with barriers (attn_softmax_1q, matmul) run one work-group at a
-// time on a pool of threads, one per work-item, with a pthread barrier for
-// barrier(); __local arrays are statics shared by those threads.
+// Kernels with barriers (attn_softmax_1q, matmul) run their work-groups in
+// parallel over OpenMP threads; within a group each work-item is a fiber on
+// its own small stack, and barrier() switches back to the group's scheduler,
+// which resumes every fiber in turn (a barrier is reached by all work-items
+// before any passes it).  __local arrays are thread_local statics, so each
+// thread's group has its own.  The switch saves only the callee-saved
+// registers and the stack pointer (x86-64 System V).
 #include "CL/cl.h"
 
 #include <pthread.h>
@@ -55,7 +59,55 @@ void refmm_64x64x16_4x4(const float *, const float *, const float *, float *, in
 
 // ---- work-item ids ------------------------------------------------------------
 static thread_local size_t t_gid[3], t_lid[3], t_grp[3], t_lsz[3] = {1, 1, 1}, t_gsz[3] = {1, 1, 1};
-static pthread_barrier_t *g_wg_barrier = nullptr;
+
+// ---- fibers: one work-group's work-items on one OS thread -------------------------
+extern "C" void g2ref_fiber_switch(void **save_sp, void *load_sp);
+asm(R"(
+    .text
+    .globl g2ref_fiber_switch
+    .type g2ref_fiber_switch,@function
+g2ref_fiber_switch:
+    pushq %rbp
+    pushq %rbx
+    pushq %r12
+    pushq %r13
+    pushq %r14
+    pushq %r15
+    movq %rsp, (%rdi)
+    movq %rsi, %rsp
+    popq %r15
+    popq %r14
+    popq %r13
+    popq %r12
+    popq %rbx
+    popq %rbp
+    ret
+    .size g2ref_fiber_switch, .-g2ref_fiber_switch
+)");
+
+namespace {
+typedef void (*thunk_fn)(const uint64_t *a);
+constexpr size_t kFiberStack = 32 * 1024;
+struct Fiber {
+    void *sp;
+    bool done;
+    size_t lid[3];
+};
+thread_local std::vector<Fiber> t_fibers;
+thread_local std::vector<char> t_stacks;
+thread_local void *t_sched_sp = nullptr;
+thread_local int t_cur = -1;             // running fiber, -1 outside a group
+thread_local thunk_fn t_job = nullptr;
+thread_local const uint64_t *t_job_args = nullptr;
+
+[[noreturn]] void fiber_entry() {
+    t_job(t_job_args);
+    t_fibers[(size_t)t_cur].done = true;
+    void *dead;
+    g2ref_fiber_switch(&dead, t_sched_sp);   // never resumed
+    __builtin_unreachable();
+}
+}  // namespace
 
 extern "C" size_t get_global_id(unsigned d) { return d < 3 ? t_gid[d] : 0; }
 extern "C" size_t get_local_id(unsigned d) { return d < 3 ? t_lid[d] : 0; }
@@ -63,8 +115,11 @@ extern "C" size_t get_group_id(unsigned d) { return d < 3 ? t_grp[d] : 0; }
 extern "C" size_t get_local_size(unsigned d) { return d < 3 ? t_lsz[d] : 1; }
 extern "C" size_t get_global_size(unsigned d) { return d < 3 ? t_gsz[d] : 1; }
 extern "C" void barrier(int) {
-    if (g_wg_barrier) pthread_barrier_wait(g_wg_barrier);
+    if (t_cur >= 0) g2ref_fiber_switch(&t_fibers[(size_t)t_cur].sp, t_sched_sp);
 }
+// Present in builds whose barrier kernels run on fibers (fast enough for the
+// full-size model); the test harness checks for this symbol.
+extern "C" int refcl_fiber_executor(void) { return 1; }
 
 // ---- objects --------------------------------------------------------------------
 struct _cl_platform_id { int dummy; };
@@ -255,88 +310,57 @@ cl_int clSetKernelArg(cl_kernel k, cl_uint idx, size_t size, const void *value) 
     return CL_SUCCESS;
 }
 
-// ---- the pool of threads that runs one work-group with barriers -------------------
+// ---- work-groups with barriers: fibers on each OpenMP thread ---------------------
 namespace {
-struct GroupPool {
-    std::vector<std::thread> threads;
-    std::mutex mu;
-    std::condition_variable cv_start, cv_done;
-    long generation = 0;
-    int active = 0;       // work-items per group in the current job
-    int finished = 0;
-    bool quit = false;
-    // job
-    thunk_t fn = nullptr;
-    const uint64_t *args = nullptr;
-    size_t lsz[3], gsz[3], ngrp[3];
-    pthread_barrier_t bar;
-
-    void worker(int tid, long seen) {
-        for (;;) {
-            {
-                std::unique_lock<std::mutex> lk(mu);
-                cv_start.wait(lk, [&] { return quit || generation != seen; });
-                if (quit) return;
-                seen = generation;
+// Run work-group (g0, g1, g2) of fn: every work-item a fiber, switched round robin.
+void run_group(thunk_fn fn, const uint64_t *a, const size_t *l, const size_t *g, size_t g0, size_t g1, size_t g2) {
+    const size_t n = l[0] * l[1] * l[2];
+    if (t_fibers.size() < n) {
+        t_fibers.resize(n);
+        t_stacks.assign(n * kFiberStack + 64, 0);
+    }
+    char *base = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(t_stacks.data()) + 63) & ~(uintptr_t)63);
+    for (size_t i = 0; i < n; ++i) {
+        Fiber &f = t_fibers[i];
+        // stack top 16-byte aligned; the first switch pops six zero registers and
+        // returns into fiber_entry with rsp = 8 mod 16, as after a call
+        uintptr_t top = (reinterpret_cast<uintptr_t>(base + (i + 1) * kFiberStack)) & ~(uintptr_t)15;
+        uint64_t *sp = reinterpret_cast<uint64_t *>(top - 16);
+        sp[0] = reinterpret_cast<uint64_t>(&fiber_entry);
+        sp[1] = 0;
+        sp -= 6;
+        for (int r = 0; r < 6; ++r) sp[r] = 0;
+        f.sp = sp;
+        f.done = false;
+        f.lid[0] = i % l[0];
+        f.lid[1] = (i / l[0]) % l[1];
+        f.lid[2] = i / (l[0] * l[1]);
+    }
+    t_job = fn;
+    t_job_args = a;
+    const size_t grp[3] = {g0, g1, g2};
+    for (int d = 0; d < 3; ++d) {
+        t_grp[d] = grp[d];
+        t_lsz[d] = l[d];
+        t_gsz[d] = g[d];
+    }
+    size_t left = n;
+    while (left > 0) {
+        for (size_t i = 0; i < n; ++i) {
+            Fiber &f = t_fibers[i];
+            if (f.done) continue;
+            t_cur = (int)i;
+            for (int d = 0; d < 3; ++d) {
+                t_lid[d] = f.lid[d];
+                t_gid[d] = grp[d] * l[d] + f.lid[d];
             }
-            if (tid < active) {
-                t_lsz[0] = lsz[0]; t_lsz[1] = lsz[1]; t_lsz[2] = lsz[2];
-                t_gsz[0] = gsz[0]; t_gsz[1] = gsz[1]; t_gsz[2] = gsz[2];
-                t_lid[0] = tid % lsz[0];
-                t_lid[1] = (tid / lsz[0]) % lsz[1];
-                t_lid[2] = tid / (lsz[0] * lsz[1]);
-                for (size_t g2 = 0; g2 < ngrp[2]; ++g2)
-                    for (size_t g1 = 0; g1 < ngrp[1]; ++g1)
-                        for (size_t g0 = 0; g0 < ngrp[0]; ++g0) {
-                            t_grp[0] = g0; t_grp[1] = g1; t_grp[2] = g2;
-                            for (int d = 0; d < 3; ++d) t_gid[d] = t_grp[d] * lsz[d] + t_lid[d];
-                            fn(args);
-                            pthread_barrier_wait(&bar);   // group g done before g+1 reuses __local
-                        }
-            }
-            std::lock_guard<std::mutex> lk(mu);
-            if (++finished == (int)threads.size()) cv_done.notify_one();
+            g2ref_fiber_switch(&t_sched_sp, f.sp);   // back at the fiber's next barrier or its end
+            if (f.done) --left;
         }
     }
-    void run(thunk_t f, const uint64_t *a, const size_t *l, const size_t *g) {
-        int n = (int)(l[0] * l[1] * l[2]);
-        while ((int)threads.size() < n) {
-            int id = (int)threads.size();
-            long gen;
-            {
-                std::lock_guard<std::mutex> lk(mu);
-                gen = generation;
-            }
-            threads.emplace_back([this, id, gen] { worker(id, gen); });
-        }
-        pthread_barrier_init(&bar, nullptr, (unsigned)n);
-        g_wg_barrier = &bar;
-        {
-            std::lock_guard<std::mutex> lk(mu);
-            fn = f; args = a; active = n; finished = 0;
-            for (int d = 0; d < 3; ++d) { lsz[d] = l[d]; gsz[d] = g[d]; ngrp[d] = g[d] / l[d]; }
-            ++generation;
-        }
-        cv_start.notify_all();
-        std::unique_lock<std::mutex> lk(mu);
-        cv_done.wait(lk, [&] { return finished == (int)threads.size(); });
-        g_wg_barrier = nullptr;
-        pthread_barrier_destroy(&bar);
-    }
-    ~GroupPool() {
-        {
-            std::lock_guard<std::mutex> lk(mu);
-            quit = true;
-        }
-        cv_start.notify_all();
-        for (auto &t : threads) t.join();
-    }
-};
-GroupPool &pool() {
-    static GroupPool p;
-    return p;
+    t_cur = -1;
 }
-}   // namespace
+}  // namespace
 
 cl_int clEnqueueNDRangeKernel(cl_command_queue, cl_kernel k, cl_uint dim, const size_t *off, const size_t *gws,
                               const size_t *lws, cl_uint, const cl_event *, cl_event *) {
@@ -360,7 +384,12 @@ cl_int clEnqueueNDRangeKernel(cl_command_queue, cl_kernel k, cl_uint dim, const 
     }
     if (k->barrier_kernel) {
         if (l[0] * l[1] * l[2] > 1024) return CL_INVALID_WORK_GROUP_SIZE;
-        pool().run(k->fn, a, l, g);
+        const long ng[3] = {(long)(g[0] / l[0]), (long)(g[1] / l[1]), (long)(g[2] / l[2])};
+        const long groups = ng[0] * ng[1] * ng[2];
+        thunk_fn fn = k->fn;
+#pragma omp parallel for schedule(dynamic, 1)
+        for (long q = 0; q < groups; ++q)
+            run_group(fn, a, l, g, (size_t)(q % ng[0]), (size_t)((q / ng[0]) % ng[1]), (size_t)(q / (ng[0] * ng[1])));
         return CL_SUCCESS;
     }
     const long total = (long)(g[0] * g[1] * g[2]);

@@ -5,8 +5,9 @@
  * time) so those kernels build unchanged from the reference's own files:
  *
  *   __kernel  -> extern "C" function     __global -> nothing
- *   __local   -> static (one work-group runs at a time, so the work-items of
- *                that group share it, as local memory is shared)
+ *   __local   -> static thread_local (each OS thread runs one work-group at a
+ *                time, its work-items as fibers, so they share it as local
+ *                memory is shared, and groups on other threads have their own)
  *   float4    -> struct with .s0-.s3 and the scalar*vector / vector+vector
  *                operators the kernels use
  *   get_*_id, barrier -> the work-item executor in cl_cpu.cpp
@@ -20,7 +21,7 @@
 
 #define __kernel extern "C"
 #define __global
-#define __local static
+#define __local static thread_local
 #define CLK_LOCAL_MEM_FENCE 1
 #define CLK_GLOBAL_MEM_FENCE 2
 

@@ -13,11 +13,9 @@ seeded synthetic models and records, per case:
 It also replays each case through the restated oracle (oracle/ref_cpu.c)
 and refuses to write a fixture unless the two agree bit for bit.
 
-Cases marked "port" are made by the restated oracle alone: on GPT-2 small the
-reference build is impractically slow on this host (its startup tuning sweeps
-and barrier kernels run on the CPU OpenCL shim), so the full-size fixture
-comes from the restatement, which tests/test_oracle_pin.py pins bit for bit
-to the reference on the smaller shapes.
+Cases listed in PORT_CASES would be made by the restated oracle alone (for
+shapes too slow for the reference build); none are, since the shim runs the
+reference's barrier kernels on fibers.
 
 Usage: python tests/golden/make_golden.py [case ...]   (needs /root/reference
 or a prebuilt oracle/_ref).  Each case runs in its own process because the
@@ -40,7 +38,7 @@ CASES = {
     "tiny_affine_s1": ("TINY", 1, True, 5, 16, 33),
     "c1_small_s0": ("SMALL", 0, False, 0, 64, 129),
 }
-PORT_CASES = {"c1_small_s0"}
+PORT_CASES = set()   # cases made by the restatement alone (none: the fiber executor runs every case)
 N_IDX = 1024
 LOGIT_STEPS = (0, 1, 32)
 
