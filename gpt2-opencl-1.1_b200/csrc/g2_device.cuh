@@ -21,6 +21,20 @@ __device__ __forceinline__ float gelu_f(float v) {
     return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
 }
 
+// Store v as element i of a GEMM operand (OperandOut): tf32 hi / lo, or fp16.
+__device__ __forceinline__ void put_operand(const OperandOut &o, size_t i, float v) {
+    if (o.kind == 1) {
+        unsigned t;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(v));
+        const float h = __uint_as_float(t);
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(v - h));
+        o.hi[i] = h;
+        o.lo[i] = __uint_as_float(t);
+    } else if (o.kind == 0) {
+        o.h16[i] = __float2half_rn(v);
+    }
+}
+
 // Epilogue shared by gemv and gemm: v = acc (+bias) (GELU) (+resid), stored to
 // out[r][n]; with EPI_KV the K and V thirds of a qkv row are also appended to
 // the cache at (slot[r], layer, head, pos[r]) -- split_kv (math.cl:367-383).
@@ -36,23 +50,26 @@ struct Epi {
     const int *slot;
     int E;
 
-    __device__ __forceinline__ void apply(int r, int n, float v) const {
+    // Returns the value stored to out[r][n].
+    __device__ __forceinline__ float apply(int r, int n, float v) const {
         if (epi & EPI_BIAS) v += tof(bias[n]);
         if (epi & EPI_GELU) v = gelu_f(v);
         if (epi & EPI_RESID) v = resid[(size_t)r * N + n] + v;
         out[(size_t)r * N + n] = v;
         if ((epi & EPI_KV) && n >= E) {
+            const float stored = v;
             int m = n - E;
             const bool isv = m >= E;
             if (isv) m -= E;
             const int h = m >> 6, d = m & 63;
             const int p = pos[r];
-            if (p < 0 || p >= kv.max_seq) return;   // positions are validated on the host; never write outside
+            if (p < 0 || p >= kv.max_seq) return stored;   // positions are validated on the host; never write outside
             const long long off = (long long)slot[r] * kv.slot_stride + (long long)layer * kv.layer_stride +
                                   ((long long)h * kv.max_seq + p) * kHeadDim + d;
             WT *base = reinterpret_cast<WT *>(isv ? kv.v : kv.k);
             base[off] = fromf<WT>(v);
         }
+        return v;
     }
 };
 

@@ -133,7 +133,9 @@ struct g2_engine {
     bool tc = false;
     int tc_kind = TC_TF32X3;
     float *tc_w = nullptr;                    // fp32 engine: tf32 hi / lo copies of the projections
-    float *tc_xhi = nullptr, *tc_xlo = nullptr;   // GEMM input rows: hi / lo (fp32) or fp16 (in tc_xhi)
+    float *tc_xhi = nullptr, *tc_xlo = nullptr;     // GEMM input rows with K = E: hi / lo (fp32) or fp16 (in tc_xhi)
+    float *tc_x2hi = nullptr, *tc_x2lo = nullptr;   // fc2's input rows (K = F), written by the fc GEMM
+    unsigned *tc_ctr = nullptr;                    // split-K tile counters
     float *tc_part = nullptr;                 // split-K partial sums
     size_t tc_part_floats = 0;
     int *tc_err = nullptr;
@@ -142,7 +144,9 @@ struct g2_engine {
     int *sample_ctx = nullptr;      // [n_ctx] context ids
     int *h_ctx = nullptr;           // pinned staging of the context ids
     std::vector<TcWeights> tc_maps;           // [L][4]: qkv, proj, fc, fc2
-    TcRowsOperand tc_x_e{}, tc_x_f{};         // input rows with K = E and K = F
+    TcWeights tc_lm{};                        // the tied LM head: wte [V][E] as a K-major operand
+    float *tc_lm_w = nullptr;                 // fp32 engine: tf32 hi / lo copies of wte
+    TcRowsOperand tc_x_e{}, tc_x_f{};         // input rows with K = E (tc_x*) and K = F (tc_x2*)
 
     template <typename WT>
     const WT *w(size_t off) const {
@@ -171,7 +175,7 @@ static void free_engine(g2_engine *e) {
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
     for (auto &kv : e->prefill_graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_xhi, e->tc_xlo, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f,
+    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_lm_w, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f,
                         e->t_best, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
                         e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
@@ -620,11 +624,31 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
                     o += align_up(n, 64);
                 }
             }
-            const size_t xr = (size_t)R * (E > F ? E : F);
-            TRY(dalloc(e, &e->tc_xhi, xr));
-            if (e->tc_kind == TC_TF32X3) TRY(dalloc(e, &e->tc_xlo, xr));
+            {
+                const size_t n = (size_t)c.vocab_size * E;
+                int rc;
+                if (e->tc_kind == TC_TF32X3) {
+                    TRY(dalloc(e, &e->tc_lm_w, 2 * align_up(n, 64)));
+                    float *hi = e->tc_lm_w, *lo_ = e->tc_lm_w + align_up(n, 64);
+                    launch_tc_prep(TC_TF32X3, e->w<float>(e->lm), hi, lo_, nullptr, (long long)n, e->st);
+                    rc = tc_weights_kmajor(&e->tc_lm, TC_TF32X3, hi, lo_, E, c.vocab_size);
+                } else {
+                    rc = tc_weights_kmajor(&e->tc_lm, TC_F16, e->w<__half>(e->lm), nullptr, E, c.vocab_size);
+                }
+                if (rc) {
+                    free_engine(e);
+                    return set_err(rc, "tensor map of the LM head");
+                }
+            }
+            TRY(dalloc(e, &e->tc_xhi, (size_t)R * E));
+            TRY(dalloc(e, &e->tc_x2hi, (size_t)R * F));
+            if (e->tc_kind == TC_TF32X3) {
+                TRY(dalloc(e, &e->tc_xlo, (size_t)R * E));
+                TRY(dalloc(e, &e->tc_x2lo, (size_t)R * F));
+            }
+            TRY(dalloc(e, &e->tc_ctr, (size_t)kTcMaxTiles));
             int rc = tc_rows_operand(&e->tc_x_e, e->tc_kind, e->tc_xhi, e->tc_xlo, E, R);
-            if (!rc) rc = tc_rows_operand(&e->tc_x_f, e->tc_kind, e->tc_xhi, e->tc_xlo, F, R);
+            if (!rc) rc = tc_rows_operand(&e->tc_x_f, e->tc_kind, e->tc_x2hi, e->tc_x2lo, F, R);
             if (rc) {
                 free_engine(e);
                 return set_err(rc, "tensor maps of the GEMM input rows");
@@ -692,52 +716,97 @@ static int stage_rows(g2_engine *e, int n, const int *tok, const int *pos, const
 // All layers over `nrows` rows described by the device row arrays (prefill of
 // one slot, or one decode token for each of several slots).  Leaves the
 // residual stream in e->h.
-// One projection of a many-row pass: out[r] = epilogue(X[r] W) on the tensor
-// cores (X split / rounded into the GEMM input rows first), or the SIMT GEMM.
+// Where a kernel writes the next tensor-core GEMM's operand: the rows with
+// K = E (LN and attention outputs) or fc2's rows (fc's output).
+static OperandOut operand_e(const g2_engine *e) {
+    OperandOut o;
+    if (e->tc) {
+        o.kind = e->tc_kind;
+        o.hi = e->tc_xhi;
+        o.lo = e->tc_xlo;
+        o.h16 = reinterpret_cast<__half *>(e->tc_xhi);
+    }
+    return o;
+}
+static OperandOut operand_f(const g2_engine *e) {
+    OperandOut o;
+    if (e->tc) {
+        o.kind = e->tc_kind;
+        o.hi = e->tc_x2hi;
+        o.lo = e->tc_x2lo;
+        o.h16 = reinterpret_cast<__half *>(e->tc_x2hi);
+    }
+    return o;
+}
+
+// One projection of a many-row pass: out[r] = epilogue(X[r] W), on the tensor
+// cores (X already written as the operand by its producer) or by the SIMT GEMM.
 template <typename WT>
 static void rows_gemm(g2_engine *e, int l, int q, const float *X, int nrows, const WT *W, const WT *bias,
-                      const float *resid, float *out, int N, int K, int epi, const KVLayout *kv, Rows rows) {
-    cudaStream_t st = e->st;
+                      const float *resid, float *out, int N, int K, int epi, const KVLayout *kv, Rows rows,
+                      OperandOut op = OperandOut()) {
     if (e->tc) {
-        launch_tc_prep(e->tc_kind, X, e->tc_xhi, e->tc_xlo, reinterpret_cast<__half *>(e->tc_xhi),
-                       (long long)nrows * K, st);
-        e->launches += 1 + launch_tc_gemm<WT>(e->tc_kind, e->tc_maps[(size_t)l * 4 + q], K == e->c.n_embd ? e->tc_x_e : e->tc_x_f,
-                                              nrows, e->tc_part, e->tc_part_floats, e->tc_err, bias, resid, out, epi, kv,
-                                              l, rows, e->sms, st);
+        e->launches += launch_tc_gemm<WT>(e->tc_kind, e->tc_maps[(size_t)l * 4 + q],
+                                          K == e->c.n_embd ? e->tc_x_e : e->tc_x_f, nrows, e->tc_part,
+                                          e->tc_part_floats, e->tc_ctr, e->tc_err, bias, resid, out, epi, kv, l, rows,
+                                          e->sms, e->st, op);
     } else {
-        launch_gemm_rows<WT>(X, W, bias, resid, out, nrows, N, K, epi, kv, l, rows, st);
+        launch_gemm_rows<WT>(X, W, bias, resid, out, nrows, N, K, epi, kv, l, rows, e->st);
         e->launches += 1;
     }
 }
 
 // All layers over `nrows` rows described by the device row arrays (prefill of
 // one slot, or one decode token for each of several slots).  Leaves the
-// residual stream in e->h.
+// residual stream in e->h.  With the tensor cores, LayerNorm and attention
+// write the next GEMM's operand themselves and fc writes fc2's, so a layer is
+// seven launches.
 template <typename WT>
 static int forward_rows(g2_engine *e, int nrows, int max_pos) {
     const ModelConfig &c = e->c;
     const int E = c.n_embd, F = c.ffn_dim;
     cudaStream_t st = e->st;
     Rows rows{e->rows_tok, e->rows_pos, e->rows_slot};
+    const OperandOut ope = operand_e(e), opf = operand_f(e);
     launch_embed<WT>(e->w<WT>(e->wte), e->w<WT>(e->wpe), rows, e->h, E, c.vocab_size, c.n_ctx, nrows, st);
     for (int l = 0; l < c.n_layer; ++l) {
         const LayerOff &o = e->L[l];
-        launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln1_g), e->w<WT>(o.ln1_b), E, nrows, st);
+        launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln1_g), e->w<WT>(o.ln1_b), E, nrows, st, ope);
         rows_gemm<WT>(e, l, 0, e->xln, nrows, e->w<WT>(o.qkv_w), e->w<WT>(o.qkv_b), nullptr, e->qkv, 3 * E, E,
                       EPI_BIAS | EPI_KV, &e->kv, rows);
         launch_attention<WT>(e->qkv, 3 * E, e->kv, l, rows, nrows, e->attn, E, e->attn_partial, e->attn_ctr, max_pos,
-                             st);
+                             st, ope);
         rows_gemm<WT>(e, l, 1, e->attn, nrows, e->w<WT>(o.proj_w), e->w<WT>(o.proj_b), e->h, e->h, E, E,
                       EPI_BIAS | EPI_RESID, nullptr, rows);
-        launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln2_g), e->w<WT>(o.ln2_b), E, nrows, st);
+        launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln2_g), e->w<WT>(o.ln2_b), E, nrows, st, ope);
         rows_gemm<WT>(e, l, 2, e->xln, nrows, e->w<WT>(o.fc_w), e->w<WT>(o.fc_b), nullptr, e->ffn, F, E,
-                      EPI_BIAS | EPI_GELU, nullptr, rows);
+                      EPI_BIAS | EPI_GELU, nullptr, rows, opf);
         rows_gemm<WT>(e, l, 3, e->ffn, nrows, e->w<WT>(o.fc2_w), e->w<WT>(o.fc2_b), e->h, e->h, E, F,
                       EPI_BIAS | EPI_RESID, nullptr, rows);
     }
     e->launches += 1 + 3LL * c.n_layer;
     CKL();
     return G2_OK;
+}
+
+// ln_f + the tied LM head over the `nrows` rows of e->h (one token of each
+// sequence of a batched step) into e->logits_rows (row stride padded_vocab):
+// on the tensor cores, ln_f writes the operand and the GEMM reads wte's rows.
+template <typename WT>
+static void lm_head_rows(g2_engine *e, int nrows) {
+    const ModelConfig &c = e->c;
+    launch_layernorm<WT>(e->h, e->xln, e->w<WT>(e->lnf_g), e->w<WT>(e->lnf_b), c.n_embd, nrows, e->st, operand_e(e));
+    if (e->tc) {
+        Rows rows{e->rows_tok, e->rows_pos, e->rows_slot};
+        e->launches += launch_tc_gemm<WT>(e->tc_kind, e->tc_lm, e->tc_x_e, nrows, e->tc_part, e->tc_part_floats,
+                                          e->tc_ctr, e->tc_err, nullptr, nullptr, e->logits_rows, 0, nullptr, 0, rows,
+                                          e->sms, e->st, OperandOut(), c.padded_vocab);
+    } else {
+        launch_lm_head_rows<WT>(e->xln, e->w<WT>(e->lm), e->logits_rows, c.n_embd, c.vocab_size, c.padded_vocab,
+                                nrows, e->st);
+        e->launches += 1;
+    }
+    e->launches += 1;
 }
 
 // LM head on row `row` of e->h for `slot`, optionally advancing the step state.
@@ -1001,17 +1070,15 @@ extern "C" int g2_decode_batch(g2_engine *e, int n, const int *slots, const int 
     const ModelConfig &c = e->c;
     if (e->dtype == G2_F32) {
         if ((rc = forward_rows<float>(e, n, maxp))) return rc;
-        launch_layernorm<float>(e->h, e->xln, e->w<float>(e->lnf_g), e->w<float>(e->lnf_b), c.n_embd, n, e->st);
-        launch_lm_head_rows<float>(e->xln, e->w<float>(e->lm), e->logits_rows, c.n_embd, c.vocab_size, c.padded_vocab, n, e->st);
+        lm_head_rows<float>(e, n);
     } else {
         if ((rc = forward_rows<__half>(e, n, maxp))) return rc;
-        launch_layernorm<__half>(e->h, e->xln, e->w<__half>(e->lnf_g), e->w<__half>(e->lnf_b), c.n_embd, n, e->st);
-        launch_lm_head_rows<__half>(e->xln, e->w<__half>(e->lm), e->logits_rows, c.n_embd, c.vocab_size, c.padded_vocab, n, e->st);
+        lm_head_rows<__half>(e, n);
     }
     for (int i = 0; i < n; ++i)
         launch_copy_row(e->logits_rows + (size_t)i * c.padded_vocab, e->logits + (size_t)slots[i] * c.padded_vocab,
                         c.vocab_size, e->st);
-    e->launches += 2 + n;
+    e->launches += n;
     CKL();
     for (int i = 0; i < n; ++i) e->filled[slots[i]] = pos[i] + 1;
     e->result_slot = -1;
@@ -1152,12 +1219,11 @@ static int record_batch_step(g2_engine *e, int n) {
     const ModelConfig &c = e->c;
     int rc = forward_rows<WT>(e, n, -1);
     if (rc) return rc;
-    launch_layernorm<WT>(e->h, e->xln, e->w<WT>(e->lnf_g), e->w<WT>(e->lnf_b), c.n_embd, n, e->st);
-    launch_lm_head_rows<WT>(e->xln, e->w<WT>(e->lm), e->logits_rows, c.n_embd, c.vocab_size, c.padded_vocab, n, e->st);
+    lm_head_rows<WT>(e, n);
     launch_argmax_rows(e->logits_rows, c.vocab_size, c.padded_vocab, n, 1, nullptr, nullptr, e->rows_tok,
                        e->rows_pos, e->out_tokens, c.n_ctx, e->batch_step, e->st);
     launch_step_advance(e->batch_step, e->st);
-    e->launches += 4;
+    e->launches += 2;
     return G2_OK;
 }
 
@@ -1284,12 +1350,14 @@ extern "C" int g2k_matmul(const float *A, const float *B, const float *bias, con
     return G2_OK;
 }
 
-// Workspace of g2k_matmul_tc: [err | A hi | A lo | B hi | B lo | partial sums], 256-byte aligned parts.
+// Workspace of g2k_matmul_tc: [err + tile counters | A hi | A lo | B hi | B lo | partial sums],
+// 256-byte aligned parts.
 static size_t tc_ws_layout(int M, int N, int K, int precision, int sms, size_t off[6]) {
     const int kind = precision == G2_F16 ? TC_F16 : TC_TF32X3;
     const size_t es = kind == TC_F16 ? 2 : 4;
-    const size_t sz[6] = {256, (size_t)M * K * es, kind == TC_F16 ? 0 : (size_t)M * K * 4, (size_t)K * N * es,
-                          kind == TC_F16 ? 0 : (size_t)K * N * 4, tc_partial_floats(M, N, K, kind, sms) * 4};
+    const size_t sz[6] = {256 + (size_t)kTcMaxTiles * 4, (size_t)M * K * es, kind == TC_F16 ? 0 : (size_t)M * K * 4,
+                          (size_t)K * N * es, kind == TC_F16 ? 0 : (size_t)K * N * 4,
+                          tc_partial_floats(M, N, K, kind, sms) * 4};
     size_t o = 0;
     for (int i = 0; i < 6; ++i) {
         off[i] = o;
@@ -1326,7 +1394,8 @@ extern "C" int g2k_matmul_tc(const float *A, const float *B, const float *bias, 
     char *ws = static_cast<char *>(workspace);
     cudaStream_t st = (cudaStream_t)stream;
     int *err = reinterpret_cast<int *>(ws);
-    CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+    unsigned *ctr = reinterpret_cast<unsigned *>(ws + 256);
+    CK(cudaMemsetAsync(ws, 0, 256 + (size_t)kTcMaxTiles * 4, st));
     float *ahi = reinterpret_cast<float *>(ws + off[1]), *alo = reinterpret_cast<float *>(ws + off[2]);
     float *bhi = reinterpret_cast<float *>(ws + off[3]), *blo = reinterpret_cast<float *>(ws + off[4]);
     launch_tc_prep(kind, A, ahi, alo, reinterpret_cast<__half *>(ahi), (long long)M * K, st);
@@ -1337,8 +1406,10 @@ extern "C" int g2k_matmul_tc(const float *A, const float *B, const float *bias, 
     if (!rc) rc = tc_rows_operand(&x, kind, ahi, alo, K, M);
     if (rc) return set_err(rc, "g2k_matmul_tc: tensor map encoding failed");
     const int epi = (bias ? EPI_BIAS : 0) | (apply_gelu ? EPI_GELU : 0) | (residual ? EPI_RESID : 0);
+    if (((size_t)(N + kTcTileF - 1) / kTcTileF) * ((M + 31) / 32) > (size_t)kTcMaxTiles)
+        return set_err(G2_ERR_RANGE, "g2k_matmul_tc: more than %d output tiles", kTcMaxTiles);
     launch_tc_gemm<float>(kind, w, x, M, reinterpret_cast<float *>(ws + off[5]),
-                          tc_partial_floats(M, N, K, kind, sms), err, bias, residual, C, epi, nullptr, 0,
+                          tc_partial_floats(M, N, K, kind, sms), ctr, err, bias, residual, C, epi, nullptr, 0,
                           Rows{nullptr, nullptr, nullptr}, sms, st);
     CKL();
     return G2_OK;

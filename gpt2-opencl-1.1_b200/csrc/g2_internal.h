@@ -45,6 +45,15 @@ struct Rows {
 
 enum Epilogue { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_RESID = 4, EPI_KV = 8 };
 
+// A kernel's output also written as the next tensor-core GEMM's operand (row
+// stride = that GEMM's K): kind 1 = tf32 hi / lo pair (TC_TF32X3), 0 = fp16
+// (TC_F16), -1 = not written.
+struct OperandOut {
+    int kind = -1;
+    float *hi = nullptr, *lo = nullptr;
+    __half *h16 = nullptr;
+};
+
 // ---- launchers (g2_kernels.cu); all asynchronous on `st` ------------------------
 // p[0..4) = a, b, c, d on the device (g2_kernels.cu).
 void launch_set_ints(int *p, int a, int b, int c, int d, cudaStream_t st);
@@ -57,7 +66,8 @@ void launch_embed(const WT *wte, const WT *wpe, Rows rows, float *h, int E, int 
                   cudaStream_t st);
 
 template <typename WT>
-void launch_layernorm(const float *x, float *out, const WT *g, const WT *b, int E, int nrows, cudaStream_t st);
+void launch_layernorm(const float *x, float *out, const WT *g, const WT *b, int E, int nrows, cudaStream_t st,
+                      OperandOut op = OperandOut());
 
 // B=1 GEMV: y = x' W (+bias)(GELU)(+resid)(KV append), x' = LN(x) if ln_g.
 // partial: [ksplit][N] floats, counters: [N / cols-per-CTA] zeroed uints.
@@ -84,7 +94,7 @@ size_t attn_counter_count(int nrows, int n_head);
 template <typename KT>
 void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
                       float *out, int out_stride, float *partial, unsigned *counters, int max_pos_hint,
-                      cudaStream_t st);
+                      cudaStream_t st, OperandOut op = OperandOut());
 
 // LM head on one row x (fp32 [E]) with the final LayerNorm fused:
 // logits[v] = LN_f(x) . wte[v]; argmax over v < V (first index on ties,

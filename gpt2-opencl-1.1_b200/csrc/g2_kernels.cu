@@ -144,13 +144,18 @@ __global__ void embed_kernel(const WT *wte, const WT *wpe, Rows rows, float *h, 
 
 // layernorm (math.cl:283-311), one CTA per row.
 template <typename WT>
-__global__ void __launch_bounds__(256) layernorm_kernel(const float *x, float *out, const WT *g, const WT *b, int E) {
+__global__ void __launch_bounds__(256) layernorm_kernel(const float *x, float *out, const WT *g, const WT *b, int E,
+                                                        OperandOut op) {
     __shared__ float sh[32];
     const float *xr = x + (size_t)blockIdx.x * E;
     float mean, rstd;
     ln_stats(xr, E, sh, mean, rstd);
-    for (int i = threadIdx.x; i < E; i += blockDim.x)
-        out[(size_t)blockIdx.x * E + i] = (xr[i] - mean) * rstd * tof(g[i]) + tof(b[i]);
+    for (int i = threadIdx.x; i < E; i += blockDim.x) {
+        const float v = (xr[i] - mean) * rstd * tof(g[i]) + tof(b[i]);
+        const size_t o = (size_t)blockIdx.x * E + i;
+        out[o] = v;
+        put_operand(op, o, v);
+    }
 }
 
 // ------------------------------------------------------------------------------
@@ -333,6 +338,7 @@ struct AttnArgs {
     float *partial;      // [rows][heads][max_splits][66]
     unsigned *counters;  // [rows][heads]
     int max_splits;
+    OperandOut op;       // the output also as the next GEMM's operand (row stride out_stride)
 };
 
 template <typename KT>
@@ -386,7 +392,12 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
     const float* none = nullptr;
     (void)none;
     if (nsplit == 1) {
-        if (tid < kHeadDim) a.out[(size_t)r * a.out_stride + h * kHeadDim + tid] = (accs[0][tid] + accs[1][tid]) / l;
+        if (tid < kHeadDim) {
+            const size_t o = (size_t)r * a.out_stride + h * kHeadDim + tid;
+            const float v = (accs[0][tid] + accs[1][tid]) / l;
+            a.out[o] = v;
+            put_operand(a.op, o, v);
+        }
         return;
     }
     float *P = a.partial + (((size_t)r * NH + h) * a.max_splits + sp) * (kHeadDim + 2);
@@ -413,7 +424,9 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
             L = fmaf(__ldcg(Pi + 1), w, L);
             O = fmaf(__ldcg(Pi + 2 + tid), w, O);
         }
-        a.out[(size_t)r * a.out_stride + h * kHeadDim + tid] = O / L;
+        const size_t o = (size_t)r * a.out_stride + h * kHeadDim + tid;
+        a.out[o] = O / L;
+        put_operand(a.op, o, O / L);
     }
     if (tid == 0) *ctr = 0u;
 }
@@ -523,12 +536,29 @@ __global__ void __launch_bounds__(256) argmax_rows_kernel(const float *logits, i
     const float *L = logits + (size_t)r * Vp;
     float best = -FLT_MAX;
     int besti = INT_MAX;
-    for (int v = tid; v < V; v += 256) {
-        if (forbid_eos && v == kEos) continue;
-        const float s = L[v];
-        if (better(s, v, best, besti)) {
-            best = s;
-            besti = v;
+    // float4 chunks (rows are Vp = multiple of 4 floats, 16-byte aligned), four in flight per thread
+    const float4 *L4 = reinterpret_cast<const float4 *>(L);
+    const int n4 = (V + 3) / 4;
+    for (int c0 = tid; c0 < n4; c0 += 4 * 256) {
+        float4 q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u * 256;
+            q[u] = c < n4 ? L4[c] : make_float4(-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u * 256;
+            const float vals[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int v = 4 * c + k;
+                if (c >= n4 || v >= V || (forbid_eos && v == kEos)) continue;
+                if (better(vals[k], v, best, besti)) {
+                    best = vals[k];
+                    besti = v;
+                }
+            }
         }
     }
 #pragma unroll
@@ -575,8 +605,9 @@ void launch_embed(const WT *wte, const WT *wpe, Rows rows, float *h, int E, int 
 }
 
 template <typename WT>
-void launch_layernorm(const float *x, float *out, const WT *g, const WT *b, int E, int nrows, cudaStream_t st) {
-    layernorm_kernel<WT><<<nrows, 256, 0, st>>>(x, out, g, b, E);
+void launch_layernorm(const float *x, float *out, const WT *g, const WT *b, int E, int nrows, cudaStream_t st,
+                      OperandOut op) {
+    layernorm_kernel<WT><<<nrows, 256, 0, st>>>(x, out, g, b, E, op);
 }
 
 template <typename WT>
@@ -661,8 +692,9 @@ size_t attn_counter_count(int nrows, int n_head) { return (size_t)nrows * n_head
 template <typename KT>
 void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
                       float *out, int out_stride, float *partial, unsigned *counters, int max_pos_hint,
-                      cudaStream_t st) {
+                      cudaStream_t st, OperandOut op) {
     AttnArgs<KT> a;
+    a.op = op;
     a.qkv = qkv;
     a.qkv_stride = qkv_stride;
     a.kv = kv;
@@ -752,7 +784,8 @@ void launch_step_advance(int *step_ptr, cudaStream_t st) { step_advance_kernel<<
 // explicit instantiations
 #define G2_INST(WT)                                                                                                   \
     template void launch_embed<WT>(const WT *, const WT *, Rows, float *, int, int, int, int, cudaStream_t);         \
-    template void launch_layernorm<WT>(const float *, float *, const WT *, const WT *, int, int, cudaStream_t);      \
+    template void launch_layernorm<WT>(const float *, float *, const WT *, const WT *, int, int, cudaStream_t,       \
+                                       OperandOut);                                                                   \
     template GemvPlan gemv_plan<WT>(int, int, int);                                                                    \
     template void launch_gemv<WT>(const float *, const WT *, const WT *, const float *, float *, int, int, int,      \
                                   const WT *, const WT *, float *, unsigned *, GemvPlan, const KVLayout *, int,     \
@@ -760,7 +793,7 @@ void launch_step_advance(int *step_ptr, cudaStream_t st) { step_advance_kernel<<
     template void launch_gemm_rows<WT>(const float *, const WT *, const WT *, const float *, float *, int, int, int, \
                                        int, const KVLayout *, int, Rows, cudaStream_t);                              \
     template void launch_attention<WT>(const float *, int, const KVLayout &, int, Rows, int, float *, int, float *,  \
-                                       unsigned *, int, cudaStream_t);                                                \
+                                       unsigned *, int, cudaStream_t, OperandOut);                                    \
     template void launch_lm_head<WT>(const float *, const WT *, const WT *, const WT *, float *, int, int, int, int, \
                                      float *, unsigned *, int *, StepState *, int *, cudaStream_t);                  \
     template void launch_lm_head_rows<WT>(const float *, const WT *, float *, int, int, int, int, cudaStream_t);

@@ -84,11 +84,12 @@ __device__ __forceinline__ u64 sw128_desc(unsigned saddr, unsigned lbo, unsigned
            (1ull << 46) | ((u64)layout << 61);
 }
 
-// Instruction descriptor: D f32; A, B tf32 or f16; A MN-major, B K-major; N = BN, M = 128.
-template <int KIND, int BN>
+// Instruction descriptor: D f32; A, B tf32 or f16; A MN-major (Conv1D weights)
+// or K-major (AK: rows of wte), B K-major; N = BN, M = 128.
+template <int KIND, int BN, bool AK>
 __host__ __device__ constexpr unsigned make_idesc() {
-    return (1u << 4) | ((KIND == TC_TF32X3 ? 2u : 0u) << 7) | ((KIND == TC_TF32X3 ? 2u : 0u) << 10) | (1u << 15) |
-           ((unsigned)(BN >> 3) << 17) | ((unsigned)(kTcTileF >> 4) << 24);
+    return (1u << 4) | ((KIND == TC_TF32X3 ? 2u : 0u) << 7) | ((KIND == TC_TF32X3 ? 2u : 0u) << 10) |
+           ((AK ? 0u : 1u) << 15) | ((unsigned)(BN >> 3) << 17) | ((unsigned)(kTcTileF >> 4) << 24);
 }
 
 template <int KIND>
@@ -126,11 +127,15 @@ __device__ __forceinline__ void tmem_ld32(unsigned taddr, float (&v)[32]) {
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
+template <typename WT>
 struct TcArgs {
     int N, R;
     int kb_total, kb_per;   // K blocks in total and per split
-    float *part;            // [splits][R][N]
+    int splits;
+    float *part;            // [splits][R][N] when splits > 1
     int *err;
+    Epi<WT> e;              // bias / GELU / residual / K,V append, out
+    OperandOut op;          // the output also as the next GEMM's operand (row stride N)
 };
 
 template <int KIND>
@@ -157,10 +162,11 @@ struct TcCfg {
     static constexpr size_t SMEM = (size_t)STAGES * STAGE + 1024 + 256;
 };
 
-template <int KIND, int BN>
+template <int KIND, int BN, typename WT, bool AK>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mw_hi, const __grid_constant__ CUtensorMap mw_lo,
-                   const __grid_constant__ CUtensorMap mx_hi, const __grid_constant__ CUtensorMap mx_lo, TcArgs a) {
+                   const __grid_constant__ CUtensorMap mx_hi, const __grid_constant__ CUtensorMap mx_lo,
+                   TcArgs<WT> a) {
     using S = TcShape<KIND>;
     using C = TcCfg<KIND, BN>;
     constexpr int STAGES = C::STAGES;
@@ -207,11 +213,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int k = (kb0 + i) * S::BK;
             mbar_expect_tx(&full[s], C::STAGE);
 #pragma unroll
-            for (int p = 0; p < S::NPASS; ++p)
+            for (int p = 0; p < S::NPASS; ++p) {
+                if (AK) {   // 128 rows x 128 bytes of K in one box
+                    tma_load_2d(st + p * S::A_BYTES, p ? &mw_lo : &mw_hi, k, f0, &full[s]);
+                } else {
 #pragma unroll
-                for (int b = 0; b < S::NBOX; ++b)
-                    tma_load_2d(st + p * S::A_BYTES + b * (S::BK * 128), p ? &mw_lo : &mw_hi, f0 + b * S::BOX_F, k,
-                                &full[s]);
+                    for (int b = 0; b < S::NBOX; ++b)
+                        tma_load_2d(st + p * S::A_BYTES + b * (S::BK * 128), p ? &mw_lo : &mw_hi, f0 + b * S::BOX_F,
+                                    k, &full[s]);
+                }
+            }
 #pragma unroll
             for (int p = 0; p < S::NPASS; ++p)
                 tma_load_2d(st + S::NPASS * S::A_BYTES + p * C::B_BYTES, p ? &mx_lo : &mx_hi, k, r0, &full[s]);
@@ -221,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
     } else if (threadIdx.x == 32) {
         // ---- MMA issuer ----
-        constexpr unsigned idesc = make_idesc<KIND, BN>();
+        constexpr unsigned idesc = make_idesc<KIND, BN, AK>();
         for (int i = 0; i < nkb; ++i) {
             const int s = i % STAGES;
             if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
@@ -233,13 +244,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const unsigned b_hi = a_hi + S::NPASS * S::A_BYTES;
 #pragma unroll
             for (int j = 0; j < S::NSTEP; ++j) {
-                const unsigned ao = j * S::KSTEP * 128, bo = j * S::KSTEP * S::ELEM;
-                const u64 ad = sw128_desc(a_hi + ao, S::BK * 128, S::A_SBO, S::A_LAYOUT);
+                const unsigned ao = AK ? j * S::KSTEP * S::ELEM : j * S::KSTEP * 128, bo = j * S::KSTEP * S::ELEM;
+                const u64 ad = AK ? sw128_desc(a_hi + ao, 16, 1024) : sw128_desc(a_hi + ao, S::BK * 128, S::A_SBO, S::A_LAYOUT);
                 const u64 bd = sw128_desc(b_hi + bo, 16, 1024);
                 const unsigned acc = (i | j) != 0;
                 mma<KIND>(tmem, ad, bd, idesc, acc);
                 if (KIND == TC_TF32X3) {
-                    const u64 ad_lo = sw128_desc(a_hi + S::A_BYTES + ao, S::BK * 128, S::A_SBO, S::A_LAYOUT);
+                    const u64 ad_lo = AK ? sw128_desc(a_hi + S::A_BYTES + ao, 16, 1024)
+                                         : sw128_desc(a_hi + S::A_BYTES + ao, S::BK * 128, S::A_SBO, S::A_LAYOUT);
                     const u64 bd_lo = sw128_desc(b_hi + C::B_BYTES + bo, 16, 1024);
                     mma<KIND>(tmem, ad, bd_lo, idesc, 1u);
                     mma<KIND>(tmem, ad_lo, bd, idesc, 1u);
@@ -251,12 +263,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
 
-    // ---- epilogue: tensor memory -> partial tile ----
+    // ---- epilogue: tensor memory -> output (one split) or partial tile ----
     const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0));   // warp-uniform: tcgen05.ld is .sync.aligned
     if (!ok && lane == 0) atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int f = f0 + warp * 32 + lane;
     if (ok) {
-        const int f = f0 + warp * 32 + lane;
         float *dst = a.part + (size_t)blockIdx.z * a.R * a.N;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -266,7 +278,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int r = r0 + c0 + j;
-                    if (r < a.R) dst[(size_t)r * a.N + f] = v[j];
+                    if (r >= a.R) continue;
+                    if (a.splits == 1) put_operand(a.op, (size_t)r * a.N + f, a.e.apply(r, f, v[j]));
+                    else dst[(size_t)r * a.N + f] = v[j];
                 }
             }
         }
@@ -274,6 +288,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((unsigned)BN));
+}
+
+// Ordered sum of the splits + epilogue (+ the next GEMM's operand), 4 outputs
+// per thread (N % 4 == 0); used when a GEMM ran with split-K.
+template <typename WT>
+__global__ void tc_reduce_kernel(const float *part, int splits, int R, int N, Epi<WT> e, OperandOut op) {
+    const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    const long long total = (long long)R * N;
+    if (i >= total) return;
+    float4 acc = *reinterpret_cast<const float4 *>(part + i);
+    for (int s = 1; s < splits; ++s) {
+        const float4 p = *reinterpret_cast<const float4 *>(part + (size_t)s * total + i);
+        acc.x += p.x;
+        acc.y += p.y;
+        acc.z += p.z;
+        acc.w += p.w;
+    }
+    const int r = (int)(i / N), n = (int)(i % N);
+    put_operand(op, (size_t)i, e.apply(r, n, acc.x));
+    put_operand(op, (size_t)i + 1, e.apply(r, n + 1, acc.y));
+    put_operand(op, (size_t)i + 2, e.apply(r, n + 2, acc.z));
+    put_operand(op, (size_t)i + 3, e.apply(r, n + 3, acc.w));
 }
 
 // x -> (hi, lo) tf32 pair, or x -> fp16.
@@ -298,27 +334,6 @@ __global__ void tc_prep_kernel(int kind, const float4 *x, float4 *hi, float4 *lo
             h16[2 * i + 1] = __floats2half2_rn(v.z, v.w);
         }
     }
-}
-
-// Ordered sum of the splits + epilogue, 4 outputs per thread (N % 4 == 0).
-template <typename WT>
-__global__ void tc_reduce_kernel(const float *part, int splits, int R, int N, Epi<WT> e) {
-    const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
-    const long long total = (long long)R * N;
-    if (i >= total) return;
-    float4 acc = *reinterpret_cast<const float4 *>(part + i);
-    for (int s = 1; s < splits; ++s) {
-        const float4 p = *reinterpret_cast<const float4 *>(part + (size_t)s * total + i);
-        acc.x += p.x;
-        acc.y += p.y;
-        acc.z += p.z;
-        acc.w += p.w;
-    }
-    const int r = (int)(i / N), n = (int)(i % N);
-    e.apply(r, n, acc.x);
-    e.apply(r, n + 1, acc.y);
-    e.apply(r, n + 2, acc.z);
-    e.apply(r, n + 3, acc.w);
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -355,22 +370,21 @@ TcPlan plan(int R, int N, int kb_total, int sms) {
     return p;
 }
 
-template <int KIND, int BN>
-void launch_kernel(const TcWeights &w, const TcRowsOperand &x, int bn_idx, const TcArgs &a, int splits,
-                   cudaStream_t st) {
+template <int KIND, int BN, typename WT, bool AK>
+void launch_kernel(const TcWeights &w, const TcRowsOperand &x, int bn_idx, const TcArgs<WT> &a, cudaStream_t st) {
     using C = TcCfg<KIND, BN>;
     static unsigned long long attr_set = 0;   // devices on which this instantiation's smem limit was raised
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !(__atomic_load_n(&attr_set, __ATOMIC_ACQUIRE) >> dev & 1ull)) {
-        cudaFuncSetAttribute(tc_gemm_kernel<KIND, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+        cudaFuncSetAttribute(tc_gemm_kernel<KIND, BN, WT, AK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
         __atomic_fetch_or(&attr_set, 1ull << dev, __ATOMIC_RELEASE);
     } else if (dev >= 64) {
-        cudaFuncSetAttribute(tc_gemm_kernel<KIND, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+        cudaFuncSetAttribute(tc_gemm_kernel<KIND, BN, WT, AK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     }
-    dim3 grid((a.N + kTcTileF - 1) / kTcTileF, (a.R + BN - 1) / BN, splits);
-    tc_gemm_kernel<KIND, BN><<<grid, kThreads, C::SMEM, st>>>(w.hi, KIND == TC_TF32X3 ? w.lo : w.hi, x.hi[bn_idx],
-                                                            KIND == TC_TF32X3 ? x.lo[bn_idx] : x.hi[bn_idx], a);
+    dim3 grid((a.N + kTcTileF - 1) / kTcTileF, (a.R + BN - 1) / BN, a.splits);
+    tc_gemm_kernel<KIND, BN, WT, AK><<<grid, kThreads, C::SMEM, st>>>(w.hi, KIND == TC_TF32X3 ? w.lo : w.hi, x.hi[bn_idx],
+                                                                KIND == TC_TF32X3 ? x.lo[bn_idx] : x.hi[bn_idx], a);
 }
 
 }  // namespace
@@ -397,8 +411,22 @@ int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, in
     const unsigned bf = t ? 32 : 64, bk = t ? 32 : 64;
     w->K = K;
     w->N = N;
+    w->kmajor = false;
     int rc = tc_encode(&w->hi, dt, hi, N, K, bf, bk, t);
     if (!rc && t) rc = tc_encode(&w->lo, dt, lo, N, K, bf, bk, t);
+    if (!t) w->lo = w->hi;
+    return rc;
+}
+
+int tc_weights_kmajor(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N) {
+    const bool t = kind == TC_TF32X3;
+    const CUtensorMapDataType dt = t ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const unsigned bk = t ? 32 : 64;
+    w->K = K;
+    w->N = N;
+    w->kmajor = true;
+    int rc = tc_encode(&w->hi, dt, hi, K, N, bk, kTcTileF, false);
+    if (!rc && t) rc = tc_encode(&w->lo, dt, lo, K, N, bk, kTcTileF, false);
     if (!t) w->lo = w->hi;
     return rc;
 }
@@ -440,54 +468,71 @@ size_t tc_partial_floats(int R_max, int N, int K, int kind, int sms) {
 
 template <typename WT>
 int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, float *partial, size_t partial_floats,
-                   int *err, const WT *bias, const float *resid, float *out, int epi, const KVLayout *kv, int layer,
-                   Rows rows, int sms, cudaStream_t st) {
+                   unsigned *tile_ctr, int *err, const WT *bias, const float *resid, float *out, int epi,
+                   const KVLayout *kv, int layer, Rows rows, int sms, cudaStream_t st, OperandOut op, int out_stride) {
     const int bk = kind == TC_TF32X3 ? 32 : 64;
     const int kb_total = w.K / bk;
     TcPlan p = plan(R, w.N, kb_total, sms);
-    // fewer splits if the scratch is smaller than the plan needs (one split always fits R x N)
+    if (w.N % 4) {   // the reduce kernel works in float4s: no split-K (the LM head's 393 tiles need none)
+        p.splits = 1;
+        p.kb_per = kb_total;
+    }
+    // fewer splits if the scratch is smaller than the plan needs (one split needs none)
     while (p.splits > 1 && (size_t)p.splits * R * w.N > partial_floats) {
         p.kb_per = (kb_total + p.splits - 2) / (p.splits - 1);
         p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
     }
-    TcArgs a;
+    TcArgs<WT> a;
     a.N = w.N;
     a.R = R;
     a.kb_total = kb_total;
     a.kb_per = p.kb_per;
+    a.splits = p.splits;
     a.part = partial;
     a.err = err;
+    (void)tile_ctr;
+    a.e.bias = bias;
+    a.e.resid = resid;
+    a.e.out = out;
+    a.e.N = out_stride > 0 ? out_stride : w.N;   // row stride of out (and resid)
+    a.e.epi = epi;
+    if (kv) a.e.kv = *kv;
+    a.e.layer = layer;
+    a.e.pos = rows.pos;
+    a.e.slot = rows.slot;
+    a.e.E = w.N / 3;
+    a.op = op;
     const int bi = p.bn == 32 ? 0 : p.bn == 64 ? 1 : 2;
-    if (kind == TC_TF32X3) {
-        if (p.bn == 32) launch_kernel<TC_TF32X3, 32>(w, x, bi, a, p.splits, st);
-        else if (p.bn == 64) launch_kernel<TC_TF32X3, 64>(w, x, bi, a, p.splits, st);
-        else launch_kernel<TC_TF32X3, 128>(w, x, bi, a, p.splits, st);
+    if (w.kmajor) {   // the LM head (rows of wte): one row tile of 32 per launch suffices for batched steps
+        if (kind == TC_TF32X3) {
+            if (p.bn == 32) launch_kernel<TC_TF32X3, 32, WT, true>(w, x, bi, a, st);
+            else if (p.bn == 64) launch_kernel<TC_TF32X3, 64, WT, true>(w, x, bi, a, st);
+            else launch_kernel<TC_TF32X3, 128, WT, true>(w, x, bi, a, st);
+        } else {
+            if (p.bn == 32) launch_kernel<TC_F16, 32, WT, true>(w, x, bi, a, st);
+            else if (p.bn == 64) launch_kernel<TC_F16, 64, WT, true>(w, x, bi, a, st);
+            else launch_kernel<TC_F16, 128, WT, true>(w, x, bi, a, st);
+        }
+    } else if (kind == TC_TF32X3) {
+        if (p.bn == 32) launch_kernel<TC_TF32X3, 32, WT, false>(w, x, bi, a, st);
+        else if (p.bn == 64) launch_kernel<TC_TF32X3, 64, WT, false>(w, x, bi, a, st);
+        else launch_kernel<TC_TF32X3, 128, WT, false>(w, x, bi, a, st);
     } else {
-        if (p.bn == 32) launch_kernel<TC_F16, 32>(w, x, bi, a, p.splits, st);
-        else if (p.bn == 64) launch_kernel<TC_F16, 64>(w, x, bi, a, p.splits, st);
-        else launch_kernel<TC_F16, 128>(w, x, bi, a, p.splits, st);
+        if (p.bn == 32) launch_kernel<TC_F16, 32, WT, false>(w, x, bi, a, st);
+        else if (p.bn == 64) launch_kernel<TC_F16, 64, WT, false>(w, x, bi, a, st);
+        else launch_kernel<TC_F16, 128, WT, false>(w, x, bi, a, st);
     }
-    Epi<WT> e;
-    e.bias = bias;
-    e.resid = resid;
-    e.out = out;
-    e.N = w.N;
-    e.epi = epi;
-    if (kv) e.kv = *kv;
-    e.layer = layer;
-    e.pos = rows.pos;
-    e.slot = rows.slot;
-    e.E = w.N / 3;
+    if (p.splits == 1) return 1;   // the GEMM applied the epilogue itself
     const long long n4 = (long long)R * w.N / 4;
-    tc_reduce_kernel<WT><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(partial, p.splits, R, w.N, e);
+    tc_reduce_kernel<WT><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(partial, p.splits, R, w.N, a.e, op);
     return 2;
 }
 
-template int launch_tc_gemm<float>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, int *,
-                                   const float *, const float *, float *, int, const KVLayout *, int, Rows, int,
-                                   cudaStream_t);
-template int launch_tc_gemm<__half>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, int *,
-                                    const __half *, const float *, float *, int, const KVLayout *, int, Rows, int,
-                                    cudaStream_t);
+template int launch_tc_gemm<float>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, unsigned *,
+                                   int *, const float *, const float *, float *, int, const KVLayout *, int, Rows, int,
+                                   cudaStream_t, OperandOut, int);
+template int launch_tc_gemm<__half>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, unsigned *,
+                                    int *, const __half *, const float *, float *, int, const KVLayout *, int, Rows, int,
+                                    cudaStream_t, OperandOut, int);
 
 }  // namespace g2

@@ -31,8 +31,11 @@ int tc_encode(CUtensorMap *map, CUtensorMapDataType dt, const void *base, unsign
 struct TcWeights {
     CUtensorMap hi, lo;
     int K, N;
+    bool kmajor;   // false: [K][N] (Conv1D, feature-contiguous); true: [N][K] (rows of wte)
 };
 int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N);
+// The same for a [N][K] row-major weight (K-contiguous), e.g. the tied LM head wte.
+int tc_weights_kmajor(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N);
 
 // Activation operand X [R][K] (hi / lo fp32 copies, or fp16): maps for every
 // row-tile height the planner may pick.
@@ -50,13 +53,21 @@ void launch_tc_prep(int kind, const float *x, float *hi, float *lo, __half *h16,
 // N x K projection on `sms` SMs.
 size_t tc_partial_floats(int R_max, int N, int K, int kind, int sms);
 
-// out[r][n] = epilogue(sum_k X[r][k] W[k][n]) for r < R: the tensor-core pass
-// into `partial`, then an ordered split-K reduction with the epilogue
-// (bias / GELU / residual / K,V append of g2_device.cuh).  `err` receives an
+// Output tiles one GEMM may have (tile counters to allocate, zeroed).
+constexpr int kTcMaxTiles = 4096;
+
+// out[r][n] = epilogue(sum_k X[r][k] W[k][n]) for r < R (bias / GELU /
+// residual / K,V append of g2_device.cuh); `op` optionally also writes the
+// output as the next GEMM's operand.  With one K split the GEMM applies the
+// epilogue from tensor memory (one launch); with split-K the partials go to
+// `partial` and one kernel sums them in split order (two launches).
+// `tile_ctr` is reserved (kTcMaxTiles zeroed counters).  out_stride > 0 sets
+// the row stride of out and resid (else N).  `err` receives an
 // error code if a wait inside the kernel expires.  Returns the launch count.
 template <typename WT>
 int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, float *partial, size_t partial_floats,
-                   int *err, const WT *bias, const float *resid, float *out, int epi, const KVLayout *kv, int layer,
-                   Rows rows, int sms, cudaStream_t st);
+                   unsigned *tile_ctr, int *err, const WT *bias, const float *resid, float *out, int epi,
+                   const KVLayout *kv, int layer, Rows rows, int sms, cudaStream_t st, OperandOut op = OperandOut(),
+                   int out_stride = 0);
 
 }  // namespace g2
