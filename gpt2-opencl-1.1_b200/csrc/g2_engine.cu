@@ -115,19 +115,20 @@ struct g2_engine {
     long long launches = 0;
     // persistent B = 1 decode kernel (fp32)
     bool mega = false;
-    float *packed = nullptr;            // strip-packed projection weights
-    std::vector<long long> layer_off;   // [L][4] float offsets into packed
+    float *packed = nullptr;            // unit-packed projection weights
+    std::vector<long long> layer_off;   // [L][3] float offsets into packed (A, B, D units)
     long long *d_layer_off = nullptr;
     LayerPtrs *d_layers = nullptr;
-    unsigned long long *t_qkv = nullptr, *t_part = nullptr, *t_ha = nullptr, *t_hb = nullptr, *t_f = nullptr,
-                       *t_best = nullptr;
+    unsigned long long *t_qkv = nullptr, *t_best = nullptr;
+    unsigned long long *mega_acc = nullptr;   // [kMegaMaxSteps][L][2][E] accumulators
     int *d_err = nullptr;
     unsigned long long *d_trace = nullptr;   // phase trace, when G2_MEGA_TRACE names an output file
     std::string trace_path;
     unsigned mega_epoch = 0;
     int mega_inflight = 3;   // outstanding bulk copies per CTA (G2_MEGA_INFLIGHT overrides)
     int mega_grid = 0;
-    int mega_cw[4] = {0, 0, 0, 0};   // strip widths of qkv, proj, fc, fc2
+    int mega_cw[2] = {0, 0};   // strip widths of c_attn and c_fc
+    int mega_nq = 0;           // attn.c_proj column slices per head
     size_t mega_smem = 0;
     // tensor-core GEMMs of the many-row passes (prefill, batched decode)
     bool tc = false;
@@ -175,7 +176,7 @@ static void free_engine(g2_engine *e) {
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
     for (auto &kv : e->prefill_graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_lm_w, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f,
+    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_lm_w, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
                         e->t_best, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
                         e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
@@ -228,6 +229,39 @@ static void pack_strips(const float *W, const float *b, const float *g, const fl
                 for (int k = 0; k < K; ++k) cs += (double)o[(size_t)k * CW + cc];
             o[(size_t)K * CW + cc] = (float)acc;
             o[(size_t)(K + 1) * CW + cc] = (float)cs;
+        }
+    }
+}
+
+// Units of one layer for the persistent decode kernel, part q (0: A, 1: B,
+// 2: D; layout in g2_mega.h).  T holds the layer's twelve tensors in file
+// order: ln_1.w/b, c_attn.w/b, attn.c_proj.w/b, ln_2.w/b, c_fc.w/b,
+// mlp.c_proj.w/b (Conv1D [in][out]).  The projection biases of B and D are
+// not packed: the kernel adds them when it reads the accumulators.
+static void pack_mega_layer(const std::vector<float> *T, int E, int F, int NH, int cwq, int cwf, int nq, int q,
+                            std::vector<float> &out) {
+    if (q == 0) {
+        out.resize((size_t)mega_packed_a(E));
+        pack_strips(T[2].data(), T[3].data(), T[0].data(), T[1].data(), E, 3 * E, cwq, out.data());
+    } else if (q == 1) {
+        out.resize((size_t)mega_packed_b(E));
+        const int NB = E / nq;
+        const float *W = T[4].data();   // [E][E]
+        float *o = out.data();
+        for (int h = 0; h < NH; ++h)
+            for (int j = 0; j < nq; ++j)
+                for (int d = 0; d < 64; ++d)
+                    for (int n = 0; n < NB; ++n) *o++ = W[(size_t)(h * 64 + d) * E + j * NB + n];
+    } else {
+        out.resize((size_t)mega_packed_d(E, F));
+        std::vector<float> strips((size_t)(E + 2) * F);
+        pack_strips(T[8].data(), T[9].data(), T[6].data(), T[7].data(), E, F, cwf, strips.data());
+        const float *W2 = T[10].data();   // [F][E]
+        float *o = out.data();
+        for (int u = 0; u < F / cwf; ++u) {
+            const float *st = strips.data() + (size_t)u * (E + 2) * cwf;
+            o = std::copy(st, st + (size_t)(E + 2) * cwf, o);
+            o = std::copy(W2 + (size_t)u * cwf * E, W2 + (size_t)(u + 1) * cwf * E, o);
         }
     }
 }
@@ -292,17 +326,16 @@ static int load_weights(g2_engine *e, const std::string &dir) {
     cudaError_t r = cudaMalloc(&e->wbuf, bytes);
     if (r != cudaSuccess) return set_err(G2_ERR_OOM, "cudaMalloc weights (%zu bytes): %s", bytes, cudaGetErrorString(r));
     e->device_bytes += bytes;
-    // Strip-packed copy of the projections for the persistent decode kernel
-    // (pack_strips): each unit is one contiguous run of (K + 2) * CW floats.
+    // Unit-packed copy of the projections for the persistent decode kernel
+    // (pack_mega_layer): each unit is one contiguous run of floats.
     const int *cw = e->mega_cw;
     if (e->mega) {
-        e->layer_off.assign((size_t)c.n_layer * 4, 0);
+        e->layer_off.assign((size_t)c.n_layer * 3, 0);
         long long po = 0;
         for (int l = 0; l < c.n_layer; ++l) {
-            const long long sz[4] = {mega_packed_floats(E, 3 * E), mega_packed_floats(E, E), mega_packed_floats(E, F),
-                                     mega_packed_floats(F, E)};
-            for (int q = 0; q < 4; ++q) {
-                e->layer_off[(size_t)l * 4 + q] = po;
+            const long long sz[3] = {mega_packed_a(E), mega_packed_b(E), mega_packed_d(E, F)};
+            for (int q = 0; q < 3; ++q) {
+                e->layer_off[(size_t)l * 3 + q] = po;
                 po += (sz[q] + 63) / 64 * 64;
             }
         }
@@ -360,18 +393,9 @@ static int load_weights(g2_engine *e, const std::string &dir) {
             if (++layer_have == 12) {
                 const int l = atoi(it.name.c_str() + 2);   // "h.<l>.mlp.c_proj.bias"
                 const std::vector<float> *T = layer_t.data();
-                struct P {
-                    const std::vector<float> &w, &b;
-                    const float *g, *beta;
-                    int K, N, CW, ph;
-                } proj[4] = {{T[2], T[3], T[0].data(), T[1].data(), E, 3 * E, cw[0], 0},
-                             {T[4], T[5], nullptr, nullptr, E, E, cw[1], 1},
-                             {T[8], T[9], T[6].data(), T[7].data(), E, F, cw[2], 2},
-                             {T[10], T[11], nullptr, nullptr, F, E, cw[3], 3}};
-                for (const P &q : proj) {
-                    pk.resize((size_t)mega_packed_floats(q.K, q.N));
-                    pack_strips(q.w.data(), q.b.data(), q.g, q.beta, q.K, q.N, q.CW, pk.data());
-                    r = cudaMemcpy(e->packed + e->layer_off[(size_t)l * 4 + q.ph], pk.data(), pk.size() * 4,
+                for (int q = 0; q < 3; ++q) {
+                    pack_mega_layer(T, E, F, c.n_head, cw[0], cw[1], e->mega_nq, q, pk);
+                    r = cudaMemcpy(e->packed + e->layer_off[(size_t)l * 3 + q], pk.data(), pk.size() * 4,
                                    cudaMemcpyHostToDevice);
                     if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "upload packed layer %d: %s", l, cudaGetErrorString(r));
                 }
@@ -454,18 +478,19 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
         int coop = 0, optin = 0;
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-        const size_t smem = mega_smem_bytes(e->c.n_embd, e->c.ffn_dim);
+        const size_t smem = mega_smem_bytes(e->c.n_embd);
         const int G = e->sms, E = e->c.n_embd, F = e->c.ffn_dim;
         int *cw = e->mega_cw;
         cw[0] = mega_cw(3 * E, G);
-        cw[1] = mega_cw(E, G);
-        cw[2] = mega_cw(F, G);
-        cw[3] = mega_cw(E, G);
-        const bool widths = cw[0] && cw[1] && cw[2] && cw[3];
-        // residual values per CTA and phase must fit the kernel's 64-float buffer
-        const int res_c = widths ? (E / cw[1] + G - 1) / G * cw[1] : 0, res_e = widths ? (E / cw[3] + G - 1) / G * cw[3] : 0;
-        e->mega = dtype == G2_F32 && !(off && off[0] == '1') && coop && smem <= (size_t)optin && G <= 256 && widths &&
-                  E * 4 <= mega_slot_bytes() && res_c <= 64 && res_e <= 64;
+        cw[1] = mega_cw(F, G);
+        e->mega_nq = mega_nq(E);
+        if (const char *nq = getenv("G2_MEGA_NQ"))
+            if (mega_nq_ok(E, atoi(nq))) e->mega_nq = atoi(nq);
+        // every row (E floats) fits a ring slot, an E-wide block has at most one
+        // float4 group per consumer thread, and the context fits the score buffer
+        e->mega = dtype == G2_F32 && !(off && off[0] == '1') && coop && smem <= (size_t)optin && G <= 256 && cw[0] &&
+                  cw[1] && e->mega_nq && E * 4 <= mega_slot_bytes() && E / 4 <= 480 && e->c.n_ctx <= mega_max_keys() &&
+                  e->c.n_head * 64 == E;
         e->mega_smem = smem;
     }
     TRY(load_weights(e, model_dir));
@@ -549,10 +574,7 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
     e->dec_graph.assign(max_batch, nullptr);
     if (e->mega) {
         TRY(dalloc(e, &e->t_qkv, (size_t)3 * E));
-        TRY(dalloc(e, &e->t_part, (size_t)NH * 16 * 66));
-        TRY(dalloc(e, &e->t_ha, (size_t)E));
-        TRY(dalloc(e, &e->t_hb, (size_t)E));
-        TRY(dalloc(e, &e->t_f, (size_t)F));
+        TRY(dalloc(e, &e->mega_acc, (size_t)kMegaMaxSteps * c.n_layer * 2 * E));
         TRY(dalloc(e, &e->t_best, (size_t)4 * e->sms));
         TRY(dalloc(e, &e->d_err, 1));
         TRY(dalloc(e, &e->d_layer_off, e->layer_off.size()));
@@ -881,10 +903,8 @@ static int decode_graph(g2_engine *e, int slot, cudaGraphExec_t *out) {
 static int launch_mega(g2_engine *e, int slot, int n_steps) {
     const ModelConfig &c = e->c;
     if (e->mega_epoch > 0xF0000000u) {   // epochs are 32-bit: restart them on cleared buffers
-        unsigned long long *bufs[6] = {e->t_qkv, e->t_part, e->t_ha, e->t_hb, e->t_f, e->t_best};
-        const size_t n[6] = {(size_t)3 * c.n_embd, (size_t)c.n_head * 16 * 66, (size_t)c.n_embd, (size_t)c.n_embd,
-                             (size_t)c.ffn_dim, (size_t)4 * e->sms};
-        for (int i = 0; i < 6; ++i) CK(cudaMemsetAsync(bufs[i], 0, n[i] * 8, e->st));
+        CK(cudaMemsetAsync(e->t_qkv, 0, (size_t)3 * c.n_embd * 8, e->st));
+        CK(cudaMemsetAsync(e->t_best, 0, (size_t)4 * e->sms * 8, e->st));
         e->mega_epoch = 0;
     }
     MegaParams P;
@@ -894,7 +914,9 @@ static int launch_mega(g2_engine *e, int slot, int n_steps) {
     P.NH = c.n_head;
     P.V = c.vocab_size;
     P.max_seq = e->kv.max_seq;
-    for (int q = 0; q < 4; ++q) P.cw[q] = e->mega_cw[q];
+    P.cw_qkv = e->mega_cw[0];
+    P.cw_fc = e->mega_cw[1];
+    P.nq = e->mega_nq;
     P.lm_rows = mega_lm_rows(P.E);
     P.n_steps = n_steps;
     P.layer_stride = e->kv.layer_stride;
@@ -909,10 +931,7 @@ static int launch_mega(g2_engine *e, int slot, int n_steps) {
     P.kc = reinterpret_cast<float *>(e->kbuf) + (size_t)slot * e->kv.slot_stride;
     P.vc = reinterpret_cast<float *>(e->vbuf) + (size_t)slot * e->kv.slot_stride;
     P.t_qkv = e->t_qkv;
-    P.t_part = e->t_part;
-    P.t_ha = e->t_ha;
-    P.t_hb = e->t_hb;
-    P.t_f = e->t_f;
+    P.acc = e->mega_acc;
     P.t_best = e->t_best;
     P.logits = e->logits + (size_t)slot * c.padded_vocab;
     P.out_tokens = e->out_tokens + (size_t)slot * c.n_ctx;
@@ -921,12 +940,19 @@ static int launch_mega(g2_engine *e, int slot, int n_steps) {
     P.err = e->d_err;
     P.trace = e->d_trace;
     P.max_inflight = e->mega_inflight;
-    P.epoch0 = e->mega_epoch + 1;
-    e->mega_epoch += mega_epochs(c.n_layer, n_steps);
-    void *args[] = {&P};
-    CK(cudaLaunchCooperativeKernel(mega_kernel_ptr(), dim3(e->mega_grid), dim3(mega_threads()), args, e->mega_smem,
-                                   e->st));
-    e->launches += 1;
+    // launches of at most kMegaMaxSteps steps, each on zeroed accumulators
+    for (int done = 0; done < n_steps;) {
+        const int n = std::min(kMegaMaxSteps, n_steps - done);
+        CK(cudaMemsetAsync(e->mega_acc, 0, (size_t)n * c.n_layer * 2 * c.n_embd * 8, e->st));
+        P.n_steps = n;
+        P.epoch0 = e->mega_epoch + 1;
+        e->mega_epoch += mega_epochs(c.n_layer, n);
+        void *args[] = {&P};
+        CK(cudaLaunchCooperativeKernel(mega_kernel_ptr(), dim3(e->mega_grid), dim3(mega_threads()), args, e->mega_smem,
+                                       e->st));
+        e->launches += 1;
+        done += n;
+    }
     return G2_OK;
 }
 

@@ -6,38 +6,45 @@
 //
 // Structure (one CTA per SM; 15 consumer warps + 1 producer warp):
 //
-//  * Weights are repacked at load time into "units": a column strip of a
-//    projection over its full K (so no output needs a cross-CTA reduction),
-//    followed by a bias row and a column-sum row.  For qkv and fc the
-//    preceding LayerNorm's gamma and beta are folded in (W' = diag(gamma) W,
-//    b' = b + beta W), and the normalisation itself is applied after the
-//    products: LN(x) W' + b' = rstd (x W' - mean colsum(W')) + b'.  The strip
-//    width of each projection (4 to 32 columns) is the narrowest that gives
-//    every CTA at most one unit per phase.  LM-head units are 16-row blocks of
-//    wte.  Unit g of a step belongs to CTA g % gridDim.x, counting across all
-//    phases of the step, so the CTAs share each layer's bytes evenly.
-//  * The producer warp streams the CTA's units, in consumption order, through
-//    an 8-slot shared-memory ring with cp.async.bulk (mbarrier full/empty,
-//    L2 evict-first).  The stream is the same every step and waits on no
-//    activation, so it runs ahead across layer and token boundaries.
-//  * Activations move between CTAs as 64-bit words (epoch << 32 | float
-//    bits).  A consumer polls the vector it needs until every word carries the
-//    epoch of the producing phase: readiness costs one L2 round trip, with no
-//    grid barrier and no atomics.  A buffer is rewritten only after every
-//    reader of its previous contents has produced the outputs the rewrite
-//    depends on, so a reader never sees a newer epoch than it waits for.  The
-//    values a phase needs besides its input vector (residuals) are fetched in
-//    the same polling pass; nothing else on the critical path reads DRAM.
-//  * Per layer: A = LN1 + qkv + K/V append, B = attention per (head, 64-key
-//    chunk) with online-softmax partials (the current position's K/V come
-//    from the qkv vector itself), C = combine + proj + residual, D = LN2 +
-//    fc + GELU, E = fc2 + residual.  Then LN_f + LM head with a per-CTA
-//    argmax; every CTA reads all CTA partials and derives the next token.
-//    The K/V rows a step appends are read by later steps only; one fence pair
-//    per step at that exchange orders them.
-//  * Barriers per phase are few: a strip unit takes one, which also reduces
-//    the LayerNorm sums of x and x * x (double-buffered scratch; the summing
-//    threads finish the statistics and store the outputs).
+//  * A token is a chain of dependent cross-CTA exchanges; their latency, not
+//    HBM bandwidth, bounds B = 1 decode.  A layer takes three:
+//      A  LN1 + c_attn + K/V append      needs x (the residual stream)
+//      B  attention + attn.c_proj        needs q, k, v of one head
+//      D  LN2 + c_fc + GELU + mlp.c_proj needs x + attention output
+//    B and D compute their projection split over K: a B unit (head h, column
+//    slice j) runs the whole attention of head h (every unit of head h repeats
+//    it, reading the head's K/V rows from L2) and multiplies the head's 64
+//    outputs by rows 64h..64h+63 of attn.c_proj, slice j.  A D unit computes a
+//    strip of c_fc columns, applies GELU in shared memory and multiplies the
+//    strip by the same rows of mlp.c_proj, for all E outputs.  No unit waits
+//    for another unit's partial: the partial sums meet in an accumulator.
+//  * Accumulators are 64-bit words holding count * 2^55 + sum(round(v * 2^32))
+//    modulo 2^64.  A contribution is one red.add of 2^55 + round(v * 2^32).
+//    Integer addition is exact and order-independent, so the sum does not
+//    depend on timing, and the count field tells a reader when every
+//    contributor has added.  The representable range is |sum| < 2^22 (GPT-2
+//    activations stay orders of magnitude below it); a contribution is
+//    clamped to +-2^21.  Each accumulator vector is used once per launch (the
+//    host zeroes them before the launch).
+//  * Every CTA keeps the residual stream x in shared memory and applies the
+//    same update from the accumulators, x += acc + bias (add_inplace after
+//    the projection, math.cl:314), so all CTAs hold bit-identical copies.
+//  * A units are column strips of c_attn over the full K, followed by a bias
+//    row and a column-sum row.  LN1 (and LN2 in D) are folded in:
+//    W' = diag(gamma) W, b' = b + beta W, and LN(x) W' + b' =
+//    rstd (x W' - mean colsum(W')) + b', so the statistics are reduced in the
+//    same pass as the products.  q, k, v reach the B units as 64-bit words
+//    (epoch << 32 | float bits): readiness costs one L2 round trip.
+//  * LM-head units are 16-row blocks of wte.  Unit g of a layer belongs to CTA
+//    g % gridDim.x, counting A, then B, then D units; the LM-head units
+//    continue the count.  The producer warp streams the CTA's units, in
+//    consumption order, through an 8-slot shared-memory ring with
+//    cp.async.bulk (mbarrier full/empty, L2 evict-first).  The stream waits on
+//    no activation, so it runs ahead across layer and token boundaries.
+//  * Then LN_f + LM head with a per-CTA argmax; every CTA reads all CTA
+//    partials and derives the next token.  The K/V rows a step appends are
+//    read by later steps only; one fence pair per step at that exchange
+//    orders them.
 //  * Every wait is bounded (globaltimer, 2 s per wait).  On expiry the thread
 //    records an error code; the consumer warps leave together at the next
 //    uniform check, the producer stops issuing and drains its in-flight
@@ -59,8 +66,10 @@ constexpr int kSlots = 8;
 constexpr int kSlotBytes = 24832;          // 194 * 128: whole rows at every strip width (16 to 128 B)
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 constexpr int kConsBar = 1;                // named barrier of the consumer warps
-constexpr int kMaxChunks = 16;             // attention chunks per head (1024 / 64)
-constexpr int kRes = 64;                   // residual values a CTA prefetches per phase
+constexpr int kMaxKeys = 1024;             // attention keys (positions) per head
+constexpr int kKeysPerPass = kCons / 4;    // 4 threads per key in the score pass
+constexpr int kPvGroups = kCons / 16;      // key groups of the P.V pass (16 threads = 64 dims per key)
+constexpr int kPart = 2048;                // partial-sum scratch (floats)
 // Reduction scratch (floats): two alternating halves for strip units, then the
 // argmax partials, the attention scalars and the LayerNorm partials.
 constexpr int kRedHalf = 512;
@@ -70,6 +79,9 @@ constexpr int kRedLn = 1088;               // 32
 constexpr int kRedFloats = 1120;
 
 typedef unsigned long long u64;
+
+constexpr u64 kAccOne = 1ull << 55;        // one contribution in the count field
+constexpr float kAccMax = 2097152.0f;      // 2^21: clamp of one contribution
 
 __device__ __forceinline__ u64 gtime() {
     u64 t;
@@ -87,6 +99,19 @@ __device__ __forceinline__ void st_tag(u64 *p, float v, unsigned ep) {
 }
 __device__ __forceinline__ bool tag_is(u64 w, unsigned ep) { return (unsigned)(w >> 32) == ep; }
 __device__ __forceinline__ float tag_val(u64 w) { return __uint_as_float((unsigned)w); }
+
+// Accumulator words: count * 2^55 + sum of round(v * 2^32), modulo 2^64.
+__device__ __forceinline__ void acc_add(u64 *dst, float v) {
+    v = fminf(fmaxf(v, -kAccMax), kAccMax);
+    const long long q = __float2ll_rn(v * 4294967296.0f);   // exact scaling by 2^32, one rounding
+    const u64 c = kAccOne + (u64)q;
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(dst), "l"(c) : "memory");
+}
+__device__ __forceinline__ unsigned acc_count(u64 w) { return (unsigned)((w + (1ull << 54)) >> 55); }
+__device__ __forceinline__ float acc_value(u64 w, unsigned n) {
+    const long long s = (long long)(w - ((u64)n << 55));
+    return __ll2float_rn(s) * 2.3283064365386963e-10f;   // one rounding, then exact scaling by 2^-32
+}
 
 __device__ __forceinline__ void cons_sync() { asm volatile("bar.sync %0, %1;" ::"n"(kConsBar), "n"(kCons) : "memory"); }
 __device__ __forceinline__ int cons_and(int pred) {
@@ -137,6 +162,17 @@ __device__ __forceinline__ bool mbar_wait(u64 *b, unsigned parity) {
         if (gtime() > limit) return false;
     }
 }
+// The producer's wait: the same, sleeping between tries so that the waiting
+// warp leaves its scheduler's issue slots to the consumer warps.
+__device__ __forceinline__ bool mbar_wait_idle(u64 *b, unsigned parity) {
+    if (mbar_try(b, parity)) return true;
+    const u64 limit = gtime() + kTimeoutNs;
+    for (;;) {
+        __nanosleep(64);
+        if (mbar_try(b, parity)) return true;
+        if (gtime() > limit) return false;
+    }
+}
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned bytes, u64 *bar, u64 policy) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
@@ -161,34 +197,44 @@ __device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
 __device__ __forceinline__ float gelu_f(float v) {
     return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
 }
+__device__ __forceinline__ void fma4(float4 &acc, float x, const float4 &w) {
+    acc.x = fmaf(x, w.x, acc.x);
+    acc.y = fmaf(x, w.y, acc.y);
+    acc.z = fmaf(x, w.z, acc.z);
+    acc.w = fmaf(x, w.w, acc.w);
+}
 
 // ---- the per-step unit schedule (the same in producer and consumers) ------------------
 struct Sched {
-    int nA, nC, nD, nE, nLM;   // units per phase
-    int per_layer;             // nA + nC + nD + nE
-    int G;                     // CTAs
+    int nA, nB, nD, nLM;   // units per phase
+    int per_layer;         // nA + nB + nD
+    int G;                 // CTAs
     // first unit of a phase starting at global unit index g0 that belongs to CTA c
     __device__ __forceinline__ int first(int g0, int c) const {
         const int r = (c - g0) % G;
         return r < 0 ? r + G : r;
     }
-    __device__ __forceinline__ int count(int first, int n) const { return first < n ? (n - first + G - 1) / G : 0; }
+    __device__ __forceinline__ int a_first(int l, int c) const { return first(l * per_layer, c); }
+    __device__ __forceinline__ int b_first(int l, int c) const { return first(l * per_layer + nA, c); }
+    __device__ __forceinline__ int d_first(int l, int c) const { return first(l * per_layer + nA + nB, c); }
+    __device__ __forceinline__ int lm_first(int L, int c) const { return first(L * per_layer, c); }
 };
 
 struct Smem {
-    float *xs;     // input vector of the current phase (max(E, F) + 1 floats)
-    float *red;    // reduction scratch: 2 x [16 warps][16] unit partials, then [512,560) stats/ints
-    float *att;    // attention / argmax scratch (1024 floats)
-    float *res;    // residual values of this CTA's units (kRes floats)
-    float *lnf;    // final LayerNorm gamma [E] and beta [E]
+    float *xs;     // input vector of the current phase (E + 4 floats)
+    float *xres;   // the residual stream x (E floats)
+    float *red;    // reduction scratch (kRedFloats)
+    float *attp;   // attention scores, then probabilities (kMaxKeys)
+    float *attq;   // q, k, v of the head at pos (192)
+    float *atta;   // attention output of the head (64); GELU outputs of a D unit
+    float *part;   // partial sums of the P.V and block passes (kPart)
     u64 *trc;      // trace accumulators (thread 0 only)
     u64 *full, *empty;
     unsigned char *ring;
 };
 
-// Trace layout in shared memory (u64): [0..8) poll ns per phase, [8..16) work ns,
-// [16] chunk-wait ns, [18] units, [19] chunks, [20] phase-begin stamp, [21] inputs stamp,
-// [24] timeline count, [32..64) timeline stamps (CTA 0, step 0).
+// Trace layout in shared memory (u64): see g2_mega.h; [20] phase-begin stamp,
+// [21] inputs stamp, [24] timeline count, [32..64) timeline stamps (CTA 0, step 0).
 struct Cx {
     const MegaParams *p;
     Smem s;
@@ -246,22 +292,14 @@ __device__ __forceinline__ bool poll_expired(Cx &cx, unsigned round, u64 limit, 
     return false;
 }
 
-// Poll n tagged words into dst until all carry `ep`, together with the
-// residual words of this CTA's units (nunits units of cw columns, the first
-// unit index first, tagged res_ep) into cx.s.res.  All consumer threads.
-__device__ __forceinline__ bool poll_vec(Cx &cx, const u64 *src, float *dst, int n, unsigned ep,
-                                         const u64 *res_src = nullptr, int first = 0, int cw = 0, int nunits = 0,
-                                         unsigned res_ep = 0) {
+// Poll n tagged words into dst until all carry `ep`.  All consumer threads.
+__device__ __forceinline__ bool poll_vec(Cx &cx, const u64 *src, float *dst, int n, unsigned ep, int code) {
     const u64 limit = gtime() + kTimeoutNs;
-    const int G = gridDim.x;
-    const int nres = cw * nunits;
-    // bit j of `pending`: word ctid + j * kCons not yet seen with the right epoch
-    // (n <= 31 * kCons); bit 31: this thread's residual word
+    // bit j of `pending`: word ctid + j * kCons not yet seen with the right epoch (n <= 32 * kCons)
     unsigned pending = 0;
     for (int j = 0, i = cx.ctid; i < n; ++j, i += kCons) pending |= 1u << j;
-    if (cx.ctid < nres) pending |= 1u << 31;
     for (unsigned round = 0;; ++round) {
-        for (unsigned m = pending & 0x7fffffffu; m; m &= m - 1) {
+        for (unsigned m = pending; m; m &= m - 1) {
             const int j = __ffs(m) - 1, i = cx.ctid + j * kCons;
             const u64 w = ld_tag(src + i);
             if (tag_is(w, ep)) {
@@ -269,16 +307,31 @@ __device__ __forceinline__ bool poll_vec(Cx &cx, const u64 *src, float *dst, int
                 pending &= ~(1u << j);
             }
         }
-        if (pending >> 31) {
-            const int col = (first + (cx.ctid / cw) * G) * cw + cx.ctid % cw;
-            const u64 w = ld_tag(res_src + col);
-            if (tag_is(w, res_ep)) {
-                cx.s.res[cx.ctid] = tag_val(w);
-                pending &= 0x7fffffffu;
+        if (cons_and(pending == 0)) return true;
+        if (poll_expired(cx, round, limit, code)) return false;
+    }
+}
+
+// Poll the E accumulator words at src until each holds `expect` contributions,
+// then x[i] = x[i] + (acc[i] + bias[i]) in xres and xs.  All consumer threads.
+__device__ __forceinline__ bool poll_acc(Cx &cx, const u64 *src, unsigned expect, const float *bias, int E, int code) {
+    const u64 limit = gtime() + kTimeoutNs;
+    unsigned pending = 0;
+    for (int j = 0, i = cx.ctid; i < E; ++j, i += kCons) pending |= 1u << j;
+    for (unsigned round = 0;; ++round) {
+        for (unsigned m = pending; m; m &= m - 1) {
+            const int j = __ffs(m) - 1, i = cx.ctid + j * kCons;
+            const u64 w = ld_tag(src + i);
+            const unsigned n = acc_count(w);
+            if (n == expect) {
+                const float x = cx.s.xres[i] + (acc_value(w, n) + __ldg(bias + i));
+                cx.s.xres[i] = x;
+                cx.s.xs[i] = x;
+                pending &= ~(1u << j);
             }
         }
         if (cons_and(pending == 0)) return true;
-        if (poll_expired(cx, round, limit, 2)) return false;
+        if (poll_expired(cx, round, limit, code)) return false;
     }
 }
 
@@ -323,11 +376,11 @@ __device__ __forceinline__ void ln_stats(Cx &cx, int n, float &mean, float &rstd
     ln_finish(S, Q, n, mean, rstd);
 }
 
-// Next ring chunk (waits for its bytes).  On an expired wait the thread is
-// marked failed and computes on whatever the slot holds; the phase's uniform
-// check discards the result.
-__device__ __forceinline__ const float *chunk_begin(Cx &cx) {
-    const unsigned slot = cx.chunk_i % kSlots, par = (cx.chunk_i / kSlots) & 1u;
+// Ring chunk cx.chunk_i + k (waits for its bytes).  On an expired wait the
+// thread is marked failed and computes on whatever the slot holds; the
+// phase's uniform check discards the result.
+__device__ __forceinline__ const float4 *chunk_wait(Cx &cx, unsigned k = 0) {
+    const unsigned i = cx.chunk_i + k, slot = i % kSlots, par = (i / kSlots) & 1u;
     if (cx.tr) {
         const u64 t = gtime();
         if (!mbar_wait(&cx.s.full[slot], par)) fail(cx, 4);
@@ -336,187 +389,417 @@ __device__ __forceinline__ const float *chunk_begin(Cx &cx) {
     } else if (!mbar_wait(&cx.s.full[slot], par)) {
         fail(cx, 4);
     }
-    return reinterpret_cast<const float *>(cx.s.ring + (size_t)slot * kSlotBytes);
+    return reinterpret_cast<const float4 *>(cx.s.ring + (size_t)slot * kSlotBytes);
 }
-__device__ __forceinline__ void chunk_end(Cx &cx) {
+// Release the next n chunks to the producer (each consumer warp arrives once).
+__device__ __forceinline__ void chunk_done(Cx &cx, unsigned n = 1) {
     __syncwarp();
-    if (cx.lane == 0) mbar_arrive(&cx.s.empty[cx.chunk_i % kSlots]);
-    ++cx.chunk_i;
+    if (cx.lane == 0)
+        for (unsigned k = 0; k < n; ++k) mbar_arrive(&cx.s.empty[(cx.chunk_i + k) % kSlots]);
+    cx.chunk_i += n;
 }
 
 // One strip unit of K weight rows plus its bias row and column-sum row, for
-// its cw columns (4, 8, 16 or 32).  Without LayerNorm it returns
-// y = xs . W + b; with `ln` the input is normalised implicitly,
-// y = rstd * (xs . W' - mean * colsum(W')) + b', so that the statistics are
-// reduced in the same pass as the products (one barrier for the whole unit).
-// The result is in threads ctid < cw.  Every row of a chunk is loaded before
-// any product (four rows per thread and chunk cover a slot at every width).
-// The width is a run-time value so that every phase runs this one copy of the
-// code (it stays in the instruction cache across phases).
-__device__ __forceinline__ float strip_unit(Cx &cx, int K, int cw, bool ln) {
+// its cw columns (4, 8, 16 or 32), with the LayerNorm folded in:
+// y = rstd * (xs . W' - mean * colsum(W')) + b', the statistics reduced in the
+// same pass as the products (one barrier for the whole unit).  The result is
+// in threads ctid < cw.  Thread (rg, cg) = (ctid / CG, ctid % CG) takes rows
+// rg + i RG (i < 3, and i = 3 where the chunk has it) of float4 column group
+// cg: in a chunk of RPC rows its weights are float4s ctid + i kCons (3 RG <=
+// RPC <= 4 RG at every width).  Chunks of weight rows only are taken two at a
+// time without masks; the chunk with the bias and column-sum rows is masked.
+__device__ __forceinline__ float strip_unit(Cx &cx, int K, int cw) {
     const int lg = cw == 32 ? 3 : cw == 16 ? 2 : cw == 8 ? 1 : 0;   // log2 of the float4 column groups
-    const int CG = 1 << lg, RG = kCons >> lg;
-    const int RPC = kSlotBytes / (cw * 4);          // rows per chunk; RPC <= 4 * RG
-    const int cg = cx.ctid & (CG - 1), rg = cx.ctid >> lg;
+    const int RG = kCons >> lg;
+    const int RPC = kSlotBytes / (cw * 4);          // rows per chunk
+    const int rg = cx.ctid >> lg, t = cx.ctid;
     const int rows = K + 2;
+    const bool has4 = rg + 3 * RG < RPC;
     const float *xs = cx.s.xs;
-    long long c0 = cx.tr ? clock64() : 0;
-    float s = 0.0f, q = 0.0f;
-    if (ln) ln_sums(cx, K, s, q);
-    if (cx.tr) {
-        const long long c = clock64();
-        cx.s.trc[22] += c - c0;
-        c0 = c;
-    }
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float s, q;
+    ln_sums(cx, K, s, q);
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
     float bias = 0.0f, csum = 0.0f;
-    for (int r0 = 0; r0 < rows; r0 += RPC) {
-        const float *ch = chunk_begin(cx);
-        const float4 *w4 = reinterpret_cast<const float4 *>(ch);
+    const int nfull = K / RPC;   // chunks of weight rows only
+    int c = 0, r0 = 0;
+    for (; c + 1 < nfull; c += 2, r0 += 2 * RPC) {
+        const float4 *w = chunk_wait(cx, 0), *v = chunk_wait(cx, 1);
+        const float *x = xs + r0 + rg, *y = x + RPC;
+        float4 w0 = w[t], w1 = w[t + kCons], w2 = w[t + 2 * kCons], w3 = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 v0 = v[t], v1 = v[t + kCons], v2 = v[t + 2 * kCons], v3 = w3;
+        float x3 = 0.0f, y3 = 0.0f;
+        if (has4) {
+            w3 = w[t + 3 * kCons];
+            v3 = v[t + 3 * kCons];
+            x3 = x[3 * RG];
+            y3 = y[3 * RG];
+        }
+        fma4(a0, x[0], w0);
+        fma4(a1, x[RG], w1);
+        fma4(a0, x[2 * RG], w2);
+        fma4(a1, x3, w3);
+        fma4(a0, y[0], v0);
+        fma4(a1, y[RG], v1);
+        fma4(a0, y[2 * RG], v2);
+        fma4(a1, y3, v3);
+        chunk_done(cx, 2);
+    }
+    for (; r0 < rows; r0 += RPC) {
+        const float4 *w = chunk_wait(cx);
         const int nr = min(RPC, rows - r0);
-        float xv[4];
-        float4 w[4];
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-            const int r = min(rg + it * RG, nr - 1);   // in this chunk's rows; masked below
-            xv[it] = xs[r0 + r];                       // r0 + r <= K + 1 < size of xs
-            w[it] = w4[(r << lg) + cg];
-        }
-        if (cx.ctid < cw) {   // the bias and column-sum rows (possibly in different chunks)
-            if (K >= r0 && K < r0 + nr) bias = ch[(K - r0) * cw + cx.ctid];
-            if (K + 1 >= r0 && K + 1 < r0 + nr) csum = ch[(K + 1 - r0) * cw + cx.ctid];
-        }
 #pragma unroll
         for (int it = 0; it < 4; ++it) {
             const int r = rg + it * RG;
-            const bool in = r < nr && r0 + r < K;
-            const float x = in ? xv[it] : 0.0f;
-            const float4 ww = in ? w[it] : make_float4(0.f, 0.f, 0.f, 0.f);
-            acc.x = fmaf(x, ww.x, acc.x);
-            acc.y = fmaf(x, ww.y, acc.y);
-            acc.z = fmaf(x, ww.z, acc.z);
-            acc.w = fmaf(x, ww.w, acc.w);
+            if (r < nr && r0 + r < K) fma4(it & 1 ? a1 : a0, xs[r0 + r], w[t + it * kCons]);
         }
-        chunk_end(cx);
+        if (t < cw) {   // the bias and column-sum rows (possibly in different chunks)
+            const float *ch = reinterpret_cast<const float *>(w);
+            if (K >= r0 && K < r0 + nr) bias = ch[(K - r0) * cw + t];
+            if (K + 1 >= r0 && K + 1 < r0 + nr) csum = ch[(K + 1 - r0) * cw + t];
+        }
+        chunk_done(cx);
     }
-    if (cx.tr) {
-        const long long c = clock64();
-        cx.s.trc[23] += c - c0;
-        c0 = c;
-    }
+    float4 acc = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
     // lanes with equal lane % CG hold the same columns: reduce within the warp, then across warps
-    for (int o = CG; o < 32; o <<= 1) {
+    for (int o = 1 << lg; o < 32; o <<= 1) {
         acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
         acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
         acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
         acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
     }
-    if (ln) {
-        s = warp_sum(s);
-        q = warp_sum(q);
-    }
+    s = warp_sum(s);
+    q = warp_sum(q);
     float *red = cx.s.red + (cx.upar & 1) * kRedHalf;   // [warp][32] products, then [480 + 2 warp] sums
     cx.upar ^= 1u;
-    if (cx.lane < CG) reinterpret_cast<float4 *>(red)[cx.warp * 8 + cx.lane] = acc;
-    if (ln && cx.lane == 0) {
+    if (cx.lane < (1 << lg)) reinterpret_cast<float4 *>(red)[cx.warp * 8 + cx.lane] = acc;
+    if (cx.lane == 0) {
         red[480 + 2 * cx.warp] = s;
         red[481 + 2 * cx.warp] = q;
     }
     cons_sync();
     float y = 0.0f;
-    if (cx.ctid < cw) {
-        float t[kWarps];
+    if (t < cw) {
+        float tt[kWarps];
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) t[w] = red[w * 32 + cx.ctid];
+        for (int w = 0; w < kWarps; ++w) tt[w] = red[w * 32 + t];
 #pragma unroll
         for (int st = 1; st < kWarps; st <<= 1)
 #pragma unroll
-            for (int w = 0; w + st < kWarps; w += 2 * st) t[w] += t[w + st];
-        if (ln) {
-            float S = 0.0f, Q = 0.0f;
+            for (int w = 0; w + st < kWarps; w += 2 * st) tt[w] += tt[w + st];
+        float S = 0.0f, Q = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                S += red[480 + 2 * w];
-                Q += red[481 + 2 * w];
-            }
-            float mean, rstd;
-            ln_finish(S, Q, K, mean, rstd);
-            y = fmaf(rstd, fmaf(-mean, csum, t[0]), bias);
-        } else {
-            y = t[0] + bias;
+        for (int w = 0; w < kWarps; ++w) {
+            S += red[480 + 2 * w];
+            Q += red[481 + 2 * w];
         }
-    }
-    if (cx.tr) {
-        cx.s.trc[25] += clock64() - c0;
-        cx.s.trc[27] += 1;
+        float mean, rstd;
+        ln_finish(S, Q, K, mean, rstd);
+        y = fmaf(rstd, fmaf(-mean, csum, tt[0]), bias);
     }
     return y;
+}
+
+// One row block: y[n] = sum_r a[r] W[r][n] for `rows` rows of NB floats
+// streamed from the ring (NB a multiple of 4, NB / 4 <= kCons, NB * 4 <=
+// kSlotBytes), each y[n] added to the accumulator word dst[n].  Thread
+// (rg, cg) = (ctid / CG, ctid % CG) sums rows rg, rg + RG, ... of float4
+// column group cg (float4s ctid, ctid + RG CG, ... of a chunk); the RG
+// partials are then added in a fixed order.  a is in shared memory.
+__device__ __forceinline__ void block_unit(Cx &cx, const float *a, int rows, int NB, u64 *dst) {
+    const int CG = NB >> 2, RG = kCons / CG, RGCG = RG * CG;
+    const int t = cx.ctid, rg = t / CG;
+    const bool act = t < RGCG;
+    const int RPC = kSlotBytes / (NB * 4);   // rows per chunk
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    for (int r0 = 0; r0 < rows; r0 += RPC) {
+        const float4 *w = chunk_wait(cx);
+        const int nr = min(RPC, rows - r0);
+        if (act) {
+            const float *ar = a + r0 + rg;
+            int k = 0;
+            for (; rg + (k + 3) * RG < nr; k += 4) {   // four rows in flight
+                const float4 w0 = w[t + k * RGCG], w1 = w[t + (k + 1) * RGCG], w2 = w[t + (k + 2) * RGCG],
+                             w3 = w[t + (k + 3) * RGCG];
+                fma4(a0, ar[k * RG], w0);
+                fma4(a1, ar[(k + 1) * RG], w1);
+                fma4(a0, ar[(k + 2) * RG], w2);
+                fma4(a1, ar[(k + 3) * RG], w3);
+            }
+            for (; rg + k * RG < nr; ++k) fma4(k & 1 ? a1 : a0, ar[k * RG], w[t + k * RGCG]);
+        }
+        chunk_done(cx);
+    }
+    float *part = cx.s.part;   // [RG][NB], RG * NB <= 4 * kCons <= kPart
+    if (act) reinterpret_cast<float4 *>(part)[t] = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
+    cons_sync();
+    for (int n = t; n < NB; n += kCons) {
+        float y = part[n];
+        for (int g = 1; g < RG; ++g) y += part[g * NB + n];
+        acc_add(dst + n, y);
+    }
 }
 
 __device__ __forceinline__ unsigned epoch_of(const MegaParams &p, int step, int layer, int ph) {
     return p.epoch0 + (unsigned)step * (unsigned)((p.L + 1) * 8) + (unsigned)(layer * 8 + ph);
 }
+// Accumulator vector of layer l in step `step`: w = 0 after B (attention
+// projection), w = 1 after D (MLP projection).
+__device__ __forceinline__ u64 *acc_of(const MegaParams &p, int step, int l, int w) {
+    return p.acc + ((size_t)step * 2 * p.L + 2 * l + w) * p.E;
+}
 
 // ---- producer: the CTA's weight stream for all steps ------------------------------------
+// Streams `bytes` from src in whole rows of row_bytes per ring chunk.
+__device__ __forceinline__ bool produce(Cx &cx, const char *src, size_t bytes, size_t row_bytes, unsigned &i,
+                                        u64 policy) {
+    const MegaParams &p = *cx.p;
+    const size_t chunk = (kSlotBytes / row_bytes) * row_bytes;
+    for (size_t off = 0; off < bytes; off += chunk) {
+        const unsigned nb = (unsigned)(bytes - off < chunk ? bytes - off : chunk);
+        const unsigned slot = i % kSlots;
+        if (!mbar_wait_idle(&cx.s.empty[slot], ((i / kSlots) & 1u) ^ 1u)) {
+            fail(cx, 1);
+            return false;
+        }
+        // Keep at most max_inflight copies outstanding.
+        if (i >= (unsigned)p.max_inflight) {
+            const unsigned j = i - p.max_inflight;
+            if (!mbar_wait_idle(&cx.s.full[j % kSlots], (j / kSlots) & 1u)) {
+                fail(cx, 1);
+                return false;
+            }
+        }
+        mbar_expect_tx(&cx.s.full[slot], nb);
+        bulk_load(cx.s.ring + (size_t)slot * kSlotBytes, src + off, nb, &cx.s.full[slot], policy);
+        ++i;
+    }
+    return true;
+}
+
 __device__ __forceinline__ void producer(Cx &cx, const Sched &S) {
     const MegaParams &p = *cx.p;
     u64 policy;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-    const int E = p.E, F = p.F, L = p.L, G = S.G;
+    const int E = p.E, L = p.L, G = S.G, cwq = p.cw_qkv, cwf = p.cw_fc, NB = E / p.nq;
+    const size_t ua = (size_t)(E + 2) * cwq * 4, ub = (size_t)64 * NB * 4;
+    const size_t ud_strip = (size_t)(E + 2) * cwf * 4, ud_block = (size_t)cwf * E * 4;
     unsigned i = 0;
     bool ok = true;
     for (int step = 0; step < p.n_steps && ok; ++step) {
-        for (int l = 0; l <= L && ok; ++l) {
-            const int nph = l < L ? 4 : 1;
-            for (int ph = 0; ph < nph && ok; ++ph) {
-                int g0, n;
-                const char *base;
-                size_t ubytes, row_bytes;
-                if (l < L) {
-                    g0 = l * S.per_layer + (ph > 0 ? S.nA : 0) + (ph > 1 ? S.nC : 0) + (ph > 2 ? S.nD : 0);
-                    n = ph == 0 ? S.nA : ph == 1 ? S.nC : ph == 2 ? S.nD : S.nE;
-                    base = reinterpret_cast<const char *>(p.packed + p.layer_off[l * 4 + ph]);
-                    ubytes = (size_t)((ph == 3 ? F : E) + 2) * p.cw[ph] * sizeof(float);
-                    row_bytes = (size_t)p.cw[ph] * sizeof(float);
-                } else {
-                    g0 = L * S.per_layer;
-                    n = S.nLM;
-                    base = reinterpret_cast<const char *>(p.lm);
-                    ubytes = (size_t)p.lm_rows * E * sizeof(float);
-                    row_bytes = (size_t)E * sizeof(float);
-                }
-                const size_t chunk = (kSlotBytes / row_bytes) * row_bytes;
-                for (int u = S.first(g0, cx.cta); u < n && ok; u += G) {
-                    const char *src = base + (size_t)u * ubytes;
-                    size_t bytes = ubytes;
-                    if (l == L) bytes = (size_t)min(p.lm_rows, p.V - u * p.lm_rows) * E * sizeof(float);
-                    for (size_t off = 0; off < bytes; off += chunk) {
-                        const unsigned nb = (unsigned)(bytes - off < chunk ? bytes - off : chunk);
-                        const unsigned slot = i % kSlots;
-                        if (!mbar_wait(&cx.s.empty[slot], ((i / kSlots) & 1u) ^ 1u)) {
-                            fail(cx, 1);
-                            ok = false;
-                            break;
-                        }
-                        // Keep at most max_inflight copies outstanding.
-                        if (i >= (unsigned)p.max_inflight) {
-                            const unsigned j = i - p.max_inflight;
-                            if (!mbar_wait(&cx.s.full[j % kSlots], (j / kSlots) & 1u)) {
-                                fail(cx, 1);
-                                ok = false;
-                                break;
-                            }
-                        }
-                        mbar_expect_tx(&cx.s.full[slot], nb);
-                        bulk_load(cx.s.ring + (size_t)slot * kSlotBytes, src + off, nb, &cx.s.full[slot], policy);
-                        ++i;
-                    }
-                }
+        for (int l = 0; l < L && ok; ++l) {
+            const char *pa = reinterpret_cast<const char *>(p.packed + p.layer_off[l * 3 + 0]);
+            const char *pb = reinterpret_cast<const char *>(p.packed + p.layer_off[l * 3 + 1]);
+            const char *pd = reinterpret_cast<const char *>(p.packed + p.layer_off[l * 3 + 2]);
+            for (int u = S.a_first(l, cx.cta); u < S.nA && ok; u += G) ok = produce(cx, pa + u * ua, ua, cwq * 4, i, policy);
+            for (int u = S.b_first(l, cx.cta); u < S.nB && ok; u += G)
+                ok = produce(cx, pb + u * ub, ub, (size_t)NB * 4, i, policy);
+            for (int u = S.d_first(l, cx.cta); u < S.nD && ok; u += G) {
+                const char *src = pd + u * (ud_strip + ud_block);
+                ok = produce(cx, src, ud_strip, cwf * 4, i, policy) &&
+                     produce(cx, src + ud_strip, ud_block, (size_t)E * 4, i, policy);
             }
+        }
+        const char *lm = reinterpret_cast<const char *>(p.lm);
+        for (int u = S.lm_first(L, cx.cta); u < S.nLM && ok; u += G) {
+            const size_t bytes = (size_t)min(p.lm_rows, p.V - u * p.lm_rows) * E * sizeof(float);
+            ok = produce(cx, lm + (size_t)u * p.lm_rows * E * sizeof(float), bytes, (size_t)E * 4, i, policy);
         }
     }
     // Every copy issued must land before the CTA may exit (the ring is its destination).
     for (unsigned j = i > kSlots ? i - kSlots : 0; j < i; ++j) mbar_wait(&cx.s.full[j % kSlots], (j / kSlots) & 1u);
+}
+
+// ---- consumer phases --------------------------------------------------------------------
+
+// A: LN1 + c_attn strips -> tagged qkv words; K and V columns also appended
+// to the cache at pos (split_kv, math.cl:367-383).  x is in xs.
+__device__ __forceinline__ bool phase_A(Cx &cx, const Sched &S, int step, int l, int pos) {
+    const MegaParams &p = *cx.p;
+    const int E = p.E, cw = p.cw_qkv;
+    const unsigned ep = epoch_of(p, step, l, 0);
+    tr_begin(cx);
+    tr_inputs(cx, 0);
+    for (int u = S.a_first(l, cx.cta); u < S.nA; u += S.G) {
+        const float v = strip_unit(cx, E, cw);
+        if (cx.ctid < cw) {
+            const int col = u * cw + cx.ctid;
+            if (col >= E) {   // K or V of head m / 64
+                int m = col - E;
+                float *kv = m >= E ? p.vc : p.kc;
+                if (m >= E) m -= E;
+                kv[(size_t)l * p.layer_stride + ((size_t)(m >> 6) * p.max_seq + pos) * 64 + (m & 63)] = v;
+            }
+            st_tag(p.t_qkv + col, v, ep);
+        }
+        if (cx.tr) cx.s.trc[18] += 1;
+    }
+    const bool ok = cons_and(!cx.failed);
+    tr_end(cx, 0);
+    return ok;
+}
+
+// B: for each (head h, column slice j) unit of this CTA, single-query
+// attention of head h over positions 0..pos (attn_scores_1q, attn_softmax_1q,
+// attn_out_1q, math.cl:388-476), then its 64 outputs times rows 64h..64h+63
+// of attn.c_proj, columns j * NB .. j * NB + NB - 1, into the accumulator.
+// The cached keys and values are read from the cache (L2); the first pass of
+// keys is loaded before the wait for q.  The key and value at pos come from
+// the qkv vector.
+__device__ __forceinline__ bool phase_B(Cx &cx, const Sched &S, int step, int l, int pos) {
+    const MegaParams &p = *cx.p;
+    const int E = p.E, NQ = p.nq, NB = E / NQ, T = pos + 1;
+    const unsigned ep_in = epoch_of(p, step, l, 0);
+    float *q = cx.s.attq, *pr = cx.s.attp, *a = cx.s.atta, *part = cx.s.part;
+    float *rb = cx.s.red + kRedAtt;   // [0, 15) warp maxima, [16, 31) warp sums
+    u64 *acc = acc_of(p, step, l, 0);
+    const int key = cx.ctid >> 2, k4 = cx.ctid & 3;   // score pass: 4 threads per key, 16 dims each
+    const int dq = cx.ctid & 15, grp = cx.ctid >> 4;  // P.V pass: float4 dq of 64 dims, key group grp
+    for (int b = S.b_first(l, cx.cta); b < S.nB; b += S.G) {
+        const int h = b / NQ, jq = b % NQ;
+        tr_begin(cx);
+        const size_t hb = (size_t)l * p.layer_stride + (size_t)h * p.max_seq * 64;
+        const float4 *K4 = reinterpret_cast<const float4 *>(p.kc + hb);
+        const float4 *V4 = reinterpret_cast<const float4 *>(p.vc + hb);
+        float4 kr[4];
+        {
+            const bool c = key < T && key != pos;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) kr[t] = c ? K4[(size_t)key * 16 + k4 * 4 + t] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        {   // q, k, v of head h at pos
+            const u64 limit = gtime() + kTimeoutNs;
+            bool pend = cx.ctid < 192;
+            for (unsigned round = 0;; ++round) {
+                if (pend) {
+                    const u64 w = ld_tag(p.t_qkv + (cx.ctid >> 6) * E + h * 64 + (cx.ctid & 63));
+                    if (tag_is(w, ep_in)) {
+                        q[cx.ctid] = tag_val(w);
+                        pend = false;
+                    }
+                }
+                if (cons_and(!pend)) break;
+                if (poll_expired(cx, round, limit, 5)) return false;
+            }
+        }
+        tr_inputs(cx, 1);
+        const long long c0 = cx.tr ? clock64() : 0;
+        // scores s_j = q . k_j / 8 (the key at pos comes from the qkv vector)
+        float mloc = -FLT_MAX;
+        for (int j0 = 0; j0 < T; j0 += kKeysPerPass) {
+            const int j = j0 + key;
+            if (j0 > 0) {
+                const bool c = j < T && j != pos;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) kr[t] = c ? K4[(size_t)j * 16 + k4 * 4 + t] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (j == pos) {
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    kr[t] = make_float4(q[64 + k4 * 16 + 4 * t], q[64 + k4 * 16 + 4 * t + 1], q[64 + k4 * 16 + 4 * t + 2],
+                                        q[64 + k4 * 16 + 4 * t + 3]);
+            }
+            const float *qq = q + k4 * 16;
+            float s = 0.0f;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                s = fmaf(kr[t].x, qq[4 * t], s);
+                s = fmaf(kr[t].y, qq[4 * t + 1], s);
+                s = fmaf(kr[t].z, qq[4 * t + 2], s);
+                s = fmaf(kr[t].w, qq[4 * t + 3], s);
+            }
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            s *= 0.125f;   // 1 / sqrt(64)
+            if (j < T) {
+                if (k4 == 0) pr[j] = s;
+                mloc = fmaxf(mloc, s);
+            }
+        }
+        float m = warp_max(mloc);
+        if (cx.lane == 0) rb[cx.warp] = m;
+        cons_sync();
+        m = rb[0];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) m = fmaxf(m, rb[w]);
+        float lsum = 0.0f;
+        for (int j = cx.ctid; j < T; j += kCons) {
+            const float e = expf(pr[j] - m);
+            pr[j] = e;
+            lsum += e;
+        }
+        lsum = warp_sum(lsum);
+        if (cx.lane == 0) rb[16 + cx.warp] = lsum;
+        cons_sync();
+        float Lt = rb[16];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) Lt += rb[16 + w];
+        // P.V: thread (grp, dq) sums keys grp, grp + kPvGroups, ... of dims 4 dq .. 4 dq + 3
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j0 = grp; j0 < T; j0 += 4 * kPvGroups) {
+            float4 vv[4];
+            float pp[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = j0 + u * kPvGroups;
+                const bool in = j < T;
+                vv[u] = (in && j != pos) ? V4[(size_t)j * 16 + dq] : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (j == pos)
+                    vv[u] = make_float4(q[128 + 4 * dq], q[128 + 4 * dq + 1], q[128 + 4 * dq + 2], q[128 + 4 * dq + 3]);
+                pp[u] = in ? pr[j] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) fma4(o, pp[u], vv[u]);
+        }
+        reinterpret_cast<float4 *>(part)[grp * 16 + dq] = o;   // [kPvGroups][64]
+        cons_sync();
+        if (cx.ctid < 64) {
+            float y = part[cx.ctid];
+            for (int g = 1; g < kPvGroups; ++g) y += part[g * 64 + cx.ctid];
+            a[cx.ctid] = y / Lt;
+        }
+        cons_sync();
+        const long long c1 = cx.tr ? clock64() : 0;
+        block_unit(cx, a, 64, NB, acc + jq * NB);
+        if (cx.tr) {
+            cx.s.trc[18] += 1;
+            cx.s.trc[26] += c1 - c0;
+            cx.s.trc[27] += clock64() - c1;
+            cx.s.trc[28] += 1;
+        }
+        const bool ok = cons_and(!cx.failed);
+        tr_end(cx, 1);
+        if (!ok) return false;
+    }
+    return true;
+}
+
+// D: x' is in xs.  For each unit: LN2 + c_fc strip of cw columns, GELU
+// (math.cl:21-23), then those cw values times the matching cw rows of
+// mlp.c_proj (all E outputs) into the accumulator.
+__device__ __forceinline__ bool phase_D(Cx &cx, const Sched &S, int step, int l) {
+    const MegaParams &p = *cx.p;
+    const int E = p.E, cw = p.cw_fc;
+    u64 *acc = acc_of(p, step, l, 1);
+    float *gv = cx.s.atta;
+    tr_begin(cx);
+    tr_inputs(cx, 3);
+    for (int u = S.d_first(l, cx.cta); u < S.nD; u += S.G) {
+        const long long c0 = cx.tr ? clock64() : 0;
+        const float v = strip_unit(cx, E, cw);
+        if (cx.ctid < cw) gv[cx.ctid] = gelu_f(v);
+        cons_sync();
+        const long long c1 = cx.tr ? clock64() : 0;
+        block_unit(cx, gv, cw, E, acc);
+        if (cx.tr) {
+            cx.s.trc[18] += 1;
+            cx.s.trc[22] += c1 - c0;
+            cx.s.trc[23] += clock64() - c1;
+            cx.s.trc[25] += 1;
+        }
+    }
+    const bool ok = cons_and(!cx.failed);
+    tr_end(cx, 3);
+    return ok;
 }
 
 }  // namespace
@@ -529,14 +812,14 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     cx.cta = blockIdx.x;
     cx.warp = threadIdx.x >> 5;
     cx.lane = threadIdx.x & 31;
-    cx.ctid = threadIdx.x;   // consumers: 0..511
+    cx.ctid = threadIdx.x;   // consumers: 0..479
     cx.failed = 0;
     cx.chunk_i = 0;
     cx.upar = 0;
     cx.tr = p.trace != nullptr && threadIdx.x == 0;
     cx.tl = cx.tr && blockIdx.x == 0;
     cx.t0 = cx.tr ? gtime() : 0;
-    const int G = gridDim.x, E = p.E, F = p.F, L = p.L;
+    const int G = gridDim.x, E = p.E, L = p.L;
     unsigned char *sp = smem_raw;
     cx.s.ring = sp;
     sp += kSlots * kSlotBytes;
@@ -547,12 +830,16 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     sp += kTraceSlots * sizeof(u64);
     cx.s.red = reinterpret_cast<float *>(sp);
     sp += kRedFloats * sizeof(float);
-    cx.s.att = reinterpret_cast<float *>(sp);
-    sp += 1024 * sizeof(float);
-    cx.s.res = reinterpret_cast<float *>(sp);
-    sp += kRes * sizeof(float);
-    cx.s.lnf = reinterpret_cast<float *>(sp);
-    sp += 2 * (size_t)E * sizeof(float);
+    cx.s.attp = reinterpret_cast<float *>(sp);
+    sp += kMaxKeys * sizeof(float);
+    cx.s.attq = reinterpret_cast<float *>(sp);
+    sp += 192 * sizeof(float);
+    cx.s.atta = reinterpret_cast<float *>(sp);
+    sp += 64 * sizeof(float);
+    cx.s.part = reinterpret_cast<float *>(sp);
+    sp += kPart * sizeof(float);
+    cx.s.xres = reinterpret_cast<float *>(sp);
+    sp += (size_t)E * sizeof(float);
     cx.s.xs = reinterpret_cast<float *>(sp);
 
     if (threadIdx.x == 0) {
@@ -563,19 +850,14 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     for (int i = threadIdx.x; i < kTraceSlots; i += kThreads) cx.s.trc[i] = 0;
-    for (int i = threadIdx.x; i < E; i += kThreads) {
-        cx.s.lnf[i] = p.lnf_g[i];
-        cx.s.lnf[E + i] = p.lnf_b[i];
-    }
     __syncthreads();
 
     Sched S;
-    S.nA = 3 * E / p.cw[0];
-    S.nC = E / p.cw[1];
-    S.nD = F / p.cw[2];
-    S.nE = E / p.cw[3];
+    S.nA = 3 * E / p.cw_qkv;
+    S.nB = p.NH * p.nq;
+    S.nD = p.F / p.cw_fc;
     S.nLM = (p.V + p.lm_rows - 1) / p.lm_rows;
-    S.per_layer = S.nA + S.nC + S.nD + S.nE;
+    S.per_layer = S.nA + S.nB + S.nD;
     S.G = G;
 
     if (cx.warp == kWarps) {   // producer warp: one thread issues, the rest are idle
@@ -588,237 +870,42 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     int tok = p.state->token, pos = p.state->pos;
     const int step_base = p.state->step, min_new = p.state->min_new;
     for (int step = 0; step < p.n_steps; ++step) {
-        const int T = pos + 1;
-        const int nch = (T + 63) / 64;
+        // x = wte[tok] + wpe[pos] (embed, math.cl:333)
+        for (int i = cx.ctid; i < E; i += kCons) {
+            const float x = p.wte[(size_t)tok * E + i] + p.wpe[(size_t)pos * E + i];
+            xs[i] = x;
+            cx.s.xres[i] = x;
+        }
+        cons_sync();
         for (int l = 0; l < L; ++l) {
-            const int gl = l * S.per_layer;
-            // Phases in order A (LN1 + qkv + K/V append), B (attention), C (combine
-            // + proj + residual), D (LN2 + fc + GELU), E (fc2 + residual).  A, C, D
-            // and E share one body below; only their inputs and epilogues differ.
-            for (int ph = 0; ph < 5; ++ph) {
-                if (ph == 1) {
-            {
-                const int nB = p.NH * nch;
-                const unsigned ep_in = epoch_of(p, step, l, 0), ep = epoch_of(p, step, l, 1);
-                const int shift = (l * 37) % G;
-                for (int b = S.first(shift, cx.cta); b < nB; b += G) {
-                    const int h = b / nch, c = b % nch;
-                    // q, k_new, v_new of head h at pos (192); P (64); P.V partials (256)
-                    float *q = cx.s.att, *pr = cx.s.att + 192, *pv = cx.s.att + 256;
-                    tr_begin(cx);
-                    // threads 0..255: scores with 4 threads per key (16 dims each), then P.V with
-                    // thread (d, grp) over keys grp*16 .. grp*16+15.  The cached keys and values
-                    // (positions before pos, written by earlier steps) are loaded before the
-                    // wait for q; the key and value at pos come from the qkv vector (q + 64, q + 128).
-                    const size_t hb = (size_t)l * p.layer_stride + (size_t)h * p.max_seq * 64;
-                    const float *K = p.kc + hb, *V = p.vc + hb;
-                    const int j0 = c * 64, nj = min(64, T - j0);
-                    const bool act = cx.ctid < 256;
-                    const int key = (cx.ctid >> 2) & 63, part = cx.ctid & 3;
-                    const int d = cx.ctid & 63, grp = (cx.ctid >> 6) & 3;
-                    const bool kcached = act && key < nj && j0 + key != pos;
-                    float4 kr[4];
-#pragma unroll
-                    for (int t = 0; t < 4; ++t)
-                        kr[t] = kcached ? reinterpret_cast<const float4 *>(K + (size_t)(j0 + key) * 64 + part * 16)[t]
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-                    float vv[16];
-#pragma unroll
-                    for (int t = 0; t < 16; ++t) {
-                        const int jj = grp * 16 + t, j = j0 + jj;
-                        vv[t] = (act && jj < nj && j != pos) ? V[(size_t)j * 64 + d] : 0.0f;
-                    }
-                    {
-                        const u64 limit = gtime() + kTimeoutNs;
-                        bool pend = cx.ctid < 192;
-                        for (unsigned round = 0;; ++round) {
-                            if (pend) {
-                                const u64 w = ld_tag(p.t_qkv + (cx.ctid >> 6) * E + h * 64 + (cx.ctid & 63));
-                                if (tag_is(w, ep_in)) {
-                                    q[cx.ctid] = tag_val(w);
-                                    pend = false;
-                                }
-                            }
-                            if (cons_and(!pend)) break;
-                            if (poll_expired(cx, round, limit, 5)) goto out;
-                        }
-                    }
-                    tr_inputs(cx, 1);
-                    float s = 0.0f;
-                    if (act && key < nj) {
-                        const float *qq = q + part * 16;
-                        if (!kcached) {   // the key at pos
-#pragma unroll
-                            for (int t = 0; t < 16; ++t) s = fmaf(q[64 + part * 16 + t], qq[t], s);
-                        } else {
-#pragma unroll
-                            for (int t = 0; t < 4; ++t) {
-                                s = fmaf(kr[t].x, qq[4 * t], s);
-                                s = fmaf(kr[t].y, qq[4 * t + 1], s);
-                                s = fmaf(kr[t].z, qq[4 * t + 2], s);
-                                s = fmaf(kr[t].w, qq[4 * t + 3], s);
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int t = 0; t < 16; ++t)   // the value at pos (constant indices keep vv in registers)
-                        if (act && j0 + grp * 16 + t == pos) vv[t] = q[128 + d];
-                    s += __shfl_xor_sync(0xffffffffu, s, 1);
-                    s += __shfl_xor_sync(0xffffffffu, s, 2);
-                    s *= 0.125f;   // 1 / sqrt(64)
-                    const bool valid = act && key < nj;
-                    float m = warp_max(valid ? s : -FLT_MAX);
-                    float *rb = cx.s.red + kRedAtt;   // 32 floats
-                    if (cx.lane == 0 && cx.warp < 8) rb[cx.warp] = m;
-                    cons_sync();
-                    m = -FLT_MAX;
-                    for (int w = 0; w < 8; ++w) m = fmaxf(m, rb[w]);
-                    const float e = valid ? expf(s - m) : 0.0f;
-                    if (act && part == 0) pr[key] = e;
-                    const float lsum = warp_sum(act && part == 0 ? e : 0.0f);
-                    if (cx.lane == 0 && cx.warp < 8) rb[16 + cx.warp] = lsum;
-                    cons_sync();
-                    if (act) {
-                        float o = 0.0f;
-#pragma unroll
-                        for (int t = 0; t < 16; ++t) o = fmaf(pr[grp * 16 + t], vv[t], o);
-                        pv[grp * 64 + d] = o;
-                    }
-                    cons_sync();
-                    u64 *rec = p.t_part + ((size_t)h * kMaxChunks + c) * 66;
-                    if (cx.ctid < 64) {
-                        float acc = 0.0f;
-                        for (int g2 = 0; g2 < 4; ++g2) acc += pv[g2 * 64 + cx.ctid];
-                        st_tag(rec + 2 + cx.ctid, acc, ep);
-                    } else if (cx.ctid == 64) {
-                        float lt = 0.0f;
-                        for (int w = 0; w < 8; ++w) lt += rb[16 + w];
-                        st_tag(rec, m, ep);
-                        st_tag(rec + 1, lt, ep);
-                    }
-                    cons_sync();
-                    tr_end(cx, 1);
-                }
-            }
-                    continue;
-                }
-                // strip phase: ph 0 = A, 2 = C, 3 = D, 4 = E
-                const int g0 = gl + (ph >= 2 ? S.nA : 0) + (ph >= 3 ? S.nC : 0) + (ph >= 4 ? S.nD : 0);
-                const int n = ph == 0 ? S.nA : ph == 2 ? S.nC : ph == 3 ? S.nD : S.nE;
-                int u = S.first(g0, cx.cta);
-                if (u >= n) continue;
-                const int cw = p.cw[ph == 0 ? 0 : ph - 1], K = ph == 4 ? F : E;
-                const int tph = ph == 0 ? 0 : ph;    // trace slot
+            if (l > 0) {   // x += MLP output of layer l - 1
                 tr_begin(cx);
-                // ---- inputs ----
-                if (ph == 2) {
-                    const int nres = S.count(u, S.nC) * cw;
-                    const unsigned ep_b = epoch_of(p, step, l, 1), ep_res = epoch_of(p, step, l - 1, 4);
-                    // attn[h*64 + d] = sum_c acc_c[d] e^(m_c - M) / sum_c l_c e^(m_c - M), and the residuals
-                    const u64 limit = gtime() + kTimeoutNs;
-                    // pending: bit j for output ctid + j * kCons, bit 31 for the residual word
-                    unsigned pending = 0;
-                    for (int j = 0, i = cx.ctid; i < E; ++j, i += kCons) pending |= 1u << j;
-                    if (cx.ctid < nres) pending |= 1u << 31;
-                    for (unsigned round = 0;; ++round) {
-                        for (unsigned mk = pending & 0x7fffffffu; mk; mk &= mk - 1) {
-                            const int j = __ffs(mk) - 1, i = cx.ctid + j * kCons;
-                            const int h = i >> 6, dd = i & 63;
-                            // merge the chunks' (m, l, acc) in one pass, rescaling to the running max
-                            float M = -FLT_MAX, Lt = 0.0f, O = 0.0f;
-                            bool ok = true;
-                            for (int c = 0; c < nch; ++c) {
-                                const u64 *rec = p.t_part + ((size_t)h * kMaxChunks + c) * 66;
-                                const u64 w0 = ld_tag(rec), w1 = ld_tag(rec + 1), w2 = ld_tag(rec + 2 + dd);
-                                ok = ok && tag_is(w0, ep_b) && tag_is(w1, ep_b) && tag_is(w2, ep_b);
-                                const float mc = tag_val(w0), lc = tag_val(w1), ac = tag_val(w2);
-                                if (mc > M) {
-                                    const float sc = expf(M - mc);   // 0 on the first chunk
-                                    Lt = fmaf(Lt, sc, lc);
-                                    O = fmaf(O, sc, ac);
-                                    M = mc;
-                                } else {
-                                    const float wgt = expf(mc - M);
-                                    Lt = fmaf(lc, wgt, Lt);
-                                    O = fmaf(ac, wgt, O);
-                                }
-                            }
-                            if (!ok) continue;
-                            xs[i] = O / Lt;
-                            pending &= ~(1u << j);
-                        }
-                        if (pending >> 31) {
-                            const int n = (u + (cx.ctid / cw) * G) * cw + cx.ctid % cw;
-                            if (l == 0) {
-                                cx.s.res[cx.ctid] = p.wte[(size_t)tok * E + n] + p.wpe[(size_t)pos * E + n];
-                                pending &= 0x7fffffffu;
-                            } else {
-                                const u64 w = ld_tag(p.t_hb + n);
-                                if (tag_is(w, ep_res)) {
-                                    cx.s.res[cx.ctid] = tag_val(w);
-                                    pending &= 0x7fffffffu;
-                                }
-                            }
-                        }
-                        if (cons_and(pending == 0)) break;
-                        if (poll_expired(cx, round, limit, 6)) goto out;
-                    }
-                } else if (ph == 0 && l == 0) {
-                    for (int i = cx.ctid; i < E; i += kCons)
-                        xs[i] = p.wte[(size_t)tok * E + i] + p.wpe[(size_t)pos * E + i];
-                    cons_sync();
-                } else {
-                    // A: h'' of the previous layer; D: h'; E: f, with the residuals h' of its columns
-                    const u64 *src = ph == 0 ? p.t_hb : ph == 3 ? p.t_ha : p.t_f;
-                    const unsigned ep_in = ph == 0 ? epoch_of(p, step, l - 1, 4) : epoch_of(p, step, l, ph == 3 ? 2 : 3);
-                    if (!poll_vec(cx, src, xs, ph == 4 ? F : E, ep_in, p.t_ha, u, cw, ph == 4 ? S.count(u, S.nE) : 0,
-                                  epoch_of(p, step, l, 2)))
-                        goto out;
-                }
-                tr_inputs(cx, tph);
-                // ---- units ----
-                {
-                    const unsigned ep = epoch_of(p, step, l, ph == 0 ? 0 : ph == 2 ? 2 : ph == 3 ? 3 : 4);
-                    u64 *dst = ph == 0 ? p.t_qkv : ph == 2 ? p.t_ha : ph == 3 ? p.t_f : p.t_hb;
-                    for (int k = 0; u < n; u += G, ++k) {
-                        float v = strip_unit(cx, K, cw, ph == 0 || ph == 3);   // LN1 / LN2 folded in
-                        if (cx.ctid < cw) {
-                            const int col = u * cw + cx.ctid;
-                            if (ph == 0) {
-                                if (col >= E) {   // K or V of head m / 64: append at pos (math.cl:367-383)
-                                    int m = col - E;
-                                    float *kv = m >= E ? p.vc : p.kc;
-                                    if (m >= E) m -= E;
-                                    kv[(size_t)l * p.layer_stride + ((size_t)(m >> 6) * p.max_seq + pos) * 64 + (m & 63)] = v;
-                                }
-                            } else if (ph == 3) {
-                                v = gelu_f(v);
-                            } else {
-                                v += cx.s.res[k * cw + cx.ctid];   // C, E: residual
-                            }
-                            st_tag(dst + col, v, ep);
-                        }
-                        if (cx.tr) cx.s.trc[18] += 1;
-                    }
-                }
-                if (!cons_and(!cx.failed)) goto out;
-                tr_end(cx, tph);
+                if (!poll_acc(cx, acc_of(p, step, l - 1, 1), (unsigned)S.nD, p.layers[l - 1].fc2_b, E, 2)) goto out;
+                tr_inputs(cx, 2);
             }
+            if (!phase_A(cx, S, step, l, pos)) goto out;
+            if (!phase_B(cx, S, step, l, pos)) goto out;
+            // x += attention output (every CTA keeps the residual stream)
+            tr_begin(cx);
+            if (!poll_acc(cx, acc_of(p, step, l, 0), (unsigned)p.NH, p.layers[l].proj_b, E, 6)) goto out;
+            tr_inputs(cx, 4);
+            if (!phase_D(cx, S, step, l)) goto out;
         }
         // ---------------- LN_f + LM head + greedy argmax ----------------
         {
-            int u = S.first(L * S.per_layer, cx.cta);
+            tr_begin(cx);
+            if (!poll_acc(cx, acc_of(p, step, L - 1, 1), (unsigned)S.nD, p.layers[L - 1].fc2_b, E, 7)) goto out;
+            tr_inputs(cx, 5);
+            int u = S.lm_first(L, cx.cta);
             const bool forbid = (step_base + step) < min_new;
             float best = -FLT_MAX;
             int besti = INT_MAX;
             if (u < S.nLM) {
-                tr_begin(cx);
-                if (!poll_vec(cx, p.t_hb, xs, E, epoch_of(p, step, L - 1, 4))) goto out;
-                tr_inputs(cx, 5);
                 float mean, rstd;
                 ln_stats(cx, E, mean, rstd);
                 // normalise in place with gamma / beta (math.cl:310); the rows read it 16 times
-                for (int i = cx.ctid; i < E; i += kCons) xs[i] = (xs[i] - mean) * rstd * cx.s.lnf[i] + cx.s.lnf[E + i];
+                for (int i = cx.ctid; i < E; i += kCons)
+                    xs[i] = (xs[i] - mean) * rstd * __ldg(p.lnf_g + i) + __ldg(p.lnf_b + i);
                 cons_sync();
                 const int RPC = kSlotBytes / (E * 4);
                 const int E4 = E / 4;
@@ -826,7 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
                 for (; u < S.nLM; u += G) {
                     const int v0 = u * p.lm_rows, rows = min(p.lm_rows, p.V - v0);
                     for (int r0 = 0; r0 < rows; r0 += RPC) {
-                        const float *ch = chunk_begin(cx);
+                        const float *ch = reinterpret_cast<const float *>(chunk_wait(cx));
                         const int nr = min(RPC, rows - r0);
                         for (int r = cx.warp; r < nr; r += kWarps) {
                             const float4 *w4 = reinterpret_cast<const float4 *>(ch + (size_t)r * E);
@@ -846,12 +933,12 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
                                 besti = v;
                             }
                         }
-                        chunk_end(cx);
+                        chunk_done(cx);
                     }
                 }
                 if (!cons_and(!cx.failed)) goto out;
-                tr_end(cx, 5);
             }
+            tr_end(cx, 5);
             // this CTA's best -> tagged partial; then every CTA reduces all partials
             float *rv = cx.s.red + kRedArg;
             int *ri = reinterpret_cast<int *>(cx.s.red) + kRedArg + 16;
@@ -878,10 +965,10 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
                 st_tag(tb + 2 * cx.cta, best, ep);
                 st_tag(tb + 2 * cx.cta + 1, __int_as_float(besti), ep);
             }
-            float *bv = cx.s.att;                                    // 2 * G <= 512 floats
-            int *bi = reinterpret_cast<int *>(cx.s.att + 512);      // [0] token
+            float *bv = cx.s.part;                                  // 2 * G <= kPart floats
+            int *bi = reinterpret_cast<int *>(cx.s.attq);           // [0] token
             tr_begin(cx);
-            if (!poll_vec(cx, tb, bv, 2 * G, ep)) goto out;
+            if (!poll_vec(cx, tb, bv, 2 * G, ep, 3)) goto out;
             __threadfence();   // acquire: every CTA's K/V rows of this step, for the steps that follow
             tr_inputs(cx, 6);
             if (cx.ctid == 0) {
@@ -926,14 +1013,13 @@ out:
     return;
 }
 
-size_t mega_smem_bytes(int E, int F) {
-    const int xs = (E > F ? E : F) + 4;
+size_t mega_smem_bytes(int E) {
     return (size_t)kSlots * kSlotBytes + 2 * kSlots * sizeof(unsigned long long) + kTraceSlots * sizeof(unsigned long long) +
-           kRedFloats * sizeof(float) + 1024 * sizeof(float) + kRes * sizeof(float) + 2 * (size_t)E * sizeof(float) +
-           (size_t)xs * sizeof(float);
+           (kRedFloats + kMaxKeys + 192 + 64 + kPart) * sizeof(float) + (size_t)(2 * E + 4) * sizeof(float);
 }
 int mega_threads() { return kThreads; }
 const void *mega_kernel_ptr() { return (const void *)mega_decode_kernel; }
 int mega_slot_bytes() { return kSlotBytes; }
+int mega_max_keys() { return kMaxKeys; }
 
 }  // namespace g2

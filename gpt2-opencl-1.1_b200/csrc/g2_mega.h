@@ -13,16 +13,18 @@ struct LayerPtrs {
 
 struct MegaParams {
     int L, E, F, NH, V, max_seq;
-    int cw[4];           // strip widths (columns per unit) of qkv, proj, fc and fc2
+    int cw_qkv, cw_fc;   // strip widths (columns per unit) of c_attn and c_fc
+    int nq;              // column slices of attn.c_proj per head (B units = NH * nq)
     int lm_rows;         // wte rows per LM unit
     int n_steps;         // greedy decode steps in this launch
     long long layer_stride;                 // KV elements per layer of one slot
-    const float *packed;                    // strip-packed projection weights
-    const long long *layer_off;             // [L][4] float offsets of qkv, proj, fc, fc2 strips
+    const float *packed;                    // unit-packed projection weights
+    const long long *layer_off;             // [L][3] float offsets of the A, B and D units
     const LayerPtrs *layers;                // [L]
     const float *wte, *wpe, *lnf_g, *lnf_b, *lm;
     float *kc, *vc;                         // this slot's KV cache bases
-    unsigned long long *t_qkv, *t_part, *t_ha, *t_hb, *t_f, *t_best;   // tagged activations
+    unsigned long long *t_qkv, *t_best;     // tagged activations: q, k, v; argmax partials
+    unsigned long long *acc;                // [n_steps][L][2][E] accumulators, zero at launch
     float *logits;                          // [V_pad] of this slot
     int *out_tokens;                        // this slot's token row
     int *result;                            // [0] last token, [1] its logit bits
@@ -35,20 +37,31 @@ struct MegaParams {
 };
 
 constexpr int kTraceSlots = 64;
-// Trace words per CTA: [0..8) ns spent polling inputs per phase (A, B, C, D, E, LM, argmax),
-// [8..16) ns of work after the inputs arrived per phase, [16] ns waiting for ring chunks,
-// [17] kernel ns, [18] units, [19] chunks, [22] / [23] / [25] SM cycles of strip units in
-// LayerNorm sums / row products (chunk waits included) / reduction, [27] strip units,
-// [32..64) CTA 0 only: step-0 timeline of layer 0 (phase start/end stamps relative to kernel start).
+// Trace words per CTA: [0..8) ns spent waiting for inputs: [1] B (q, k, v), [2] x after
+// the MLP, [4] x after attention, [5] LM head, [6] argmax; [8..16) ns of work after the
+// inputs arrived: [8] A, [9] B, [11] D, [13] LM head, [14] argmax; [16] ns waiting for ring
+// chunks, [17] kernel ns, [18] units, [19] chunks; SM cycles of D units in the c_fc strip
+// [22] and the mlp.c_proj block [23] over [25] units, of B units in attention [26] and the
+// attn.c_proj block [27] over [28] units; [32..64) CTA 0 only: step-0 timeline (phase
+// start/end stamps relative to kernel start).
 
-size_t mega_smem_bytes(int E, int F);
+size_t mega_smem_bytes(int E);
 int mega_threads();
 const void *mega_kernel_ptr();
 int mega_slot_bytes();
-// Packed floats of one projection: N / CW units of (K + 2) rows x CW.  Rows
-// 0..K-1 are the weights, row K the bias, row K + 1 the column sums of the
-// weights (used when a LayerNorm is folded in, zero otherwise).
-inline long long mega_packed_floats(int K, int N) { return (long long)(K + 2) * N; }
+int mega_max_keys();
+// Steps per launch (the accumulators of one launch are sized for this many).
+constexpr int kMegaMaxSteps = 256;
+// Packed floats of a layer's units:
+//  A: 3E / cw_qkv strips of (E + 2) rows x cw_qkv (weights with ln_1's gamma
+//     folded in, then the bias row with beta folded in, then the column sums);
+//  B: NH * nq blocks of 64 rows x E / nq (rows 64h.. of attn.c_proj, one
+//     column slice);
+//  D: F / cw_fc units, each a c_fc strip (as in A, with ln_2) followed by
+//     the matching cw_fc rows of mlp.c_proj (E floats each).
+inline long long mega_packed_a(int E) { return (long long)(E + 2) * 3 * E; }
+inline long long mega_packed_b(int E) { return (long long)E * E; }
+inline long long mega_packed_d(int E, int F) { return (long long)(E + 2) * F + (long long)F * E; }
 // Strip width of a projection with N outputs on G CTAs: the narrowest of 4, 8,
 // 16 and 32 columns that gives every CTA at most one unit, else 32 (every CTA
 // then streams several units).  0 if N is not a multiple of 4.
@@ -60,6 +73,15 @@ inline int mega_cw(int N, int G) {
 inline int mega_lm_rows(int E) {
     const int rpc = 24576 / (E * 4);
     return rpc < 1 ? 1 : 2 * rpc;
+}
+// Column slices of attn.c_proj per head (B units = NH * nq): a slice is a
+// whole number of float4 groups, at most one per consumer thread.
+inline bool mega_nq_ok(int E, int nq) { return nq >= 1 && E % nq == 0 && (E / nq) % 4 == 0 && E / nq / 4 <= 480; }
+// Default: the largest of 4, 3, 2, 1 that is valid (G2_MEGA_NQ overrides).
+inline int mega_nq(int E) {
+    for (int nq = 4; nq >= 1; --nq)
+        if (mega_nq_ok(E, nq)) return nq;
+    return 0;
 }
 // Epochs one launch of n_steps uses.
 inline unsigned mega_epochs(int L, int n_steps) { return (unsigned)n_steps * (unsigned)((L + 1) * 8) + 8u; }

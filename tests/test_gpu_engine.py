@@ -254,3 +254,15 @@ def test_prefill_graph_replay_matches_oracle(g2, tiny_affine_model):
             eng.decode(tok, 19, slot=slot)
             assert rel(eng.logits(slot), ref.logits()) <= 1e-4
     ref.close()
+
+
+def test_generation_across_launch_chunks(g2, tiny_affine_model):
+    """A generation longer than one persistent launch (256 steps) continues
+    across launches with the same tokens as the oracle."""
+    prompt = synth.prompt_ids(23, 12)
+    ref = oracle.RefModel(tiny_affine_model)
+    want = ref.generate(prompt, 300)
+    ref.close()
+    with g2.Engine(tiny_affine_model) as eng:
+        got = eng.generate(prompt, 300)
+    assert list(got) == list(want)
