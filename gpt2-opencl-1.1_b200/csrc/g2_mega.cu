@@ -381,14 +381,7 @@ __device__ __forceinline__ void ln_stats(Cx &cx, int n, float &mean, float &rstd
 // phase's uniform check discards the result.
 __device__ __forceinline__ const float4 *chunk_wait(Cx &cx, unsigned k = 0) {
     const unsigned i = cx.chunk_i + k, slot = i % kSlots, par = (i / kSlots) & 1u;
-    if (cx.tr) {
-        const u64 t = gtime();
-        if (!mbar_wait(&cx.s.full[slot], par)) fail(cx, 4);
-        cx.s.trc[16] += gtime() - t;
-        cx.s.trc[19] += 1;
-    } else if (!mbar_wait(&cx.s.full[slot], par)) {
-        fail(cx, 4);
-    }
+    if (!mbar_wait(&cx.s.full[slot], par)) fail(cx, 4);
     return reinterpret_cast<const float4 *>(cx.s.ring + (size_t)slot * kSlotBytes);
 }
 // Release the next n chunks to the producer (each consumer warp arrives once).
@@ -609,197 +602,183 @@ __device__ __forceinline__ void producer(Cx &cx, const Sched &S) {
     for (unsigned j = i > kSlots ? i - kSlots : 0; j < i; ++j) mbar_wait(&cx.s.full[j % kSlots], (j / kSlots) & 1u);
 }
 
-// ---- consumer phases --------------------------------------------------------------------
+// ---- consumer units --------------------------------------------------------------------
 
-// A: LN1 + c_attn strips -> tagged qkv words; K and V columns also appended
-// to the cache at pos (split_kv, math.cl:367-383).  x is in xs.
-__device__ __forceinline__ bool phase_A(Cx &cx, const Sched &S, int step, int l, int pos) {
+// Single-query attention of head h over positions 0..pos (attn_scores_1q,
+// attn_softmax_1q, attn_out_1q, math.cl:388-476) into atta[0..64).  The
+// cached keys and values are read from the cache (L2); the first pass of keys
+// is loaded before the wait for q.  The key and value at pos come from the
+// qkv vector.
+__device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int pos) {
     const MegaParams &p = *cx.p;
-    const int E = p.E, cw = p.cw_qkv;
-    const unsigned ep = epoch_of(p, step, l, 0);
-    tr_begin(cx);
-    tr_inputs(cx, 0);
-    for (int u = S.a_first(l, cx.cta); u < S.nA; u += S.G) {
-        const float v = strip_unit(cx, E, cw);
-        if (cx.ctid < cw) {
-            const int col = u * cw + cx.ctid;
-            if (col >= E) {   // K or V of head m / 64
-                int m = col - E;
-                float *kv = m >= E ? p.vc : p.kc;
-                if (m >= E) m -= E;
-                kv[(size_t)l * p.layer_stride + ((size_t)(m >> 6) * p.max_seq + pos) * 64 + (m & 63)] = v;
-            }
-            st_tag(p.t_qkv + col, v, ep);
-        }
-        if (cx.tr) cx.s.trc[18] += 1;
-    }
-    const bool ok = cons_and(!cx.failed);
-    tr_end(cx, 0);
-    return ok;
-}
-
-// B: for each (head h, column slice j) unit of this CTA, single-query
-// attention of head h over positions 0..pos (attn_scores_1q, attn_softmax_1q,
-// attn_out_1q, math.cl:388-476), then its 64 outputs times rows 64h..64h+63
-// of attn.c_proj, columns j * NB .. j * NB + NB - 1, into the accumulator.
-// The cached keys and values are read from the cache (L2); the first pass of
-// keys is loaded before the wait for q.  The key and value at pos come from
-// the qkv vector.
-__device__ __forceinline__ bool phase_B(Cx &cx, const Sched &S, int step, int l, int pos) {
-    const MegaParams &p = *cx.p;
-    const int E = p.E, NQ = p.nq, NB = E / NQ, T = pos + 1;
+    const int E = p.E, T = pos + 1;
     const unsigned ep_in = epoch_of(p, step, l, 0);
     float *q = cx.s.attq, *pr = cx.s.attp, *a = cx.s.atta, *part = cx.s.part;
     float *rb = cx.s.red + kRedAtt;   // [0, 15) warp maxima, [16, 31) warp sums
-    u64 *acc = acc_of(p, step, l, 0);
     const int key = cx.ctid >> 2, k4 = cx.ctid & 3;   // score pass: 4 threads per key, 16 dims each
     const int dq = cx.ctid & 15, grp = cx.ctid >> 4;  // P.V pass: float4 dq of 64 dims, key group grp
-    for (int b = S.b_first(l, cx.cta); b < S.nB; b += S.G) {
-        const int h = b / NQ, jq = b % NQ;
-        tr_begin(cx);
-        const size_t hb = (size_t)l * p.layer_stride + (size_t)h * p.max_seq * 64;
-        const float4 *K4 = reinterpret_cast<const float4 *>(p.kc + hb);
-        const float4 *V4 = reinterpret_cast<const float4 *>(p.vc + hb);
-        float4 kr[4];
-        {
-            const bool c = key < T && key != pos;
+    const size_t hb = (size_t)l * p.layer_stride + (size_t)h * p.max_seq * 64;
+    const float4 *K4 = reinterpret_cast<const float4 *>(p.kc + hb);
+    const float4 *V4 = reinterpret_cast<const float4 *>(p.vc + hb);
+    float4 kr[4];
+    {
+        const bool c = key < T && key != pos;
 #pragma unroll
-            for (int t = 0; t < 4; ++t) kr[t] = c ? K4[(size_t)key * 16 + k4 * 4 + t] : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        {   // q, k, v of head h at pos
-            const u64 limit = gtime() + kTimeoutNs;
-            bool pend = cx.ctid < 192;
-            for (unsigned round = 0;; ++round) {
-                if (pend) {
-                    const u64 w = ld_tag(p.t_qkv + (cx.ctid >> 6) * E + h * 64 + (cx.ctid & 63));
-                    if (tag_is(w, ep_in)) {
-                        q[cx.ctid] = tag_val(w);
-                        pend = false;
-                    }
-                }
-                if (cons_and(!pend)) break;
-                if (poll_expired(cx, round, limit, 5)) return false;
-            }
-        }
-        tr_inputs(cx, 1);
-        const long long c0 = cx.tr ? clock64() : 0;
-        // scores s_j = q . k_j / 8 (the key at pos comes from the qkv vector)
-        float mloc = -FLT_MAX;
-        for (int j0 = 0; j0 < T; j0 += kKeysPerPass) {
-            const int j = j0 + key;
-            if (j0 > 0) {
-                const bool c = j < T && j != pos;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) kr[t] = c ? K4[(size_t)j * 16 + k4 * 4 + t] : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            if (j == pos) {
-#pragma unroll
-                for (int t = 0; t < 4; ++t)
-                    kr[t] = make_float4(q[64 + k4 * 16 + 4 * t], q[64 + k4 * 16 + 4 * t + 1], q[64 + k4 * 16 + 4 * t + 2],
-                                        q[64 + k4 * 16 + 4 * t + 3]);
-            }
-            const float *qq = q + k4 * 16;
-            float s = 0.0f;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                s = fmaf(kr[t].x, qq[4 * t], s);
-                s = fmaf(kr[t].y, qq[4 * t + 1], s);
-                s = fmaf(kr[t].z, qq[4 * t + 2], s);
-                s = fmaf(kr[t].w, qq[4 * t + 3], s);
-            }
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            s *= 0.125f;   // 1 / sqrt(64)
-            if (j < T) {
-                if (k4 == 0) pr[j] = s;
-                mloc = fmaxf(mloc, s);
-            }
-        }
-        float m = warp_max(mloc);
-        if (cx.lane == 0) rb[cx.warp] = m;
-        cons_sync();
-        m = rb[0];
-#pragma unroll
-        for (int w = 1; w < kWarps; ++w) m = fmaxf(m, rb[w]);
-        float lsum = 0.0f;
-        for (int j = cx.ctid; j < T; j += kCons) {
-            const float e = expf(pr[j] - m);
-            pr[j] = e;
-            lsum += e;
-        }
-        lsum = warp_sum(lsum);
-        if (cx.lane == 0) rb[16 + cx.warp] = lsum;
-        cons_sync();
-        float Lt = rb[16];
-#pragma unroll
-        for (int w = 1; w < kWarps; ++w) Lt += rb[16 + w];
-        // P.V: thread (grp, dq) sums keys grp, grp + kPvGroups, ... of dims 4 dq .. 4 dq + 3
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int j0 = grp; j0 < T; j0 += 4 * kPvGroups) {
-            float4 vv[4];
-            float pp[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int j = j0 + u * kPvGroups;
-                const bool in = j < T;
-                vv[u] = (in && j != pos) ? V4[(size_t)j * 16 + dq] : make_float4(0.f, 0.f, 0.f, 0.f);
-                if (j == pos)
-                    vv[u] = make_float4(q[128 + 4 * dq], q[128 + 4 * dq + 1], q[128 + 4 * dq + 2], q[128 + 4 * dq + 3]);
-                pp[u] = in ? pr[j] : 0.0f;
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) fma4(o, pp[u], vv[u]);
-        }
-        reinterpret_cast<float4 *>(part)[grp * 16 + dq] = o;   // [kPvGroups][64]
-        cons_sync();
-        if (cx.ctid < 64) {
-            float y = part[cx.ctid];
-            for (int g = 1; g < kPvGroups; ++g) y += part[g * 64 + cx.ctid];
-            a[cx.ctid] = y / Lt;
-        }
-        cons_sync();
-        const long long c1 = cx.tr ? clock64() : 0;
-        block_unit(cx, a, 64, NB, acc + jq * NB);
-        if (cx.tr) {
-            cx.s.trc[18] += 1;
-            cx.s.trc[26] += c1 - c0;
-            cx.s.trc[27] += clock64() - c1;
-            cx.s.trc[28] += 1;
-        }
-        const bool ok = cons_and(!cx.failed);
-        tr_end(cx, 1);
-        if (!ok) return false;
+        for (int t = 0; t < 4; ++t) kr[t] = c ? K4[(size_t)key * 16 + k4 * 4 + t] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    {   // q, k, v of head h at pos
+        const u64 limit = gtime() + kTimeoutNs;
+        bool pend = cx.ctid < 192;
+        for (unsigned round = 0;; ++round) {
+            if (pend) {
+                const u64 w = ld_tag(p.t_qkv + (cx.ctid >> 6) * E + h * 64 + (cx.ctid & 63));
+                if (tag_is(w, ep_in)) {
+                    q[cx.ctid] = tag_val(w);
+                    pend = false;
+                }
+            }
+            if (cons_and(!pend)) break;
+            if (poll_expired(cx, round, limit, 5)) return false;
+        }
+    }
+    tr_inputs(cx, 1);
+    // scores s_j = q . k_j / 8 (the key at pos comes from the qkv vector)
+    float mloc = -FLT_MAX;
+    for (int j0 = 0; j0 < T; j0 += kKeysPerPass) {
+        const int j = j0 + key;
+        if (j0 > 0) {
+            const bool c = j < T && j != pos;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) kr[t] = c ? K4[(size_t)j * 16 + k4 * 4 + t] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (j == pos) {
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                kr[t] = make_float4(q[64 + k4 * 16 + 4 * t], q[64 + k4 * 16 + 4 * t + 1], q[64 + k4 * 16 + 4 * t + 2],
+                                    q[64 + k4 * 16 + 4 * t + 3]);
+        }
+        const float *qq = q + k4 * 16;
+        float s = 0.0f;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            s = fmaf(kr[t].x, qq[4 * t], s);
+            s = fmaf(kr[t].y, qq[4 * t + 1], s);
+            s = fmaf(kr[t].z, qq[4 * t + 2], s);
+            s = fmaf(kr[t].w, qq[4 * t + 3], s);
+        }
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        s *= 0.125f;   // 1 / sqrt(64)
+        if (j < T) {
+            if (k4 == 0) pr[j] = s;
+            mloc = fmaxf(mloc, s);
+        }
+    }
+    float m = warp_max(mloc);
+    if (cx.lane == 0) rb[cx.warp] = m;
+    cons_sync();
+    m = rb[0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) m = fmaxf(m, rb[w]);
+    float lsum = 0.0f;
+    for (int j = cx.ctid; j < T; j += kCons) {
+        const float e = expf(pr[j] - m);
+        pr[j] = e;
+        lsum += e;
+    }
+    lsum = warp_sum(lsum);
+    if (cx.lane == 0) rb[16 + cx.warp] = lsum;
+    cons_sync();
+    float Lt = rb[16];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) Lt += rb[16 + w];
+    // P.V: thread (grp, dq) sums keys grp, grp + kPvGroups, ... of dims 4 dq .. 4 dq + 3
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j0 = grp; j0 < T; j0 += 4 * kPvGroups) {
+        float4 vv[4];
+        float pp[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = j0 + u * kPvGroups;
+            const bool in = j < T;
+            vv[u] = (in && j != pos) ? V4[(size_t)j * 16 + dq] : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (j == pos)
+                vv[u] = make_float4(q[128 + 4 * dq], q[128 + 4 * dq + 1], q[128 + 4 * dq + 2], q[128 + 4 * dq + 3]);
+            pp[u] = in ? pr[j] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) fma4(o, pp[u], vv[u]);
+    }
+    reinterpret_cast<float4 *>(part)[grp * 16 + dq] = o;   // [kPvGroups][64]
+    cons_sync();
+    if (cx.ctid < 64) {
+        float y = part[cx.ctid];
+        for (int g = 1; g < kPvGroups; ++g) y += part[g * 64 + cx.ctid];
+        a[cx.ctid] = y / Lt;
+    }
+    cons_sync();
     return true;
 }
 
-// D: x' is in xs.  For each unit: LN2 + c_fc strip of cw columns, GELU
-// (math.cl:21-23), then those cw values times the matching cw rows of
-// mlp.c_proj (all E outputs) into the accumulator.
-__device__ __forceinline__ bool phase_D(Cx &cx, const Sched &S, int step, int l) {
+// The units of this CTA in one half of layer l, each kind through one copy of
+// its code (the loop stays in the instruction cache):
+//   half 0: A units -- LN1 + c_attn strip -> tagged qkv words, and the K and
+//           V columns appended to the cache at pos (split_kv,
+//           math.cl:367-383); then B units -- attention of head h, then its
+//           64 outputs times rows 64h.. of attn.c_proj, column slice j, into
+//           the attention accumulator;
+//   half 1: D units -- LN2 + c_fc strip, GELU (math.cl:21-23), then the cw
+//           values times the matching cw rows of mlp.c_proj (all E outputs)
+//           into the MLP accumulator.
+// xs holds the input x.
+__device__ __forceinline__ bool run_units(Cx &cx, const Sched &S, int step, int l, int pos, int half) {
     const MegaParams &p = *cx.p;
-    const int E = p.E, cw = p.cw_fc;
-    u64 *acc = acc_of(p, step, l, 1);
-    float *gv = cx.s.atta;
-    tr_begin(cx);
-    tr_inputs(cx, 3);
-    for (int u = S.d_first(l, cx.cta); u < S.nD; u += S.G) {
-        const long long c0 = cx.tr ? clock64() : 0;
-        const float v = strip_unit(cx, E, cw);
-        if (cx.ctid < cw) gv[cx.ctid] = gelu_f(v);
-        cons_sync();
-        const long long c1 = cx.tr ? clock64() : 0;
-        block_unit(cx, gv, cw, E, acc);
-        if (cx.tr) {
-            cx.s.trc[18] += 1;
-            cx.s.trc[22] += c1 - c0;
-            cx.s.trc[23] += clock64() - c1;
-            cx.s.trc[25] += 1;
+    const int E = p.E, t = cx.ctid;
+    for (int kind = half ? 2 : 0; kind <= (half ? 2 : 1); ++kind) {
+        const int n = kind == 0 ? S.nA : kind == 1 ? S.nB : S.nD;
+        int u = kind == 0 ? S.a_first(l, cx.cta) : kind == 1 ? S.b_first(l, cx.cta) : S.d_first(l, cx.cta);
+        const int cw = kind == 0 ? p.cw_qkv : p.cw_fc;
+        const int NB = kind == 1 ? E / p.nq : E;
+        u64 *acc = acc_of(p, step, l, kind == 1 ? 0 : 1);
+        const unsigned ep = epoch_of(p, step, l, 0);
+        const int ph = kind == 0 ? 0 : kind == 1 ? 1 : 3;   // trace slot
+        float *av = cx.s.atta;
+        for (; u < n; u += S.G) {
+            tr_begin(cx);
+            int rows;
+            u64 *dst;
+            if (kind != 1) {
+                tr_inputs(cx, ph);
+                const float v = strip_unit(cx, E, cw);
+                if (kind == 0) {
+                    if (t < cw) {
+                        const int col = u * cw + t;
+                        if (col >= E) {   // K or V of head m / 64
+                            int m = col - E;
+                            float *kv = m >= E ? p.vc : p.kc;
+                            if (m >= E) m -= E;
+                            kv[(size_t)l * p.layer_stride + ((size_t)(m >> 6) * p.max_seq + pos) * 64 + (m & 63)] = v;
+                        }
+                        st_tag(p.t_qkv + col, v, ep);
+                    }
+                    tr_end(cx, ph);
+                    continue;
+                }
+                if (t < cw) av[t] = gelu_f(v);
+                cons_sync();
+                rows = cw;
+                dst = acc;
+            } else {
+                if (!attention(cx, u / p.nq, step, l, pos)) return false;
+                rows = 64;
+                dst = acc + (u % p.nq) * NB;
+            }
+            block_unit(cx, av, rows, NB, dst);
+            tr_end(cx, ph);
         }
+        if (!cons_and(!cx.failed)) return false;
     }
-    const bool ok = cons_and(!cx.failed);
-    tr_end(cx, 3);
-    return ok;
+    return true;
 }
 
 }  // namespace
@@ -877,64 +856,80 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
             cx.s.xres[i] = x;
         }
         cons_sync();
-        for (int l = 0; l < L; ++l) {
-            if (l > 0) {   // x += MLP output of layer l - 1
-                tr_begin(cx);
-                if (!poll_acc(cx, acc_of(p, step, l - 1, 1), (unsigned)S.nD, p.layers[l - 1].fc2_b, E, 2)) goto out;
-                tr_inputs(cx, 2);
+        // Per layer: A and B units on x; x += attention; D units; x += MLP.
+        // The last pass (l == L) only takes in the MLP output of the last layer.
+        for (int l = 0; l <= L; ++l) {
+            for (int half = 0; half < 2; ++half) {
+                if (l == L && half == 1) break;
+                if (l > 0 || half == 1) {   // x += (MLP of layer l - 1 | attention of layer l) + bias
+                    const int lp = half ? l : l - 1;
+                    tr_begin(cx);
+                    if (!poll_acc(cx, acc_of(p, step, lp, 1 - half), half ? (unsigned)p.NH : (unsigned)S.nD,
+                                  half ? p.layers[lp].proj_b : p.layers[lp].fc2_b, E, half ? 6 : 2))
+                        goto out;
+                    tr_inputs(cx, half ? 4 : l == L ? 5 : 2);
+                }
+                if (l == L) break;
+                if (!run_units(cx, S, step, l, pos, half)) goto out;
             }
-            if (!phase_A(cx, S, step, l, pos)) goto out;
-            if (!phase_B(cx, S, step, l, pos)) goto out;
-            // x += attention output (every CTA keeps the residual stream)
-            tr_begin(cx);
-            if (!poll_acc(cx, acc_of(p, step, l, 0), (unsigned)p.NH, p.layers[l].proj_b, E, 6)) goto out;
-            tr_inputs(cx, 4);
-            if (!phase_D(cx, S, step, l)) goto out;
         }
         // ---------------- LN_f + LM head + greedy argmax ----------------
         {
-            tr_begin(cx);
-            if (!poll_acc(cx, acc_of(p, step, L - 1, 1), (unsigned)S.nD, p.layers[L - 1].fc2_b, E, 7)) goto out;
-            tr_inputs(cx, 5);
             int u = S.lm_first(L, cx.cta);
             const bool forbid = (step_base + step) < min_new;
             float best = -FLT_MAX;
             int besti = INT_MAX;
             if (u < S.nLM) {
+                tr_begin(cx);
+                tr_inputs(cx, 5);
                 float mean, rstd;
                 ln_stats(cx, E, mean, rstd);
                 // normalise in place with gamma / beta (math.cl:310); the rows read it 16 times
                 for (int i = cx.ctid; i < E; i += kCons)
                     xs[i] = (xs[i] - mean) * rstd * __ldg(p.lnf_g + i) + __ldg(p.lnf_b + i);
                 cons_sync();
+                // A unit holds up to kWarps rows over one or more chunks: all of its
+                // chunks are waited for, then warp w takes row w.
                 const int RPC = kSlotBytes / (E * 4);
                 const int E4 = E / 4;
                 const float4 *x4 = reinterpret_cast<const float4 *>(xs);
                 for (; u < S.nLM; u += G) {
                     const int v0 = u * p.lm_rows, rows = min(p.lm_rows, p.V - v0);
-                    for (int r0 = 0; r0 < rows; r0 += RPC) {
-                        const float *ch = reinterpret_cast<const float *>(chunk_wait(cx));
-                        const int nr = min(RPC, rows - r0);
-                        for (int r = cx.warp; r < nr; r += kWarps) {
-                            const float4 *w4 = reinterpret_cast<const float4 *>(ch + (size_t)r * E);
-                            float sacc = 0.0f;
-                            for (int j = cx.lane; j < E4; j += 32) {
-                                const float4 w = w4[j], xv = x4[j];
-                                sacc = fmaf(w.x, xv.x, sacc);
-                                sacc = fmaf(w.y, xv.y, sacc);
-                                sacc = fmaf(w.z, xv.z, sacc);
-                                sacc = fmaf(w.w, xv.w, sacc);
-                            }
-                            sacc = warp_sum(sacc);
-                            const int v = v0 + r0 + r;
-                            if (cx.lane == 0) p.logits[v] = sacc;
-                            if (!(forbid && v == kEos) && better(sacc, v, best, besti)) {
-                                best = sacc;
-                                besti = v;
-                            }
+                    const int nch = (rows + RPC - 1) / RPC;
+                    for (int k = 0; k < nch; ++k) chunk_wait(cx, k);
+                    if (cx.warp < rows) {
+                        const float4 *w4 = reinterpret_cast<const float4 *>(
+                                               cx.s.ring + (size_t)((cx.chunk_i + cx.warp / RPC) % kSlots) * kSlotBytes) +
+                                           (size_t)(cx.warp % RPC) * E4;
+                        float s0 = 0.0f, s1 = 0.0f;
+                        int j = cx.lane;
+                        for (; j + 32 < E4; j += 64) {
+                            const float4 w = w4[j], xv = x4[j], w2 = w4[j + 32], xv2 = x4[j + 32];
+                            s0 = fmaf(w.x, xv.x, s0);
+                            s1 = fmaf(w2.x, xv2.x, s1);
+                            s0 = fmaf(w.y, xv.y, s0);
+                            s1 = fmaf(w2.y, xv2.y, s1);
+                            s0 = fmaf(w.z, xv.z, s0);
+                            s1 = fmaf(w2.z, xv2.z, s1);
+                            s0 = fmaf(w.w, xv.w, s0);
+                            s1 = fmaf(w2.w, xv2.w, s1);
                         }
-                        chunk_done(cx);
+                        if (j < E4) {
+                            const float4 w = w4[j], xv = x4[j];
+                            s0 = fmaf(w.x, xv.x, s0);
+                            s0 = fmaf(w.y, xv.y, s0);
+                            s0 = fmaf(w.z, xv.z, s0);
+                            s0 = fmaf(w.w, xv.w, s0);
+                        }
+                        const float sacc = warp_sum(s0 + s1);
+                        const int v = v0 + cx.warp;
+                        if (cx.lane == 0) p.logits[v] = sacc;
+                        if (!(forbid && v == kEos) && better(sacc, v, best, besti)) {
+                            best = sacc;
+                            besti = v;
+                        }
                     }
+                    chunk_done(cx, nch);
                 }
                 if (!cons_and(!cx.failed)) goto out;
             }

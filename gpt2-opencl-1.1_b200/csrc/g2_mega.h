@@ -70,9 +70,11 @@ inline int mega_cw(int N, int G) {
         if (N % cw == 0 && N / cw <= G) return cw;
     return N % 32 == 0 ? 32 : N % 16 == 0 ? 16 : N % 8 == 0 ? 8 : N % 4 == 0 ? 4 : 0;
 }
+// wte rows per LM-head unit: one per consumer warp (15), over at most a few
+// ring chunks.
 inline int mega_lm_rows(int E) {
-    const int rpc = 24576 / (E * 4);
-    return rpc < 1 ? 1 : 2 * rpc;
+    (void)E;
+    return 15;
 }
 // Column slices of attn.c_proj per head (B units = NH * nq): a slice is a
 // whole number of float4 groups, at most one per consumer thread.
