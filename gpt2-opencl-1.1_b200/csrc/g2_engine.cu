@@ -120,7 +120,7 @@ struct g2_engine {
     long long *d_layer_off = nullptr;
     LayerPtrs *d_layers = nullptr;
     unsigned long long *t_qkv = nullptr, *t_best = nullptr;
-    unsigned long long *mega_acc = nullptr;   // [kMegaMaxSteps][L][2][E] accumulators
+    unsigned long long *mega_acc = nullptr;   // mega_acc_words(kMegaMaxSteps, L, E) accumulator words
     int *d_err = nullptr;
     unsigned long long *d_trace = nullptr;   // phase trace, when G2_MEGA_TRACE names an output file
     std::string trace_path;
@@ -574,7 +574,7 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
     e->dec_graph.assign(max_batch, nullptr);
     if (e->mega) {
         TRY(dalloc(e, &e->t_qkv, (size_t)3 * E));
-        TRY(dalloc(e, &e->mega_acc, (size_t)kMegaMaxSteps * c.n_layer * 2 * E));
+        TRY(dalloc(e, &e->mega_acc, mega_acc_words(kMegaMaxSteps, c.n_layer, E)));
         TRY(dalloc(e, &e->t_best, (size_t)4 * e->sms));
         TRY(dalloc(e, &e->d_err, 1));
         TRY(dalloc(e, &e->d_layer_off, e->layer_off.size()));
@@ -943,7 +943,7 @@ static int launch_mega(g2_engine *e, int slot, int n_steps) {
     // launches of at most kMegaMaxSteps steps, each on zeroed accumulators
     for (int done = 0; done < n_steps;) {
         const int n = std::min(kMegaMaxSteps, n_steps - done);
-        CK(cudaMemsetAsync(e->mega_acc, 0, (size_t)n * c.n_layer * 2 * c.n_embd * 8, e->st));
+        CK(cudaMemsetAsync(e->mega_acc, 0, mega_acc_words(n, c.n_layer, c.n_embd) * 8, e->st));
         P.n_steps = n;
         P.epoch0 = e->mega_epoch + 1;
         e->mega_epoch += mega_epochs(c.n_layer, n);

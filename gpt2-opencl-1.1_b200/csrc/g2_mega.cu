@@ -312,19 +312,32 @@ __device__ __forceinline__ bool poll_vec(Cx &cx, const u64 *src, float *dst, int
     }
 }
 
-// Poll the E accumulator words at src until each holds `expect` contributions,
-// then x[i] = x[i] + (acc[i] + bias[i]) in xres and xs.  All consumer threads.
-__device__ __forceinline__ bool poll_acc(Cx &cx, const u64 *src, unsigned expect, const float *bias, int E, int code) {
+// Poll the accumulator at src (ncopy copies of E words; copy c collects the
+// units u with u % ncopy == c of the nunits contributors) until every word
+// holds its count, then x[i] = x[i] + (sum over copies in order + bias[i]) in
+// xres and xs.  All consumer threads.
+__device__ __forceinline__ bool poll_acc(Cx &cx, const u64 *src, int ncopy, int nunits, const float *bias, int E,
+                                         int code) {
     const u64 limit = gtime() + kTimeoutNs;
     unsigned pending = 0;
     for (int j = 0, i = cx.ctid; i < E; ++j, i += kCons) pending |= 1u << j;
     for (unsigned round = 0;; ++round) {
         for (unsigned m = pending; m; m &= m - 1) {
             const int j = __ffs(m) - 1, i = cx.ctid + j * kCons;
-            const u64 w = ld_tag(src + i);
-            const unsigned n = acc_count(w);
-            if (n == expect) {
-                const float x = cx.s.xres[i] + (acc_value(w, n) + __ldg(bias + i));
+            u64 w[kAccCopies];
+            bool ready = true;
+#pragma unroll
+            for (int c = 0; c < kAccCopies; ++c) {
+                if (c >= ncopy) break;
+                w[c] = ld_tag(src + (size_t)c * E + i);
+                ready = ready && acc_count(w[c]) == (unsigned)((nunits - c + ncopy - 1) / ncopy);
+            }
+            if (ready) {
+                float v = acc_value(w[0], acc_count(w[0]));
+#pragma unroll
+                for (int c = 1; c < kAccCopies; ++c)
+                    if (c < ncopy) v += acc_value(w[c], acc_count(w[c]));
+                const float x = cx.s.xres[i] + (v + __ldg(bias + i));
                 cx.s.xres[i] = x;
                 cx.s.xs[i] = x;
                 pending &= ~(1u << j);
@@ -535,10 +548,12 @@ __device__ __forceinline__ void block_unit(Cx &cx, const float *a, int rows, int
 __device__ __forceinline__ unsigned epoch_of(const MegaParams &p, int step, int layer, int ph) {
     return p.epoch0 + (unsigned)step * (unsigned)((p.L + 1) * 8) + (unsigned)(layer * 8 + ph);
 }
-// Accumulator vector of layer l in step `step`: w = 0 after B (attention
-// projection), w = 1 after D (MLP projection).
+// Accumulator of layer l in step `step`: w = 0 after B (attention
+// projection, one copy of E words), w = 1 after D (MLP projection,
+// kAccCopies copies of E words; D unit u adds into copy u % kAccCopies, which
+// cuts the contention on each word).
 __device__ __forceinline__ u64 *acc_of(const MegaParams &p, int step, int l, int w) {
-    return p.acc + ((size_t)step * 2 * p.L + 2 * l + w) * p.E;
+    return p.acc + ((size_t)(step * p.L + l) * (1 + kAccCopies) + (w ? 1 : 0)) * p.E;
 }
 
 // ---- producer: the CTA's weight stream for all steps ------------------------------------
@@ -767,7 +782,7 @@ __device__ __forceinline__ bool run_units(Cx &cx, const Sched &S, int step, int 
                 if (t < cw) av[t] = gelu_f(v);
                 cons_sync();
                 rows = cw;
-                dst = acc;
+                dst = acc + (size_t)(u % kAccCopies) * E;
             } else {
                 if (!attention(cx, u / p.nq, step, l, pos)) return false;
                 rows = 64;
@@ -864,7 +879,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
                 if (l > 0 || half == 1) {   // x += (MLP of layer l - 1 | attention of layer l) + bias
                     const int lp = half ? l : l - 1;
                     tr_begin(cx);
-                    if (!poll_acc(cx, acc_of(p, step, lp, 1 - half), half ? (unsigned)p.NH : (unsigned)S.nD,
+                    if (!poll_acc(cx, acc_of(p, step, lp, 1 - half), half ? 1 : kAccCopies, half ? p.NH : S.nD,
                                   half ? p.layers[lp].proj_b : p.layers[lp].fc2_b, E, half ? 6 : 2))
                         goto out;
                     tr_inputs(cx, half ? 4 : l == L ? 5 : 2);

@@ -24,7 +24,7 @@ struct MegaParams {
     const float *wte, *wpe, *lnf_g, *lnf_b, *lm;
     float *kc, *vc;                         // this slot's KV cache bases
     unsigned long long *t_qkv, *t_best;     // tagged activations: q, k, v; argmax partials
-    unsigned long long *acc;                // [n_steps][L][2][E] accumulators, zero at launch
+    unsigned long long *acc;                // mega_acc_words(n_steps, L, E) accumulator words, zero at launch
     float *logits;                          // [V_pad] of this slot
     int *out_tokens;                        // this slot's token row
     int *result;                            // [0] last token, [1] its logit bits
@@ -52,6 +52,11 @@ int mega_slot_bytes();
 int mega_max_keys();
 // Steps per launch (the accumulators of one launch are sized for this many).
 constexpr int kMegaMaxSteps = 256;
+// Copies of the MLP accumulator (D units spread their additions over them).
+constexpr int kAccCopies = 4;
+// Accumulator words of one launch of n steps: per step and layer, one
+// attention vector and kAccCopies MLP vectors of E words.
+inline size_t mega_acc_words(int n, int L, int E) { return (size_t)n * L * (1 + kAccCopies) * E; }
 // Packed floats of a layer's units:
 //  A: 3E / cw_qkv strips of (E + 2) rows x cw_qkv (weights with ln_1's gamma
 //     folded in, then the bias row with beta folded in, then the column sums);
