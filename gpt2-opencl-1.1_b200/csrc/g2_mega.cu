@@ -406,7 +406,8 @@ __device__ __forceinline__ void chunk_done(Cx &cx, unsigned n = 1) {
 }
 
 // One strip unit of K weight rows plus its bias row and column-sum row, for
-// its cw columns (4, 8, 16 or 32), with the LayerNorm folded in:
+// its cw columns (4 CG with CG in 1..6 or 8, so that CG divides kCons), with
+// the LayerNorm folded in:
 // y = rstd * (xs . W' - mean * colsum(W')) + b', the statistics reduced in the
 // same pass as the products (one barrier for the whole unit).  The result is
 // in threads ctid < cw.  Thread (rg, cg) = (ctid / CG, ctid % CG) takes rows
@@ -415,10 +416,10 @@ __device__ __forceinline__ void chunk_done(Cx &cx, unsigned n = 1) {
 // RPC <= 4 RG at every width).  Chunks of weight rows only are taken two at a
 // time without masks; the chunk with the bias and column-sum rows is masked.
 __device__ __forceinline__ float strip_unit(Cx &cx, int K, int cw) {
-    const int lg = cw == 32 ? 3 : cw == 16 ? 2 : cw == 8 ? 1 : 0;   // log2 of the float4 column groups
-    const int RG = kCons >> lg;
+    const int CG = cw >> 2;                         // float4 column groups
+    const int RG = kCons / CG;                      // row groups (RG * CG == kCons)
     const int RPC = kSlotBytes / (cw * 4);          // rows per chunk
-    const int rg = cx.ctid >> lg, t = cx.ctid;
+    const int rg = cx.ctid / CG, t = cx.ctid;
     const int rows = K + 2;
     const bool has4 = rg + 3 * RG < RPC;
     const float *xs = cx.s.xs;
@@ -466,18 +467,23 @@ __device__ __forceinline__ float strip_unit(Cx &cx, int K, int cw) {
         chunk_done(cx);
     }
     float4 acc = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
-    // lanes with equal lane % CG hold the same columns: reduce within the warp, then across warps
-    for (int o = 1 << lg; o < 32; o <<= 1) {
-        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
-        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
-        acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
-        acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+    // Lanes congruent mod CG hold the same column group ((32 warp + lane) % CG):
+    // fold them into lanes 0..CG-1 of the warp, then add across warps.
+    for (int o = CG; o < 32; o <<= 1) {
+        const float4 u = make_float4(__shfl_down_sync(0xffffffffu, acc.x, o), __shfl_down_sync(0xffffffffu, acc.y, o),
+                                     __shfl_down_sync(0xffffffffu, acc.z, o), __shfl_down_sync(0xffffffffu, acc.w, o));
+        if (cx.lane + o < 32) {
+            acc.x += u.x;
+            acc.y += u.y;
+            acc.z += u.z;
+            acc.w += u.w;
+        }
     }
     s = warp_sum(s);
     q = warp_sum(q);
     float *red = cx.s.red + (cx.upar & 1) * kRedHalf;   // [warp][32] products, then [480 + 2 warp] sums
     cx.upar ^= 1u;
-    if (cx.lane < (1 << lg)) reinterpret_cast<float4 *>(red)[cx.warp * 8 + cx.lane] = acc;
+    if (cx.lane < CG) reinterpret_cast<float4 *>(red)[cx.warp * 8 + (cx.warp * 32 + cx.lane) % CG] = acc;
     if (cx.lane == 0) {
         red[480 + 2 * cx.warp] = s;
         red[481 + 2 * cx.warp] = q;

@@ -67,13 +67,17 @@ inline size_t mega_acc_words(int n, int L, int E) { return (size_t)n * L * (1 + 
 inline long long mega_packed_a(int E) { return (long long)(E + 2) * 3 * E; }
 inline long long mega_packed_b(int E) { return (long long)E * E; }
 inline long long mega_packed_d(int E, int F) { return (long long)(E + 2) * F + (long long)F * E; }
-// Strip width of a projection with N outputs on G CTAs: the narrowest of 4, 8,
-// 16 and 32 columns that gives every CTA at most one unit, else 32 (every CTA
-// then streams several units).  0 if N is not a multiple of 4.
+// Strip width of a projection with N outputs on G CTAs: the narrowest of 4,
+// 8, 12, 16, 20, 24 and 32 columns (cw / 4 float4 groups dividing the 480
+// consumer threads) that gives every CTA at most one unit, else the widest
+// that divides N.  0 if none divides N.
 inline int mega_cw(int N, int G) {
-    for (int cw = 4; cw <= 32; cw *= 2)
+    static const int widths[7] = {4, 8, 12, 16, 20, 24, 32};
+    for (int cw : widths)
         if (N % cw == 0 && N / cw <= G) return cw;
-    return N % 32 == 0 ? 32 : N % 16 == 0 ? 16 : N % 8 == 0 ? 8 : N % 4 == 0 ? 4 : 0;
+    for (int k = 6; k >= 0; --k)
+        if (N % widths[k] == 0) return widths[k];
+    return 0;
 }
 // wte rows per LM-head unit: one per consumer warp (15), over at most a few
 // ring chunks.
