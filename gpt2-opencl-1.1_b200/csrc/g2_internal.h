@@ -10,7 +10,7 @@
 namespace g2 {
 
 constexpr int kHeadDim = 64;        // GPT-2 head size (all family members)
-constexpr int kAttnChunk = 64;      // keys per attention CTA (flash-decoding split)
+constexpr int kAttnChunk = 128;     // keys per attention CTA (flash-decoding split)
 constexpr int kMaxSeq = 1024;       // KV positions per slot (main.c:51)
 constexpr int kEos = 50256;         // main.c:58
 

@@ -343,10 +343,14 @@ struct AttnArgs {
 
 template <typename KT>
 __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
-    constexpr int CH = kAttnChunk;
+    constexpr int CH = kAttnChunk;              // keys per CTA: one per thread in the score pass
+    constexpr int VN = 16 / sizeof(KT);         // elements per 16-byte load
+    constexpr int DG = kHeadDim / VN;           // 16-byte groups per 64-dim row (8 fp16, 16 fp32)
+    constexpr int KG = 128 / DG;                // key groups of the P.V pass
+    static_assert(CH == 128, "one key per thread");
     __shared__ float q[kHeadDim];
     __shared__ float p[CH];
-    __shared__ float accs[2][kHeadDim];
+    __shared__ float red[KG][kHeadDim];
     __shared__ float sh[32];
     __shared__ int s_last;
     const int h = blockIdx.x, sp = blockIdx.y, r = blockIdx.z, tid = threadIdx.x;
@@ -356,52 +360,64 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
     if (sp >= nsplit) return;
     const int slot = a.rows.slot[r];
     if (tid < kHeadDim) q[tid] = a.qkv[(size_t)r * a.qkv_stride + h * kHeadDim + tid] * 0.125f;  // 1/sqrt(64)
-    __syncthreads();
     const long long base = (long long)slot * a.kv.slot_stride + (long long)a.layer * a.kv.layer_stride +
                            (long long)h * a.kv.max_seq * kHeadDim;
     const KT *K = reinterpret_cast<const KT *>(a.kv.k) + base;
     const KT *V = reinterpret_cast<const KT *>(a.kv.v) + base;
     const int j0 = sp * CH;
     const int nj = min(CH, T - j0);
-
-    // scores: two threads per key, 32 dims each
-    const int key = tid >> 1, half = tid & 1;
-    float s = -FLT_MAX;
-    if (key < nj) {
-        const KT *kr = K + (size_t)(j0 + key) * kHeadDim + half * 32;
-        const float *qh = q + half * 32;
-        float d = 0.0f;
-        constexpr int VN = 16 / sizeof(KT);
+    // scores: one key per thread, its 64 dims in 16-byte loads issued together
+    uint4 kw[DG];
+    if (tid < nj) {
+        const uint4 *kr = reinterpret_cast<const uint4 *>(K + (size_t)(j0 + tid) * kHeadDim);
 #pragma unroll
-        for (int i = 0; i < 32; i += VN) d += dot_vec(*reinterpret_cast<const uint4 *>(kr + i), qh + i, KT());
+        for (int i = 0; i < DG; ++i) kw[i] = kr[i];
+    }
+    __syncthreads();   // q
+    float s = -FLT_MAX;
+    if (tid < nj) {
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DG; ++i) d += dot_vec(kw[i], q + i * VN, KT());
         s = d;
     }
-    s += __shfl_xor_sync(0xffffffffu, key < nj ? s : 0.0f, 1) * (key < nj ? 1.0f : 0.0f);
     const float m = block_max(s, sh);
-    const float e = key < nj ? expf(s - m) : 0.0f;
-    if (half == 0 && key < CH) p[key] = e;
-    const float l = block_sum(half == 0 ? e : 0.0f, sh);
+    const float e = tid < nj ? expf(s - m) : 0.0f;
+    p[tid] = e;
+    const float l = block_sum(e, sh);   // its barriers also publish p
+    // P.V: thread (kg, dg) sums keys kg, kg + KG, ... of dims dg * VN .. dg * VN + VN - 1
+    const int dg = tid % DG, kg = tid / DG;
+    float o[VN], o2[VN];
+#pragma unroll
+    for (int i = 0; i < VN; ++i) o[i] = o2[i] = 0.0f;
+    int jj = kg;
+    for (; jj + KG < nj; jj += 2 * KG) {   // two keys in flight
+        const uint4 v0 = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN);
+        const uint4 v1 = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj + KG) * kHeadDim + dg * VN);
+        fma_vec(o, v0, p[jj], KT());
+        fma_vec(o2, v1, p[jj + KG], KT());
+    }
+    if (jj < nj) fma_vec(o, *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN), p[jj], KT());
+#pragma unroll
+    for (int i = 0; i < VN; ++i) red[kg][dg * VN + i] = o[i] + o2[i];
     __syncthreads();
-    // P.V: thread (d, part) sums keys part*32 .. part*32+31
-    const int d = tid & 63, part = tid >> 6;
-    float o = 0.0f;
-    const int jend = min(nj, part * 32 + 32);
-    for (int jj = part * 32; jj < jend; ++jj) o = fmaf(p[jj], tof(V[(size_t)(j0 + jj) * kHeadDim + d]), o);
-    accs[part][d] = o;
-    __syncthreads();
+    float acc = 0.0f;
+    if (tid < kHeadDim)
+#pragma unroll
+        for (int g = 0; g < KG; ++g) acc += red[g][tid];
     const float* none = nullptr;
     (void)none;
     if (nsplit == 1) {
         if (tid < kHeadDim) {
             const size_t o = (size_t)r * a.out_stride + h * kHeadDim + tid;
-            const float v = (accs[0][tid] + accs[1][tid]) / l;
+            const float v = acc / l;
             a.out[o] = v;
             put_operand(a.op, o, v);
         }
         return;
     }
     float *P = a.partial + (((size_t)r * NH + h) * a.max_splits + sp) * (kHeadDim + 2);
-    if (tid < kHeadDim) P[2 + tid] = accs[0][tid] + accs[1][tid];
+    if (tid < kHeadDim) P[2 + tid] = acc;
     if (tid == 0) {
         P[0] = m;
         P[1] = l;
