@@ -7,6 +7,15 @@
 
 namespace g2 {
 
+// Programmatic dependent launch: a kernel launched with it may start while
+// the previous kernel of the stream is still running.  pdl_wait() returns once
+// that kernel has completed and its writes are visible (a no-op for a normal
+// launch); every such kernel calls it before reading anything a previous
+// kernel wrote, and before writing anything a previous kernel reads.
+// pdl_launch() lets the next kernel start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 __device__ __forceinline__ float tof(float v) { return v; }
 __device__ __forceinline__ float tof(__half v) { return __half2float(v); }
 template <typename T>

@@ -9,6 +9,26 @@
 
 namespace g2 {
 
+// Launch a kernel with programmatic dependent launch (it may start while the
+// previous kernel of the stream finishes; it calls pdl_wait() before touching
+// that kernel's data).  G2_NO_PDL=1 turns it off (plain stream order).
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 constexpr int kHeadDim = 64;        // GPT-2 head size (all family members)
 constexpr int kAttnChunk = 128;     // keys per attention CTA (flash-decoding split)
 constexpr int kMaxSeq = 1024;       // KV positions per slot (main.c:51)

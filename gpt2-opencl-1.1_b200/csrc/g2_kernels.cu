@@ -22,6 +22,7 @@
 // load).  Summation orders differ from the reference (parallel reductions);
 // parity is checked against the oracle within the stated tolerances.
 #include <cfloat>
+#include <cstdlib>
 #include <climits>
 
 #include "g2_device.cuh"
@@ -134,6 +135,8 @@ __device__ __forceinline__ float dot_vec(uint4 w, const float *xs, __half) {
 // ------------------------------------------------------------------------------
 template <typename WT>
 __global__ void embed_kernel(const WT *wte, const WT *wpe, Rows rows, float *h, int E, int V, int n_pos) {
+    pdl_wait();
+    pdl_launch();
     const int r = blockIdx.x;
     // ids and positions are validated on the host; clamp so that a bad value
     // can never address outside the tables
@@ -146,6 +149,8 @@ __global__ void embed_kernel(const WT *wte, const WT *wpe, Rows rows, float *h, 
 template <typename WT>
 __global__ void __launch_bounds__(256) layernorm_kernel(const float *x, float *out, const WT *g, const WT *b, int E,
                                                         OperandOut op) {
+    pdl_wait();
+    pdl_launch();
     __shared__ float sh[32];
     const float *xr = x + (size_t)blockIdx.x * E;
     float mean, rstd;
@@ -174,6 +179,8 @@ struct GemvArgs {
 
 template <typename WT>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs<WT> a) {
+    pdl_wait();
+    pdl_launch();
     constexpr int VN = Vec<WT>::n, BN = 16 * VN;
     extern __shared__ float smem[];
     __shared__ float sh[32];
@@ -257,6 +264,8 @@ struct GemmArgs {
 
 template <typename WT, int BM, bool BT>
 __global__ void __launch_bounds__(256) gemm_kernel(GemmArgs<WT> a) {
+    pdl_wait();
+    pdl_launch();
     constexpr int BN = 64, BK = 16, TM = BM / 16;
     __shared__ __align__(16) float As[BK][BM + 4];
     __shared__ __align__(16) float Bs[BK][BN + 4];
@@ -343,6 +352,8 @@ struct AttnArgs {
 
 template <typename KT>
 __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
+    pdl_wait();
+    pdl_launch();
     constexpr int CH = kAttnChunk;              // keys per CTA: one per thread in the score pass
     constexpr int VN = 16 / sizeof(KT);         // elements per 16-byte load
     constexpr int DG = kHeadDim / VN;           // 16-byte groups per 64-dim row (8 fp16, 16 fp32)
@@ -473,6 +484,8 @@ constexpr int kLmBlocks = 148 * 4;
 
 template <typename WT>
 __global__ void __launch_bounds__(256) lm_head_kernel(LmArgs<WT> a) {
+    pdl_wait();
+    pdl_launch();
     constexpr int VN = Vec<WT>::n;
     extern __shared__ float xs[];
     __shared__ float sh[32];
@@ -546,6 +559,8 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmArgs<WT> a) {
 __global__ void __launch_bounds__(256) argmax_rows_kernel(const float *logits, int V, int Vp, int forbid_eos,
                                                           int *tokens, float *values, int *tok_next, int *pos_next,
                                                           int *out_tokens, int out_stride, const int *step_ptr) {
+    pdl_wait();
+    pdl_launch();
     __shared__ float wv[8];
     __shared__ int wi[8];
     const int r = blockIdx.x, tid = threadIdx.x;
@@ -607,9 +622,15 @@ __global__ void __launch_bounds__(256) argmax_rows_kernel(const float *logits, i
 }
 
 __global__ void copy_kernel(const float *src, float *dst, int n) {
+    pdl_wait();
+    pdl_launch();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) dst[i] = src[i];
 }
-__global__ void step_advance_kernel(int *step) { *step += 1; }
+__global__ void step_advance_kernel(int *step) {
+    pdl_wait();
+    pdl_launch();
+    *step += 1;
+}
 
 // ------------------------------------------------------------------------------
 // launchers
@@ -617,13 +638,13 @@ __global__ void step_advance_kernel(int *step) { *step += 1; }
 template <typename WT>
 void launch_embed(const WT *wte, const WT *wpe, Rows rows, float *h, int E, int V, int n_pos, int nrows,
                   cudaStream_t st) {
-    embed_kernel<WT><<<nrows, 256, 0, st>>>(wte, wpe, rows, h, E, V, n_pos);
+    launch_pdl(embed_kernel<WT>, dim3(nrows), dim3(256), 0, st, wte, wpe, rows, h, E, V, n_pos);
 }
 
 template <typename WT>
 void launch_layernorm(const float *x, float *out, const WT *g, const WT *b, int E, int nrows, cudaStream_t st,
                       OperandOut op) {
-    layernorm_kernel<WT><<<nrows, 256, 0, st>>>(x, out, g, b, E, op);
+    launch_pdl(layernorm_kernel<WT>, dim3(nrows), dim3(256), 0, st, x, out, g, b, E, op);
 }
 
 template <typename WT>
@@ -668,7 +689,7 @@ void launch_gemv(const float *x, const WT *W, const WT *bias, const float *resid
     a.e.E = N / 3;
     const size_t smem = (size_t)(K / plan.ksplit + 16 * BN) * sizeof(float);
     dim3 grid(plan.tiles, plan.ksplit);
-    gemv_kernel<WT><<<grid, 256, smem, st>>>(a);
+    launch_pdl(gemv_kernel<WT>, grid, dim3(256), smem, st, a);
 }
 
 template <typename WT>
@@ -692,10 +713,10 @@ void launch_gemm_rows(const float *A, const WT *W, const WT *bias, const float *
     a.e.E = N / 3;
     if (M <= 32) {
         dim3 grid((N + 63) / 64, (M + 31) / 32);
-        gemm_kernel<WT, 32, false><<<grid, 256, 0, st>>>(a);
+        launch_pdl(gemm_kernel<WT, 32, false>, grid, dim3(256), 0, st, a);
     } else {
         dim3 grid((N + 63) / 64, (M + 63) / 64);
-        gemm_kernel<WT, 64, false><<<grid, 256, 0, st>>>(a);
+        launch_pdl(gemm_kernel<WT, 64, false>, grid, dim3(256), 0, st, a);
     }
 }
 
@@ -723,7 +744,7 @@ void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int 
     a.max_splits = (kv.max_seq + kAttnChunk - 1) / kAttnChunk;
     const int splits = max_pos_hint < 0 ? a.max_splits : (max_pos_hint + kAttnChunk) / kAttnChunk;
     dim3 grid(kv.n_head, splits, nrows);
-    attn_kernel<KT><<<grid, 128, 0, st>>>(a);
+    launch_pdl(attn_kernel<KT>, grid, dim3(128), 0, st, a);
 }
 
 int lm_head_blocks() { return kLmBlocks; }
@@ -737,6 +758,14 @@ __global__ void set_ints_kernel(int *p, int a, int b, int c, int d) {
     p[3] = d;
 }
 void launch_set_ints(int *p, int a, int b, int c, int d, cudaStream_t st) { set_ints_kernel<<<1, 1, 0, st>>>(p, a, b, c, d); }
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *v = getenv("G2_NO_PDL");
+        return !(v && v[0] == '1');
+    }();
+    return on;
+}
 
 template <typename WT>
 void launch_lm_head(const float *x, const WT *wte, const WT *lnf_g, const WT *lnf_b, float *logits, int E, int V,
@@ -758,7 +787,7 @@ void launch_lm_head(const float *x, const WT *wte, const WT *lnf_g, const WT *ln
     a.result = result;
     a.state = state;
     a.out_tokens = out_tokens;
-    lm_head_kernel<WT><<<kLmBlocks, 256, (size_t)E * sizeof(float), st>>>(a);
+    launch_pdl(lm_head_kernel<WT>, dim3(kLmBlocks), dim3(256), (size_t)E * sizeof(float), st, a);
 }
 
 template <typename WT>
@@ -778,24 +807,24 @@ void launch_lm_head_rows(const float *x, const WT *wte, float *logits, int E, in
     a.e.E = 0;
     if (nrows <= 32) {
         dim3 grid((V + 63) / 64, (nrows + 31) / 32);
-        gemm_kernel<WT, 32, true><<<grid, 256, 0, st>>>(a);
+        launch_pdl(gemm_kernel<WT, 32, true>, grid, dim3(256), 0, st, a);
     } else {
         dim3 grid((V + 63) / 64, (nrows + 63) / 64);
-        gemm_kernel<WT, 64, true><<<grid, 256, 0, st>>>(a);
+        launch_pdl(gemm_kernel<WT, 64, true>, grid, dim3(256), 0, st, a);
     }
 }
 
 void launch_argmax_rows(const float *logits, int V, int Vp, int nrows, int forbid_eos, int *tokens, float *values,
                         int *tok_next, int *pos_next, int *out_tokens, int out_stride, const int *step_ptr,
                         cudaStream_t st) {
-    argmax_rows_kernel<<<nrows, 256, 0, st>>>(logits, V, Vp, forbid_eos, tokens, values, tok_next, pos_next,
+    launch_pdl(argmax_rows_kernel, dim3(nrows), dim3(256), 0, st, logits, V, Vp, forbid_eos, tokens, values, tok_next, pos_next,
                                               out_tokens, out_stride, step_ptr);
 }
 
 void launch_copy_row(const float *src, float *dst, int n, cudaStream_t st) {
-    copy_kernel<<<(n + 255) / 256, 256, 0, st>>>(src, dst, n);
+    launch_pdl(copy_kernel, dim3((n + 255) / 256), dim3(256), 0, st, src, dst, n);
 }
-void launch_step_advance(int *step_ptr, cudaStream_t st) { step_advance_kernel<<<1, 1, 0, st>>>(step_ptr); }
+void launch_step_advance(int *step_ptr, cudaStream_t st) { launch_pdl(step_advance_kernel, dim3(1), dim3(1), 0, st, step_ptr); }
 
 // explicit instantiations
 #define G2_INST(WT)                                                                                                   \

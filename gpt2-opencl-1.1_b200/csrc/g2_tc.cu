@@ -202,8 +202,37 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         // ---- TMA producer ----
-        int issued = 0;
-        for (int i = 0; i < nkb; ++i) {
+        // The weights are no earlier kernel's output: the first stages' weight
+        // tiles are requested before waiting for the previous kernel, the rows
+        // (its output) after.
+        const int pre = nkb < STAGES ? nkb : STAGES;
+        for (int i = 0; i < pre; ++i) {
+            unsigned char *st = base + (size_t)i * C::STAGE;
+            const int k = (kb0 + i) * S::BK;
+            mbar_expect_tx(&full[i], C::STAGE);
+#pragma unroll
+            for (int p = 0; p < S::NPASS; ++p) {
+                if (AK) {
+                    tma_load_2d(st + p * S::A_BYTES, p ? &mw_lo : &mw_hi, k, f0, &full[i]);
+                } else {
+#pragma unroll
+                    for (int b = 0; b < S::NBOX; ++b)
+                        tma_load_2d(st + p * S::A_BYTES + b * (S::BK * 128), p ? &mw_lo : &mw_hi, f0 + b * S::BOX_F,
+                                    k, &full[i]);
+                }
+            }
+        }
+        pdl_wait();
+        pdl_launch();
+        for (int i = 0; i < pre; ++i) {
+            unsigned char *st = base + (size_t)i * C::STAGE;
+            const int k = (kb0 + i) * S::BK;
+#pragma unroll
+            for (int p = 0; p < S::NPASS; ++p)
+                tma_load_2d(st + S::NPASS * S::A_BYTES + p * C::B_BYTES, p ? &mx_lo : &mx_hi, k, r0, &full[i]);
+        }
+        int issued = pre;
+        for (int i = pre; i < nkb; ++i) {
             const int s = i % STAGES;
             if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) {
                 atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
@@ -230,7 +259,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // every copy issued must land before the CTA may exit
         for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
-    } else if (threadIdx.x == 32) {
+    } else {
+        pdl_wait();
+        pdl_launch();
+    }
+    if (threadIdx.x == 32) {
         // ---- MMA issuer ----
         constexpr unsigned idesc = make_idesc<KIND, BN, AK>();
         for (int i = 0; i < nkb; ++i) {
@@ -294,6 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // per thread (N % 4 == 0); used when a GEMM ran with split-K.
 template <typename WT>
 __global__ void tc_reduce_kernel(const float *part, int splits, int R, int N, Epi<WT> e, OperandOut op) {
+    pdl_wait();
+    pdl_launch();
     const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
     const long long total = (long long)R * N;
     if (i >= total) return;
@@ -383,8 +418,8 @@ void launch_kernel(const TcWeights &w, const TcRowsOperand &x, int bn_idx, const
         cudaFuncSetAttribute(tc_gemm_kernel<KIND, BN, WT, AK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     }
     dim3 grid((a.N + kTcTileF - 1) / kTcTileF, (a.R + BN - 1) / BN, a.splits);
-    tc_gemm_kernel<KIND, BN, WT, AK><<<grid, kThreads, C::SMEM, st>>>(w.hi, KIND == TC_TF32X3 ? w.lo : w.hi, x.hi[bn_idx],
-                                                                KIND == TC_TF32X3 ? x.lo[bn_idx] : x.hi[bn_idx], a);
+    launch_pdl(tc_gemm_kernel<KIND, BN, WT, AK>, grid, dim3(kThreads), C::SMEM, st, w.hi, KIND == TC_TF32X3 ? w.lo : w.hi,
+               x.hi[bn_idx], KIND == TC_TF32X3 ? x.lo[bn_idx] : x.hi[bn_idx], a);
 }
 
 }  // namespace
@@ -524,7 +559,8 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
     }
     if (p.splits == 1) return 1;   // the GEMM applied the epilogue itself
     const long long n4 = (long long)R * w.N / 4;
-    tc_reduce_kernel<WT><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(partial, p.splits, R, w.N, a.e, op);
+    launch_pdl(tc_reduce_kernel<WT>, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, st, (const float *)partial, p.splits,
+               R, w.N, a.e, op);
     return 2;
 }
 
