@@ -129,6 +129,7 @@ struct g2_engine {
     int mega_grid = 0;
     int mega_cw[2] = {0, 0};   // strip widths of c_attn and c_fc
     int mega_nq = 0;           // attn.c_proj column slices per head
+    bool lnf_done = false;     // the last many-row pass wrote the ln_f operand of its rows
     size_t mega_smem = 0;
     // tensor-core GEMMs of the many-row passes (prefill, batched decode)
     bool tc = false;
@@ -763,19 +764,25 @@ static OperandOut operand_f(const g2_engine *e) {
 
 // One projection of a many-row pass: out[r] = epilogue(X[r] W), on the tensor
 // cores (X already written as the operand by its producer) or by the SIMT GEMM.
+// With ln_g / ln_b (the LayerNorm that follows this residual-stream update),
+// a split-K tensor-core GEMM also writes the LayerNorm of its output rows as
+// ln_op; returns whether it did (else the caller runs the LayerNorm).
 template <typename WT>
-static void rows_gemm(g2_engine *e, int l, int q, const float *X, int nrows, const WT *W, const WT *bias,
+static bool rows_gemm(g2_engine *e, int l, int q, const float *X, int nrows, const WT *W, const WT *bias,
                       const float *resid, float *out, int N, int K, int epi, const KVLayout *kv, Rows rows,
-                      OperandOut op = OperandOut()) {
+                      OperandOut op = OperandOut(), const WT *ln_g = nullptr, const WT *ln_b = nullptr,
+                      OperandOut ln_op = OperandOut()) {
+    bool ln_done = false;
     if (e->tc) {
         e->launches += launch_tc_gemm<WT>(e->tc_kind, e->tc_maps[(size_t)l * 4 + q],
                                           K == e->c.n_embd ? e->tc_x_e : e->tc_x_f, nrows, e->tc_part,
                                           e->tc_part_floats, e->tc_ctr, e->tc_err, bias, resid, out, epi, kv, l, rows,
-                                          e->sms, e->st, op);
+                                          e->sms, e->st, op, 0, ln_g, ln_b, ln_op, &ln_done);
     } else {
         launch_gemm_rows<WT>(X, W, bias, resid, out, nrows, N, K, epi, kv, l, rows, e->st);
         e->launches += 1;
     }
+    return ln_done;
 }
 
 // All layers over `nrows` rows described by the device row arrays (prefill of
@@ -791,22 +798,35 @@ static int forward_rows(g2_engine *e, int nrows, int max_pos) {
     Rows rows{e->rows_tok, e->rows_pos, e->rows_slot};
     const OperandOut ope = operand_e(e), opf = operand_f(e);
     launch_embed<WT>(e->w<WT>(e->wte), e->w<WT>(e->wpe), rows, e->h, E, c.vocab_size, c.n_ctx, nrows, st);
+    e->launches += 1;
+    bool ln1_done = false;   // the previous layer's fc2 wrote this layer's ln_1 operand
     for (int l = 0; l < c.n_layer; ++l) {
         const LayerOff &o = e->L[l];
-        launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln1_g), e->w<WT>(o.ln1_b), E, nrows, st, ope);
+        if (!ln1_done) {
+            launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln1_g), e->w<WT>(o.ln1_b), E, nrows, st, ope);
+            e->launches += 1;
+        }
         rows_gemm<WT>(e, l, 0, e->xln, nrows, e->w<WT>(o.qkv_w), e->w<WT>(o.qkv_b), nullptr, e->qkv, 3 * E, E,
                       EPI_BIAS | EPI_KV, &e->kv, rows);
         launch_attention<WT>(e->qkv, 3 * E, e->kv, l, rows, nrows, e->attn, E, e->attn_partial, e->attn_ctr, max_pos,
                              st, ope);
-        rows_gemm<WT>(e, l, 1, e->attn, nrows, e->w<WT>(o.proj_w), e->w<WT>(o.proj_b), e->h, e->h, E, E,
-                      EPI_BIAS | EPI_RESID, nullptr, rows);
-        launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln2_g), e->w<WT>(o.ln2_b), E, nrows, st, ope);
+        e->launches += 1;
+        const bool ln2_done = rows_gemm<WT>(e, l, 1, e->attn, nrows, e->w<WT>(o.proj_w), e->w<WT>(o.proj_b), e->h,
+                                            e->h, E, E, EPI_BIAS | EPI_RESID, nullptr, rows, OperandOut(),
+                                            e->w<WT>(o.ln2_g), e->w<WT>(o.ln2_b), ope);
+        if (!ln2_done) {
+            launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln2_g), e->w<WT>(o.ln2_b), E, nrows, st, ope);
+            e->launches += 1;
+        }
         rows_gemm<WT>(e, l, 2, e->xln, nrows, e->w<WT>(o.fc_w), e->w<WT>(o.fc_b), nullptr, e->ffn, F, E,
                       EPI_BIAS | EPI_GELU, nullptr, rows, opf);
-        rows_gemm<WT>(e, l, 3, e->ffn, nrows, e->w<WT>(o.fc2_w), e->w<WT>(o.fc2_b), e->h, e->h, E, F,
-                      EPI_BIAS | EPI_RESID, nullptr, rows);
+        // the next LayerNorm: ln_1 of layer l + 1, or ln_f after the last layer
+        const bool last = l + 1 == c.n_layer;
+        const WT *ng = e->w<WT>(last ? e->lnf_g : e->L[l + 1].ln1_g), *nb = e->w<WT>(last ? e->lnf_b : e->L[l + 1].ln1_b);
+        ln1_done = rows_gemm<WT>(e, l, 3, e->ffn, nrows, e->w<WT>(o.fc2_w), e->w<WT>(o.fc2_b), e->h, e->h, E, F,
+                                 EPI_BIAS | EPI_RESID, nullptr, rows, OperandOut(), ng, nb, ope);
     }
-    e->launches += 1 + 3LL * c.n_layer;
+    e->lnf_done = ln1_done;
     CKL();
     return G2_OK;
 }
@@ -817,7 +837,10 @@ static int forward_rows(g2_engine *e, int nrows, int max_pos) {
 template <typename WT>
 static void lm_head_rows(g2_engine *e, int nrows) {
     const ModelConfig &c = e->c;
-    launch_layernorm<WT>(e->h, e->xln, e->w<WT>(e->lnf_g), e->w<WT>(e->lnf_b), c.n_embd, nrows, e->st, operand_e(e));
+    if (!(e->tc && e->lnf_done)) {   // else the last fc2 wrote the ln_f operand
+        launch_layernorm<WT>(e->h, e->xln, e->w<WT>(e->lnf_g), e->w<WT>(e->lnf_b), c.n_embd, nrows, e->st, operand_e(e));
+        e->launches += 1;
+    }
     if (e->tc) {
         Rows rows{e->rows_tok, e->rows_pos, e->rows_slot};
         e->launches += launch_tc_gemm<WT>(e->tc_kind, e->tc_lm, e->tc_x_e, nrows, e->tc_part, e->tc_part_floats,
@@ -828,7 +851,6 @@ static void lm_head_rows(g2_engine *e, int nrows) {
                                 nrows, e->st);
         e->launches += 1;
     }
-    e->launches += 1;
 }
 
 // LM head on row `row` of e->h for `slot`, optionally advancing the step state.

@@ -347,6 +347,74 @@ __global__ void tc_reduce_kernel(const float *part, int splits, int R, int N, Ep
     put_operand(op, (size_t)i + 3, e.apply(r, n + 3, acc.w));
 }
 
+// The same for a GEMM whose output rows (the residual stream) feed a
+// LayerNorm: one CTA per row sums the splits, applies the epilogue (out =
+// the residual stream), then takes the row's LayerNorm (math.cl:283-311:
+// mean, then the mean square deviation, eps 1e-5) and writes the normalised
+// row, times gamma plus beta, as the next GEMM's operand.  N % 4 == 0,
+// N <= 2048.
+template <typename WT>
+__global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, int splits, int R, int N, Epi<WT> e,
+                                                           const WT *g, const WT *b, OperandOut op) {
+    pdl_wait();
+    pdl_launch();
+    __shared__ float sh[8];
+    const int r = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const long long total = (long long)R * N;
+    float v[8];
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int n = (t + k * 256) * 4;
+        if (n < N) {
+            const long long i = (long long)r * N + n;
+            float4 acc = *reinterpret_cast<const float4 *>(part + i);
+            for (int sp = 1; sp < splits; ++sp) {
+                const float4 p = *reinterpret_cast<const float4 *>(part + (size_t)sp * total + i);
+                acc.x += p.x;
+                acc.y += p.y;
+                acc.z += p.z;
+                acc.w += p.w;
+            }
+            v[4 * k] = e.apply(r, n, acc.x);
+            v[4 * k + 1] = e.apply(r, n + 1, acc.y);
+            v[4 * k + 2] = e.apply(r, n + 2, acc.z);
+            v[4 * k + 3] = e.apply(r, n + 3, acc.w);
+            s += (v[4 * k] + v[4 * k + 1]) + (v[4 * k + 2] + v[4 * k + 3]);
+        }
+    }
+    auto block_sum = [&](float x) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        __syncthreads();
+        if (lane == 0) sh[warp] = x;
+        __syncthreads();
+        float y = lane < 8 ? sh[lane] : 0.0f;   // every lane ends with the total
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
+        return y;
+    };
+    const float mean = block_sum(s) / (float)N;
+    float q = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+        if ((t + k * 256) * 4 < N)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float d = v[4 * k + j] - mean;
+                q = fmaf(d, d, q);
+            }
+    const float rstd = 1.0f / sqrtf(block_sum(q) / (float)N + 1e-5f);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int n = (t + k * 256) * 4;
+        if (n < N)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                put_operand(op, (size_t)r * N + n + j, (v[4 * k + j] - mean) * rstd * tof(g[n + j]) + tof(b[n + j]));
+    }
+}
+
 // x -> (hi, lo) tf32 pair, or x -> fp16.
 __global__ void tc_prep_kernel(int kind, const float4 *x, float4 *hi, float4 *lo, __half2 *h16, long long n4) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
@@ -504,7 +572,8 @@ size_t tc_partial_floats(int R_max, int N, int K, int kind, int sms) {
 template <typename WT>
 int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, float *partial, size_t partial_floats,
                    unsigned *tile_ctr, int *err, const WT *bias, const float *resid, float *out, int epi,
-                   const KVLayout *kv, int layer, Rows rows, int sms, cudaStream_t st, OperandOut op, int out_stride) {
+                   const KVLayout *kv, int layer, Rows rows, int sms, cudaStream_t st, OperandOut op, int out_stride,
+                   const WT *ln_g, const WT *ln_b, OperandOut ln_op, bool *ln_done) {
     const int bk = kind == TC_TF32X3 ? 32 : 64;
     const int kb_total = w.K / bk;
     TcPlan p = plan(R, w.N, kb_total, sms);
@@ -557,7 +626,14 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
         else if (p.bn == 64) launch_kernel<TC_F16, 64, WT, false>(w, x, bi, a, st);
         else launch_kernel<TC_F16, 128, WT, false>(w, x, bi, a, st);
     }
+    if (ln_done) *ln_done = false;
     if (p.splits == 1) return 1;   // the GEMM applied the epilogue itself
+    if (ln_g && w.N <= 2048 && (w.N % 4) == 0) {   // sum the splits, epilogue and the next LayerNorm in one kernel
+        launch_pdl(tc_reduce_ln_kernel<WT>, dim3((unsigned)R), dim3(256), 0, st, (const float *)partial, p.splits, R, w.N,
+                   a.e, ln_g, ln_b, ln_op);
+        if (ln_done) *ln_done = true;
+        return 2;
+    }
     const long long n4 = (long long)R * w.N / 4;
     launch_pdl(tc_reduce_kernel<WT>, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, st, (const float *)partial, p.splits,
                R, w.N, a.e, op);
@@ -566,9 +642,9 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
 
 template int launch_tc_gemm<float>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, unsigned *,
                                    int *, const float *, const float *, float *, int, const KVLayout *, int, Rows, int,
-                                   cudaStream_t, OperandOut, int);
+                                   cudaStream_t, OperandOut, int, const float *, const float *, OperandOut, bool *);
 template int launch_tc_gemm<__half>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, unsigned *,
                                     int *, const __half *, const float *, float *, int, const KVLayout *, int, Rows, int,
-                                    cudaStream_t, OperandOut, int);
+                                    cudaStream_t, OperandOut, int, const __half *, const __half *, OperandOut, bool *);
 
 }  // namespace g2

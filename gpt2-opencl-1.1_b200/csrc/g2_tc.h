@@ -62,12 +62,16 @@ constexpr int kTcMaxTiles = 4096;
 // epilogue from tensor memory (one launch); with split-K the partials go to
 // `partial` and one kernel sums them in split order (two launches).
 // `tile_ctr` is reserved (kTcMaxTiles zeroed counters).  out_stride > 0 sets
-// the row stride of out and resid (else N).  `err` receives an
+// the row stride of out and resid (else N).  With ln_g / ln_b, a split-K GEMM
+// also takes the LayerNorm of each output row (gamma ln_g, beta ln_b) and
+// writes it as ln_op, the next GEMM's operand; *ln_done then says whether it
+// did (a single-split GEMM does not: its caller runs the LayerNorm).  `err` receives an
 // error code if a wait inside the kernel expires.  Returns the launch count.
 template <typename WT>
 int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, float *partial, size_t partial_floats,
                    unsigned *tile_ctr, int *err, const WT *bias, const float *resid, float *out, int epi,
                    const KVLayout *kv, int layer, Rows rows, int sms, cudaStream_t st, OperandOut op = OperandOut(),
-                   int out_stride = 0);
+                   int out_stride = 0, const WT *ln_g = nullptr, const WT *ln_b = nullptr, OperandOut ln_op = OperandOut(),
+                   bool *ln_done = nullptr);
 
 }  // namespace g2
