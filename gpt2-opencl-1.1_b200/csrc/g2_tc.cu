@@ -26,6 +26,7 @@
 // is bounded; on expiry the kernel records G2_ERR_TIMEOUT in *err, drains its
 // own copies, frees its tensor memory and returns.
 #include <cstdio>
+#include <cstdlib>
 
 #include "g2_device.cuh"
 #include "g2_tc.h"
@@ -580,6 +581,18 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
     if (w.N % 4) {   // the reduce kernel works in float4s: no split-K (the LM head's 393 tiles need none)
         p.splits = 1;
         p.kb_per = kb_total;
+    }
+    // Split caps measured on B200 for 32-row batched steps: more splits add
+    // partial-tile traffic and reduce time faster than they add streaming
+    // CTAs.  A reduce fused with a LayerNorm (one CTA per row) takes up to 8;
+    // a plain reduce up to 3 (fp16) or 2 (3xTF32, twice the partial bytes
+    // per weight byte).
+    {
+        const int cap = ln_g ? 8 : kind == TC_TF32X3 ? 2 : 3;
+        if (p.splits > cap) {
+            p.kb_per = (kb_total + cap - 1) / cap;
+            p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
+        }
     }
     // fewer splits if the scratch is smaller than the plan needs (one split needs none)
     while (p.splits > 1 && (size_t)p.splits * R * w.N > partial_floats) {
