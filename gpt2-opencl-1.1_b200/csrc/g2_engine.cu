@@ -484,7 +484,7 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
         int *cw = e->mega_cw;
         cw[0] = mega_cw(3 * E, G);
         cw[1] = mega_cw(F, G);
-        e->mega_nq = mega_nq(E);
+        e->mega_nq = mega_nq(E, e->c.n_head, G);
         if (const char *nq = getenv("G2_MEGA_NQ"))
             if (mega_nq_ok(E, atoi(nq))) e->mega_nq = atoi(nq);
         // every row (E floats) fits a ring slot, an E-wide block has at most one

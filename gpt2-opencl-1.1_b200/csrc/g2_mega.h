@@ -88,8 +88,11 @@ inline int mega_lm_rows(int E) {
 // Column slices of attn.c_proj per head (B units = NH * nq): a slice is a
 // whole number of float4 groups, at most one per consumer thread.
 inline bool mega_nq_ok(int E, int nq) { return nq >= 1 && E % nq == 0 && (E / nq) % 4 == 0 && E / nq / 4 <= 480; }
-// Default: the largest of 4, 3, 2, 1 that is valid (G2_MEGA_NQ overrides).
-inline int mega_nq(int E) {
+// Default: 8 (measured best for GPT-2 small: one ring chunk of attn.c_proj
+// per B unit), else the largest of 4, 3, 2, 1 that is valid, keeping NH * nq
+// within the G CTAs (G2_MEGA_NQ overrides).
+inline int mega_nq(int E, int NH, int G) {
+    if (mega_nq_ok(E, 8) && NH * 8 <= G) return 8;
     for (int nq = 4; nq >= 1; --nq)
         if (mega_nq_ok(E, nq)) return nq;
     return 0;
