@@ -786,12 +786,14 @@ static bool rows_gemm(g2_engine *e, int l, int q, const float *X, int nrows, con
 }
 
 // All layers over `nrows` rows described by the device row arrays (prefill of
-// one slot, or one decode token for each of several slots).  Leaves the
-// residual stream in e->h.  With the tensor cores, LayerNorm and attention
-// write the next GEMM's operand themselves and fc writes fc2's, so a layer is
-// seven launches.
+// one slot, or one decode token for each of several slots: decode_rows).
+// Leaves the residual stream in e->h.  With the tensor cores, LayerNorm and
+// attention write the next GEMM's operand themselves, fc writes fc2's, the
+// residual-stream reduces take the next LayerNorm, and for decode rows the
+// attention sums c_attn's split-K partials itself: a layer is five to seven
+// launches.
 template <typename WT>
-static int forward_rows(g2_engine *e, int nrows, int max_pos) {
+static int forward_rows(g2_engine *e, int nrows, int max_pos, bool decode_rows = false) {
     const ModelConfig &c = e->c;
     const int E = c.n_embd, F = c.ffn_dim;
     cudaStream_t st = e->st;
@@ -806,10 +808,24 @@ static int forward_rows(g2_engine *e, int nrows, int max_pos) {
             launch_layernorm<WT>(e->h, e->xln, e->w<WT>(o.ln1_g), e->w<WT>(o.ln1_b), E, nrows, st, ope);
             e->launches += 1;
         }
-        rows_gemm<WT>(e, l, 0, e->xln, nrows, e->w<WT>(o.qkv_w), e->w<WT>(o.qkv_b), nullptr, e->qkv, 3 * E, E,
-                      EPI_BIAS | EPI_KV, &e->kv, rows);
+        QkvPartials qp;
+        if (e->tc && decode_rows) {   // c_attn without its reduce: the attention sums the partials
+            int splits = 1;
+            e->launches += launch_tc_gemm<WT>(e->tc_kind, e->tc_maps[(size_t)l * 4], e->tc_x_e, nrows, e->tc_part,
+                                              e->tc_part_floats, e->tc_ctr, e->tc_err, e->w<WT>(o.qkv_b), nullptr,
+                                              e->qkv, EPI_BIAS | EPI_KV, &e->kv, l, rows, e->sms, st, OperandOut(), 0,
+                                              nullptr, nullptr, OperandOut(), nullptr, true, &splits);
+            if (splits > 1) {
+                qp.part = e->tc_part;
+                qp.splits = splits;
+                qp.bias = e->w<WT>(o.qkv_b);
+            }
+        } else {
+            rows_gemm<WT>(e, l, 0, e->xln, nrows, e->w<WT>(o.qkv_w), e->w<WT>(o.qkv_b), nullptr, e->qkv, 3 * E, E,
+                          EPI_BIAS | EPI_KV, &e->kv, rows);
+        }
         launch_attention<WT>(e->qkv, 3 * E, e->kv, l, rows, nrows, e->attn, E, e->attn_partial, e->attn_ctr, max_pos,
-                             st, ope);
+                             st, ope, qp);
         e->launches += 1;
         const bool ln2_done = rows_gemm<WT>(e, l, 1, e->attn, nrows, e->w<WT>(o.proj_w), e->w<WT>(o.proj_b), e->h,
                                             e->h, E, E, EPI_BIAS | EPI_RESID, nullptr, rows, OperandOut(),
@@ -1117,10 +1133,10 @@ extern "C" int g2_decode_batch(g2_engine *e, int n, const int *slots, const int 
     if ((rc = stage_rows(e, n, tokens, pos, slots))) return rc;
     const ModelConfig &c = e->c;
     if (e->dtype == G2_F32) {
-        if ((rc = forward_rows<float>(e, n, maxp))) return rc;
+        if ((rc = forward_rows<float>(e, n, maxp, true))) return rc;
         lm_head_rows<float>(e, n);
     } else {
-        if ((rc = forward_rows<__half>(e, n, maxp))) return rc;
+        if ((rc = forward_rows<__half>(e, n, maxp, true))) return rc;
         lm_head_rows<__half>(e, n);
     }
     for (int i = 0; i < n; ++i)
@@ -1265,7 +1281,7 @@ extern "C" int g2_generate(g2_engine *e, int slot, const int *prompt, int n_prom
 template <typename WT>
 static int record_batch_step(g2_engine *e, int n) {
     const ModelConfig &c = e->c;
-    int rc = forward_rows<WT>(e, n, -1);
+    int rc = forward_rows<WT>(e, n, -1, true);
     if (rc) return rc;
     lm_head_rows<WT>(e, n);
     launch_argmax_rows(e->logits_rows, c.vocab_size, c.padded_vocab, n, 1, nullptr, nullptr, e->rows_tok,

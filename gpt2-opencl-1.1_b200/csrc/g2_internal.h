@@ -111,10 +111,21 @@ void launch_gemm_rows(const float *A, const WT *W, const WT *bias, const float *
 // 0..pos[r] of its slot. partial/counters: scratch (see attn_workspace_*).
 size_t attn_partial_floats(int nrows, int n_head, int max_seq);
 size_t attn_counter_count(int nrows, int n_head);
+// The c_attn output of a batched decode step still as split-K partial tiles
+// ([splits][rows][3E], row stride qkv_stride) plus the c_attn bias: the
+// attention sums them itself (and appends the new K and V to the cache), so
+// the GEMM needs no reduce launch.  Only for rows of distinct sequences: a
+// row's attention then reads no K/V row that another row of the pass appends.
+struct QkvPartials {
+    const float *part = nullptr;
+    int splits = 0;
+    const void *bias = nullptr;   // [3E] of the engine's weight type
+};
+
 template <typename KT>
 void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
                       float *out, int out_stride, float *partial, unsigned *counters, int max_pos_hint,
-                      cudaStream_t st, OperandOut op = OperandOut());
+                      cudaStream_t st, OperandOut op = OperandOut(), QkvPartials qp = QkvPartials());
 
 // LM head on one row x (fp32 [E]) with the final LayerNorm fused:
 // logits[v] = LN_f(x) . wte[v]; argmax over v < V (first index on ties,

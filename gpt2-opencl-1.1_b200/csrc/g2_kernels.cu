@@ -348,6 +348,10 @@ struct AttnArgs {
     unsigned *counters;  // [rows][heads]
     int max_splits;
     OperandOut op;       // the output also as the next GEMM's operand (row stride out_stride)
+    const float *qpart;  // c_attn split-K partials [qsplits][rows][qkv_stride], or nullptr (qkv holds the sums)
+    int qsplits;
+    long long qtotal;    // rows * qkv_stride
+    const KT *qbias;     // c_attn bias [3E]
 };
 
 template <typename KT>
@@ -370,9 +374,33 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
     const int nsplit = (T + CH - 1) / CH;
     if (sp >= nsplit) return;
     const int slot = a.rows.slot[r];
-    if (tid < kHeadDim) q[tid] = a.qkv[(size_t)r * a.qkv_stride + h * kHeadDim + tid] * 0.125f;  // 1/sqrt(64)
+    const int pos = T - 1;
+    __shared__ float knew[2][kHeadDim];   // k and v at pos, when summed here from the c_attn partials
     const long long base = (long long)slot * a.kv.slot_stride + (long long)a.layer * a.kv.layer_stride +
                            (long long)h * a.kv.max_seq * kHeadDim;
+    const bool fused = a.qpart != nullptr;
+    if (!fused) {
+        if (tid < kHeadDim) q[tid] = a.qkv[(size_t)r * a.qkv_stride + h * kHeadDim + tid] * 0.125f;  // 1/sqrt(64)
+    } else {
+        // c_attn output = (sum of the splits in order) + bias, as its reduce would give
+        const int E = a.qkv_stride / 3;
+        const bool kv_here = sp == nsplit - 1;   // this chunk holds pos: it needs k, v and appends them
+        for (int c = tid; c < (kv_here ? 3 : 1) * kHeadDim; c += blockDim.x) {
+            const int part = c / kHeadDim, d = c % kHeadDim;   // 0 q, 1 k, 2 v
+            const size_t col = (size_t)part * E + h * kHeadDim + d;
+            float acc = a.qpart[(size_t)r * a.qkv_stride + col];
+            for (int sp2 = 1; sp2 < a.qsplits; ++sp2) acc += a.qpart[(size_t)sp2 * a.qtotal + (size_t)r * a.qkv_stride + col];
+            const float v = acc + tof(a.qbias[col]);
+            if (part == 0) {
+                q[d] = v * 0.125f;
+            } else {   // K / V append (split_kv, math.cl:367-383), kept at the cache's precision
+                const KT st = fromf<KT>(v);
+                KT *dst = reinterpret_cast<KT *>(part == 1 ? a.kv.k : a.kv.v) + base + (size_t)pos * kHeadDim + d;
+                *dst = st;
+                knew[part - 1][d] = tof(st);
+            }
+        }
+    }
     const KT *K = reinterpret_cast<const KT *>(a.kv.k) + base;
     const KT *V = reinterpret_cast<const KT *>(a.kv.v) + base;
     const int j0 = sp * CH;
@@ -384,12 +412,16 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
 #pragma unroll
         for (int i = 0; i < DG; ++i) kw[i] = kr[i];
     }
-    __syncthreads();   // q
+    __syncthreads();   // q (and k, v at pos)
     float s = -FLT_MAX;
     if (tid < nj) {
         float d = 0.0f;
+        if (fused && j0 + tid == pos) {   // the key this pass appended: from shared memory
+            for (int i = 0; i < kHeadDim; ++i) d = fmaf(knew[0][i], q[i], d);
+        } else {
 #pragma unroll
-        for (int i = 0; i < DG; ++i) d += dot_vec(kw[i], q + i * VN, KT());
+            for (int i = 0; i < DG; ++i) d += dot_vec(kw[i], q + i * VN, KT());
+        }
         s = d;
     }
     const float m = block_max(s, sh);
@@ -401,14 +433,24 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
     float o[VN], o2[VN];
 #pragma unroll
     for (int i = 0; i < VN; ++i) o[i] = o2[i] = 0.0f;
+    // (with fused c_attn partials the value at pos is taken from shared memory, not the cache)
+    const int jpos = fused ? pos - j0 : -1;
     int jj = kg;
     for (; jj + KG < nj; jj += 2 * KG) {   // two keys in flight
+        if (jj == jpos || jj + KG == jpos) break;
         const uint4 v0 = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN);
         const uint4 v1 = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj + KG) * kHeadDim + dg * VN);
         fma_vec(o, v0, p[jj], KT());
         fma_vec(o2, v1, p[jj + KG], KT());
     }
-    if (jj < nj) fma_vec(o, *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN), p[jj], KT());
+    for (; jj < nj; jj += KG) {
+        if (jj == jpos) {
+#pragma unroll
+            for (int i = 0; i < VN; ++i) o[i] = fmaf(p[jj], knew[1][dg * VN + i], o[i]);
+        } else {
+            fma_vec(o, *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN), p[jj], KT());
+        }
+    }
 #pragma unroll
     for (int i = 0; i < VN; ++i) red[kg][dg * VN + i] = o[i] + o2[i];
     __syncthreads();
@@ -729,9 +771,13 @@ size_t attn_counter_count(int nrows, int n_head) { return (size_t)nrows * n_head
 template <typename KT>
 void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
                       float *out, int out_stride, float *partial, unsigned *counters, int max_pos_hint,
-                      cudaStream_t st, OperandOut op) {
+                      cudaStream_t st, OperandOut op, QkvPartials qp) {
     AttnArgs<KT> a;
     a.op = op;
+    a.qpart = qp.part;
+    a.qsplits = qp.splits;
+    a.qtotal = (long long)nrows * qkv_stride;
+    a.qbias = reinterpret_cast<const KT *>(qp.bias);
     a.qkv = qkv;
     a.qkv_stride = qkv_stride;
     a.kv = kv;
@@ -838,7 +884,7 @@ void launch_step_advance(int *step_ptr, cudaStream_t st) { launch_pdl(step_advan
     template void launch_gemm_rows<WT>(const float *, const WT *, const WT *, const float *, float *, int, int, int, \
                                        int, const KVLayout *, int, Rows, cudaStream_t);                              \
     template void launch_attention<WT>(const float *, int, const KVLayout &, int, Rows, int, float *, int, float *,  \
-                                       unsigned *, int, cudaStream_t, OperandOut);                                    \
+                                       unsigned *, int, cudaStream_t, OperandOut, QkvPartials);                       \
     template void launch_lm_head<WT>(const float *, const WT *, const WT *, const WT *, float *, int, int, int, int, \
                                      float *, unsigned *, int *, StepState *, int *, cudaStream_t);                  \
     template void launch_lm_head_rows<WT>(const float *, const WT *, float *, int, int, int, int, cudaStream_t);

@@ -574,7 +574,8 @@ template <typename WT>
 int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, float *partial, size_t partial_floats,
                    unsigned *tile_ctr, int *err, const WT *bias, const float *resid, float *out, int epi,
                    const KVLayout *kv, int layer, Rows rows, int sms, cudaStream_t st, OperandOut op, int out_stride,
-                   const WT *ln_g, const WT *ln_b, OperandOut ln_op, bool *ln_done) {
+                   const WT *ln_g, const WT *ln_b, OperandOut ln_op, bool *ln_done, bool defer_reduce,
+                   int *splits_out) {
     const int bk = kind == TC_TF32X3 ? 32 : 64;
     const int kb_total = w.K / bk;
     TcPlan p = plan(R, w.N, kb_total, sms);
@@ -640,7 +641,9 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
         else launch_kernel<TC_F16, 128, WT, false>(w, x, bi, a, st);
     }
     if (ln_done) *ln_done = false;
+    if (splits_out) *splits_out = p.splits;
     if (p.splits == 1) return 1;   // the GEMM applied the epilogue itself
+    if (defer_reduce) return 1;    // the consumer sums the partials
     if (ln_g && w.N <= 2048 && (w.N % 4) == 0) {   // sum the splits, epilogue and the next LayerNorm in one kernel
         launch_pdl(tc_reduce_ln_kernel<WT>, dim3((unsigned)R), dim3(256), 0, st, (const float *)partial, p.splits, R, w.N,
                    a.e, ln_g, ln_b, ln_op);
@@ -655,9 +658,11 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
 
 template int launch_tc_gemm<float>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, unsigned *,
                                    int *, const float *, const float *, float *, int, const KVLayout *, int, Rows, int,
-                                   cudaStream_t, OperandOut, int, const float *, const float *, OperandOut, bool *);
+                                   cudaStream_t, OperandOut, int, const float *, const float *, OperandOut, bool *, bool,
+                                   int *);
 template int launch_tc_gemm<__half>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, unsigned *,
                                     int *, const __half *, const float *, float *, int, const KVLayout *, int, Rows, int,
-                                    cudaStream_t, OperandOut, int, const __half *, const __half *, OperandOut, bool *);
+                                    cudaStream_t, OperandOut, int, const __half *, const __half *, OperandOut, bool *,
+                                    bool, int *);
 
 }  // namespace g2

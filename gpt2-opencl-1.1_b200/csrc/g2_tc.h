@@ -65,13 +65,16 @@ constexpr int kTcMaxTiles = 4096;
 // the row stride of out and resid (else N).  With ln_g / ln_b, a split-K GEMM
 // also takes the LayerNorm of each output row (gamma ln_g, beta ln_b) and
 // writes it as ln_op, the next GEMM's operand; *ln_done then says whether it
-// did (a single-split GEMM does not: its caller runs the LayerNorm).  `err` receives an
+// did (a single-split GEMM does not: its caller runs the LayerNorm).  With
+// defer_reduce a split-K GEMM leaves its partial tiles in `partial` for the
+// consumer to sum; *splits_out receives the split count (1: the GEMM applied
+// the epilogue itself).  `err` receives an
 // error code if a wait inside the kernel expires.  Returns the launch count.
 template <typename WT>
 int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, float *partial, size_t partial_floats,
                    unsigned *tile_ctr, int *err, const WT *bias, const float *resid, float *out, int epi,
                    const KVLayout *kv, int layer, Rows rows, int sms, cudaStream_t st, OperandOut op = OperandOut(),
                    int out_stride = 0, const WT *ln_g = nullptr, const WT *ln_b = nullptr, OperandOut ln_op = OperandOut(),
-                   bool *ln_done = nullptr);
+                   bool *ln_done = nullptr, bool defer_reduce = false, int *splits_out = nullptr);
 
 }  // namespace g2
