@@ -358,7 +358,7 @@ template <typename KT>
 __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
     pdl_wait();
     pdl_launch();
-    constexpr int CH = kAttnChunk;              // keys per CTA: one per thread in the score pass
+    constexpr int CH = kAttnChunk;              // keys per chunk: one per thread in the score pass
     constexpr int VN = 16 / sizeof(KT);         // elements per 16-byte load
     constexpr int DG = kHeadDim / VN;           // 16-byte groups per 64-dim row (8 fp16, 16 fp32)
     constexpr int KG = 128 / DG;                // key groups of the P.V pass
@@ -368,14 +368,16 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
     __shared__ float red[KG][kHeadDim];
     __shared__ float sh[32];
     __shared__ int s_last;
+    __shared__ float knew[2][kHeadDim];   // k and v at pos, when summed here from the c_attn partials
     const int h = blockIdx.x, sp = blockIdx.y, r = blockIdx.z, tid = threadIdx.x;
     const int NH = a.kv.n_head;
     const int T = a.rows.pos[r] + 1;
-    const int nsplit = (T + CH - 1) / CH;
+    const int nsplit = (T + CH - 1) / CH;   // chunks; CTA sp takes chunks sp, sp + Y, ...
+    const int Y = gridDim.y;
     if (sp >= nsplit) return;
+    const int nparts = nsplit < Y ? nsplit : Y;
     const int slot = a.rows.slot[r];
     const int pos = T - 1;
-    __shared__ float knew[2][kHeadDim];   // k and v at pos, when summed here from the c_attn partials
     const long long base = (long long)slot * a.kv.slot_stride + (long long)a.layer * a.kv.layer_stride +
                            (long long)h * a.kv.max_seq * kHeadDim;
     const bool fused = a.qpart != nullptr;
@@ -384,7 +386,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
     } else {
         // c_attn output = (sum of the splits in order) + bias, as its reduce would give
         const int E = a.qkv_stride / 3;
-        const bool kv_here = sp == nsplit - 1;   // this chunk holds pos: it needs k, v and appends them
+        const bool kv_here = sp == (nsplit - 1) % Y;   // this CTA takes the chunk with pos: k, v and their append
         for (int c = tid; c < (kv_here ? 3 : 1) * kHeadDim; c += blockDim.x) {
             const int part = c / kHeadDim, d = c % kHeadDim;   // 0 q, 1 k, 2 v
             const size_t col = (size_t)part * E + h * kHeadDim + d;
@@ -403,67 +405,75 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
     }
     const KT *K = reinterpret_cast<const KT *>(a.kv.k) + base;
     const KT *V = reinterpret_cast<const KT *>(a.kv.v) + base;
-    const int j0 = sp * CH;
-    const int nj = min(CH, T - j0);
-    // scores: one key per thread, its 64 dims in 16-byte loads issued together
-    uint4 kw[DG];
-    if (tid < nj) {
-        const uint4 *kr = reinterpret_cast<const uint4 *>(K + (size_t)(j0 + tid) * kHeadDim);
-#pragma unroll
-        for (int i = 0; i < DG; ++i) kw[i] = kr[i];
-    }
-    __syncthreads();   // q (and k, v at pos)
-    float s = -FLT_MAX;
-    if (tid < nj) {
-        float d = 0.0f;
-        if (fused && j0 + tid == pos) {   // the key this pass appended: from shared memory
-            for (int i = 0; i < kHeadDim; ++i) d = fmaf(knew[0][i], q[i], d);
-        } else {
-#pragma unroll
-            for (int i = 0; i < DG; ++i) d += dot_vec(kw[i], q + i * VN, KT());
-        }
-        s = d;
-    }
-    const float m = block_max(s, sh);
-    const float e = tid < nj ? expf(s - m) : 0.0f;
-    p[tid] = e;
-    const float l = block_sum(e, sh);   // its barriers also publish p
-    // P.V: thread (kg, dg) sums keys kg, kg + KG, ... of dims dg * VN .. dg * VN + VN - 1
     const int dg = tid % DG, kg = tid / DG;
-    float o[VN], o2[VN];
+    // running online-softmax state over this CTA's chunks (acc: threads < 64, one dim each)
+    float Mr = -FLT_MAX, Lr = 0.0f, acc = 0.0f;
+    for (int ch = sp; ch < nsplit; ch += Y) {
+        const int j0 = ch * CH;
+        const int nj = min(CH, T - j0);
+        // scores: one key per thread, its 64 dims in 16-byte loads issued together
+        uint4 kw[DG];
+        if (tid < nj) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(K + (size_t)(j0 + tid) * kHeadDim);
 #pragma unroll
-    for (int i = 0; i < VN; ++i) o[i] = o2[i] = 0.0f;
-    // (with fused c_attn partials the value at pos is taken from shared memory, not the cache)
-    const int jpos = fused ? pos - j0 : -1;
-    int jj = kg;
-    for (; jj + KG < nj; jj += 2 * KG) {   // two keys in flight
-        if (jj == jpos || jj + KG == jpos) break;
-        const uint4 v0 = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN);
-        const uint4 v1 = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj + KG) * kHeadDim + dg * VN);
-        fma_vec(o, v0, p[jj], KT());
-        fma_vec(o2, v1, p[jj + KG], KT());
-    }
-    for (; jj < nj; jj += KG) {
-        if (jj == jpos) {
-#pragma unroll
-            for (int i = 0; i < VN; ++i) o[i] = fmaf(p[jj], knew[1][dg * VN + i], o[i]);
-        } else {
-            fma_vec(o, *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN), p[jj], KT());
+            for (int i = 0; i < DG; ++i) kw[i] = kr[i];
         }
+        __syncthreads();   // q (and k, v at pos); the previous chunk's readers of p and red are done
+        float s = -FLT_MAX;
+        if (tid < nj) {
+            float d = 0.0f;
+            if (fused && j0 + tid == pos) {   // the key this pass appended: from shared memory
+                for (int i = 0; i < kHeadDim; ++i) d = fmaf(knew[0][i], q[i], d);
+            } else {
+#pragma unroll
+                for (int i = 0; i < DG; ++i) d += dot_vec(kw[i], q + i * VN, KT());
+            }
+            s = d;
+        }
+        const float m = block_max(s, sh);
+        const float e = tid < nj ? expf(s - m) : 0.0f;
+        p[tid] = e;
+        const float l = block_sum(e, sh);   // its barriers also publish p
+        // P.V: thread (kg, dg) sums keys kg, kg + KG, ... of dims dg * VN .. dg * VN + VN - 1
+        float o[VN], o2[VN];
+#pragma unroll
+        for (int i = 0; i < VN; ++i) o[i] = o2[i] = 0.0f;
+        // (with fused c_attn partials the value at pos is taken from shared memory, not the cache)
+        const int jpos = fused ? pos - j0 : -1;
+        int jj = kg;
+        for (; jj + KG < nj; jj += 2 * KG) {   // two keys in flight
+            if (jj == jpos || jj + KG == jpos) break;
+            const uint4 v0 = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN);
+            const uint4 v1 = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj + KG) * kHeadDim + dg * VN);
+            fma_vec(o, v0, p[jj], KT());
+            fma_vec(o2, v1, p[jj + KG], KT());
+        }
+        for (; jj < nj; jj += KG) {
+            if (jj == jpos) {
+#pragma unroll
+                for (int i = 0; i < VN; ++i) o[i] = fmaf(p[jj], knew[1][dg * VN + i], o[i]);
+            } else {
+                fma_vec(o, *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN), p[jj], KT());
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < VN; ++i) red[kg][dg * VN + i] = o[i] + o2[i];
+        __syncthreads();
+        float ac = 0.0f;
+        if (tid < kHeadDim)
+#pragma unroll
+            for (int g = 0; g < KG; ++g) ac += red[g][tid];
+        // merge this chunk into the running state
+        const float Mn = fmaxf(Mr, m);
+        const float so = expf(Mr - Mn), sn = expf(m - Mn);   // so = 0 on the first chunk
+        acc = acc * so + ac * sn;
+        Lr = Lr * so + l * sn;
+        Mr = Mn;
     }
-#pragma unroll
-    for (int i = 0; i < VN; ++i) red[kg][dg * VN + i] = o[i] + o2[i];
-    __syncthreads();
-    float acc = 0.0f;
-    if (tid < kHeadDim)
-#pragma unroll
-        for (int g = 0; g < KG; ++g) acc += red[g][tid];
-    const float* none = nullptr;
-    (void)none;
-    if (nsplit == 1) {
+    if (nparts == 1) {
         if (tid < kHeadDim) {
             const size_t o = (size_t)r * a.out_stride + h * kHeadDim + tid;
-            const float v = acc / l;
+            const float v = acc / Lr;
             a.out[o] = v;
             put_operand(a.op, o, v);
         }
@@ -472,22 +482,22 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
     float *P = a.partial + (((size_t)r * NH + h) * a.max_splits + sp) * (kHeadDim + 2);
     if (tid < kHeadDim) P[2 + tid] = acc;
     if (tid == 0) {
-        P[0] = m;
-        P[1] = l;
+        P[0] = Mr;
+        P[1] = Lr;
     }
     __threadfence();
     __syncthreads();
     unsigned *ctr = a.counters + (size_t)r * NH + h;
-    if (tid == 0) s_last = (atomicAdd(ctr, 1u) == (unsigned)(nsplit - 1));
+    if (tid == 0) s_last = (atomicAdd(ctr, 1u) == (unsigned)(nparts - 1));
     __syncthreads();
     if (!s_last) return;
     __threadfence();
     if (tid < kHeadDim) {
         const float *P0 = a.partial + ((size_t)r * NH + h) * a.max_splits * (kHeadDim + 2);
         float M = -FLT_MAX;
-        for (int i = 0; i < nsplit; ++i) M = fmaxf(M, __ldcg(P0 + (size_t)i * (kHeadDim + 2)));
+        for (int i = 0; i < nparts; ++i) M = fmaxf(M, __ldcg(P0 + (size_t)i * (kHeadDim + 2)));
         float L = 0.0f, O = 0.0f;
-        for (int i = 0; i < nsplit; ++i) {
+        for (int i = 0; i < nparts; ++i) {
             const float *Pi = P0 + (size_t)i * (kHeadDim + 2);
             const float w = expf(__ldcg(Pi) - M);
             L = fmaf(__ldcg(Pi + 1), w, L);
