@@ -491,7 +491,7 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
         // float4 group per consumer thread, and the context fits the score buffer
         e->mega = dtype == G2_F32 && !(off && off[0] == '1') && coop && smem <= (size_t)optin && G <= 256 && cw[0] &&
                   cw[1] && e->mega_nq && E * 4 <= mega_slot_bytes() && E / 4 <= 480 && e->c.n_ctx <= mega_max_keys() &&
-                  e->c.n_head * 64 == E;
+                  e->c.n_head * 64 == E && e->c.n_layer <= kMegaMaxLayers;
         e->mega_smem = smem;
     }
     TRY(load_weights(e, model_dir));

@@ -77,6 +77,21 @@ constexpr int kRedArg = 1024;              // 16 values, then 16 indices
 constexpr int kRedAtt = 1056;              // 32
 constexpr int kRedLn = 1088;               // 32
 constexpr int kRedFloats = 1120;
+// Per-CTA constants computed once at launch (ints), so that no unit divides by
+// a runtime value: strip geometries of the A and D units, block geometries of
+// the B and D units, the B-unit slice count, and the first unit of each layer.
+constexpr int kGeoA = 0, kGeoDs = 8;       // strip: CG, RG, RPC, nfull, magic(CG), cw
+constexpr int kGeoB = 16, kGeoDb = 24;     // block: CG, RG, RPC, magic(CG), NB, RG * CG
+constexpr int kCfgMnq = 32, kCfgNq = 33;   // magic(nq), nq
+constexpr int kCfgOffB = 34, kCfgOffD = 35;   // nA % G, (nA + nB) % G
+constexpr int kCfgInvE = 36;               // 1 / E (float bits)
+constexpr int kCfgFirst = 40;              // [l] = first unit of layer l's count on this CTA, l <= L
+constexpr int kCfgInts = (kCfgFirst + kMegaMaxLayers + 1 + 3) / 4 * 4;   // a whole number of 16-byte words
+constexpr int kMaxJ = 4;                   // vector words per consumer thread (E <= kMaxJ * kCons)
+// n / d for 0 <= n < 2048 and 1 <= d <= 480 as (n * magic(d)) >> 20, with
+// magic(d) = ceil(2^20 / d) (exact in that range: n (magic * d - 2^20) < 2^20).
+__host__ __device__ constexpr int magic20(int d) { return ((1 << 20) + d - 1) / d; }
+__device__ __forceinline__ int mdiv(int n, int m) { return (n * m) >> 20; }
 
 typedef unsigned long long u64;
 
@@ -228,13 +243,14 @@ struct Smem {
     float *attq;   // q, k, v of the head at pos (192)
     float *atta;   // attention output of the head (64); GELU outputs of a D unit
     float *part;   // partial sums of the P.V and block passes (kPart)
+    int *cfg;      // per-CTA constants (kCfgInts)
     u64 *trc;      // trace accumulators (thread 0 only)
     u64 *full, *empty;
     unsigned char *ring;
 };
 
 // Trace layout in shared memory (u64): see g2_mega.h; [20] phase-begin stamp,
-// [21] inputs stamp, [24] timeline count, [32..64) timeline stamps (CTA 0, step 0).
+// [21] inputs stamp, [24] timeline count, [32..160) timeline stamps (CTA 0, one step).
 struct Cx {
     const MegaParams *p;
     Smem s;
@@ -250,7 +266,7 @@ struct Cx {
 __device__ __forceinline__ void tr_stamp(Cx &cx) {
     if (cx.tl) {
         const u64 n = cx.s.trc[24];
-        if (n < 32) {
+        if (n < (u64)(kTraceSlots - 32)) {
             cx.s.trc[32 + n] = gtime() - cx.t0;
             cx.s.trc[24] = n + 1;
         }
@@ -285,7 +301,7 @@ __device__ __forceinline__ void fail(Cx &cx, int code) {
 // Uniform deadline check of a polling loop, every 64 rounds (a barrier round).
 __device__ __forceinline__ bool poll_expired(Cx &cx, unsigned round, u64 limit, int code) {
     if ((round & 63u) != 63u) return false;
-    if (cons_or(gtime() > limit)) {
+    if (cons_or(gtime() > limit || cx.failed)) {
         fail(cx, code);
         return true;
     }
@@ -307,7 +323,7 @@ __device__ __forceinline__ bool poll_vec(Cx &cx, const u64 *src, float *dst, int
                 pending &= ~(1u << j);
             }
         }
-        if (cons_and(pending == 0)) return true;
+        if (cons_and(pending == 0 && !cx.failed)) return true;
         if (poll_expired(cx, round, limit, code)) return false;
     }
 }
@@ -315,15 +331,24 @@ __device__ __forceinline__ bool poll_vec(Cx &cx, const u64 *src, float *dst, int
 // Poll the accumulator at src (ncopy copies of E words; copy c collects the
 // units u with u % ncopy == c of the nunits contributors) until every word
 // holds its count, then x[i] = x[i] + (sum over copies in order + bias[i]) in
-// xres and xs.  All consumer threads.
+// xres and xs.  The bias is loaded before the first round, so no load waits
+// after the accumulator turns ready.  All consumer threads.
 __device__ __forceinline__ bool poll_acc(Cx &cx, const u64 *src, int ncopy, int nunits, const float *bias, int E,
                                          int code) {
     const u64 limit = gtime() + kTimeoutNs;
     unsigned pending = 0;
-    for (int j = 0, i = cx.ctid; i < E; ++j, i += kCons) pending |= 1u << j;
+    float bv[kMaxJ];
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+        const int i = cx.ctid + j * kCons;
+        bv[j] = i < E ? __ldg(bias + i) : 0.0f;
+        if (i < E) pending |= 1u << j;
+    }
     for (unsigned round = 0;; ++round) {
-        for (unsigned m = pending; m; m &= m - 1) {
-            const int j = __ffs(m) - 1, i = cx.ctid + j * kCons;
+#pragma unroll
+        for (int j = 0; j < kMaxJ; ++j) {
+            if (!(pending & (1u << j))) continue;
+            const int i = cx.ctid + j * kCons;
             u64 w[kAccCopies];
             bool ready = true;
 #pragma unroll
@@ -337,13 +362,13 @@ __device__ __forceinline__ bool poll_acc(Cx &cx, const u64 *src, int ncopy, int 
 #pragma unroll
                 for (int c = 1; c < kAccCopies; ++c)
                     if (c < ncopy) v += acc_value(w[c], acc_count(w[c]));
-                const float x = cx.s.xres[i] + (v + __ldg(bias + i));
+                const float x = cx.s.xres[i] + (v + bv[j]);
                 cx.s.xres[i] = x;
                 cx.s.xs[i] = x;
                 pending &= ~(1u << j);
             }
         }
-        if (cons_and(pending == 0)) return true;
+        if (cons_and(pending == 0 && !cx.failed)) return true;
         if (poll_expired(cx, round, limit, code)) return false;
     }
 }
@@ -361,10 +386,10 @@ __device__ __forceinline__ void ln_sums(const Cx &cx, int n, float &s, float &q)
 // LayerNorm statistics (math.cl:297-308) from the CTA totals of x and x * x:
 // mean and rstd = 1 / sqrt(var + 1e-5).  The one-pass variance is taken in
 // fp32; it loses precision only when |mean| is many times the spread of x.
-__device__ __forceinline__ void ln_finish(float S, float Q, int n, float &mean, float &rstd) {
-    mean = S / (float)n;
-    const float var = fmaxf(Q / (float)n - mean * mean, 0.0f);
-    rstd = 1.0f / sqrtf(var + 1e-5f);
+__device__ __forceinline__ void ln_finish(float S, float Q, float inv_n, float &mean, float &rstd) {
+    mean = S * inv_n;
+    const float var = fmaxf(Q * inv_n - mean * mean, 0.0f);
+    rstd = rsqrtf(var + 1e-5f);
 }
 // LayerNorm statistics of xs[0..n) in every consumer thread.  One barrier.
 __device__ __forceinline__ void ln_stats(Cx &cx, int n, float &mean, float &rstd) {
@@ -386,7 +411,7 @@ __device__ __forceinline__ void ln_stats(Cx &cx, int n, float &mean, float &rstd
         S += __shfl_xor_sync(0xffffffffu, S, o);
         Q += __shfl_xor_sync(0xffffffffu, Q, o);
     }
-    ln_finish(S, Q, n, mean, rstd);
+    ln_finish(S, Q, __int_as_float(cx.s.cfg[kCfgInvE]), mean, rstd);
 }
 
 // Ring chunk cx.chunk_i + k (waits for its bytes).  On an expired wait the
@@ -415,11 +440,13 @@ __device__ __forceinline__ void chunk_done(Cx &cx, unsigned n = 1) {
 // cg: in a chunk of RPC rows its weights are float4s ctid + i kCons (3 RG <=
 // RPC <= 4 RG at every width).  Chunks of weight rows only are taken two at a
 // time without masks; the chunk with the bias and column-sum rows is masked.
-__device__ __forceinline__ float strip_unit(Cx &cx, int K, int cw) {
-    const int CG = cw >> 2;                         // float4 column groups
-    const int RG = kCons / CG;                      // row groups (RG * CG == kCons)
-    const int RPC = kSlotBytes / (cw * 4);          // rows per chunk
-    const int rg = cx.ctid / CG, t = cx.ctid;
+__device__ __forceinline__ float strip_unit(Cx &cx, int K, int geo) {
+    const int *gm = cx.s.cfg + geo;
+    const int CG = gm[0];                           // float4 column groups (cw / 4)
+    const int RG = gm[1];                           // row groups (RG * CG == kCons)
+    const int RPC = gm[2];                          // rows per chunk
+    const int cw = gm[5];
+    const int rg = mdiv(cx.ctid, gm[4]), t = cx.ctid;
     const int rows = K + 2;
     const bool has4 = rg + 3 * RG < RPC;
     const float *xs = cx.s.xs;
@@ -427,7 +454,7 @@ __device__ __forceinline__ float strip_unit(Cx &cx, int K, int cw) {
     ln_sums(cx, K, s, q);
     float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
     float bias = 0.0f, csum = 0.0f;
-    const int nfull = K / RPC;   // chunks of weight rows only
+    const int nfull = gm[3];   // chunks of weight rows only (K / RPC)
     int c = 0, r0 = 0;
     for (; c + 1 < nfull; c += 2, r0 += 2 * RPC) {
         const float4 *w = chunk_wait(cx, 0), *v = chunk_wait(cx, 1);
@@ -466,6 +493,7 @@ __device__ __forceinline__ float strip_unit(Cx &cx, int K, int cw) {
         }
         chunk_done(cx);
     }
+    tr_stamp(cx);
     float4 acc = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
     // Lanes congruent mod CG hold the same column group ((32 warp + lane) % CG):
     // fold them into lanes 0..CG-1 of the warp, then add across warps.
@@ -489,6 +517,7 @@ __device__ __forceinline__ float strip_unit(Cx &cx, int K, int cw) {
         red[481 + 2 * cx.warp] = q;
     }
     cons_sync();
+    tr_stamp(cx);
     float y = 0.0f;
     if (t < cw) {
         float tt[kWarps];
@@ -505,7 +534,7 @@ __device__ __forceinline__ float strip_unit(Cx &cx, int K, int cw) {
             Q += red[481 + 2 * w];
         }
         float mean, rstd;
-        ln_finish(S, Q, K, mean, rstd);
+        ln_finish(S, Q, __int_as_float(cx.s.cfg[kCfgInvE]), mean, rstd);
         y = fmaf(rstd, fmaf(-mean, csum, tt[0]), bias);
     }
     return y;
@@ -517,11 +546,11 @@ __device__ __forceinline__ float strip_unit(Cx &cx, int K, int cw) {
 // (rg, cg) = (ctid / CG, ctid % CG) sums rows rg, rg + RG, ... of float4
 // column group cg (float4s ctid, ctid + RG CG, ... of a chunk); the RG
 // partials are then added in a fixed order.  a is in shared memory.
-__device__ __forceinline__ void block_unit(Cx &cx, const float *a, int rows, int NB, u64 *dst) {
-    const int CG = NB >> 2, RG = kCons / CG, RGCG = RG * CG;
-    const int t = cx.ctid, rg = t / CG;
+__device__ __forceinline__ void block_unit(Cx &cx, const float *a, int rows, int geo, u64 *dst) {
+    const int *gm = cx.s.cfg + geo;
+    const int RG = gm[1], RPC = gm[2], NB = gm[4], RGCG = gm[5];   // RPC: rows per chunk
+    const int t = cx.ctid, rg = mdiv(t, gm[3]);
     const bool act = t < RGCG;
-    const int RPC = kSlotBytes / (NB * 4);   // rows per chunk
     float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
     for (int r0 = 0; r0 < rows; r0 += RPC) {
         const float4 *w = chunk_wait(cx);
@@ -541,13 +570,21 @@ __device__ __forceinline__ void block_unit(Cx &cx, const float *a, int rows, int
         }
         chunk_done(cx);
     }
+    tr_stamp(cx);
     float *part = cx.s.part;   // [RG][NB], RG * NB <= 4 * kCons <= kPart
     if (act) reinterpret_cast<float4 *>(part)[t] = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
     cons_sync();
-    for (int n = t; n < NB; n += kCons) {
-        float y = part[n];
-        for (int g = 1; g < RG; ++g) y += part[g * NB + n];
-        acc_add(dst + n, y);
+    for (int n = t; n < NB; n += kCons) {   // four independent partial sums, then a fixed tree
+        float y0 = part[n], y1 = 0.0f, y2 = 0.0f, y3 = 0.0f;
+        int g = 1;
+        for (; g + 3 < RG; g += 4) {
+            y0 += part[g * NB + n];
+            y1 += part[(g + 1) * NB + n];
+            y2 += part[(g + 2) * NB + n];
+            y3 += part[(g + 3) * NB + n];
+        }
+        for (; g < RG; ++g) y0 += part[g * NB + n];
+        acc_add(dst + n, (y0 + y1) + (y2 + y3));
     }
 }
 
@@ -658,7 +695,7 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
                     pend = false;
                 }
             }
-            if (cons_and(!pend)) break;
+            if (cons_and(!pend && !cx.failed)) break;
             if (poll_expired(cx, round, limit, 5)) return false;
         }
     }
@@ -710,6 +747,7 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
     lsum = warp_sum(lsum);
     if (cx.lane == 0) rb[16 + cx.warp] = lsum;
     cons_sync();
+    tr_stamp(cx);
     float Lt = rb[16];
 #pragma unroll
     for (int w = 1; w < kWarps; ++w) Lt += rb[16 + w];
@@ -738,6 +776,7 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
         a[cx.ctid] = y / Lt;
     }
     cons_sync();
+    tr_stamp(cx);
     return true;
 }
 
@@ -755,25 +794,25 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
 __device__ __forceinline__ bool run_units(Cx &cx, const Sched &S, int step, int l, int pos, int half) {
     const MegaParams &p = *cx.p;
     const int E = p.E, t = cx.ctid;
+    const int *cf = cx.s.cfg;
     for (int kind = half ? 2 : 0; kind <= (half ? 2 : 1); ++kind) {
         const int n = kind == 0 ? S.nA : kind == 1 ? S.nB : S.nD;
-        int u = kind == 0 ? S.a_first(l, cx.cta) : kind == 1 ? S.b_first(l, cx.cta) : S.d_first(l, cx.cta);
-        const int cw = kind == 0 ? p.cw_qkv : p.cw_fc;
-        const int NB = kind == 1 ? E / p.nq : E;
+        int u = cf[kCfgFirst + l] - (kind == 0 ? 0 : cf[kind == 1 ? kCfgOffB : kCfgOffD]);
+        if (u < 0) u += S.G;
         u64 *acc = acc_of(p, step, l, kind == 1 ? 0 : 1);
         const unsigned ep = epoch_of(p, step, l, 0);
         const int ph = kind == 0 ? 0 : kind == 1 ? 1 : 3;   // trace slot
         float *av = cx.s.atta;
         for (; u < n; u += S.G) {
             tr_begin(cx);
-            int rows;
+            int rows, geo;
             u64 *dst;
             if (kind != 1) {
                 tr_inputs(cx, ph);
-                const float v = strip_unit(cx, E, cw);
+                const float v = strip_unit(cx, E, kind == 0 ? kGeoA : kGeoDs);
                 if (kind == 0) {
-                    if (t < cw) {
-                        const int col = u * cw + t;
+                    if (t < p.cw_qkv) {
+                        const int col = u * p.cw_qkv + t;
                         if (col >= E) {   // K or V of head m / 64
                             int m = col - E;
                             float *kv = m >= E ? p.vc : p.kc;
@@ -785,19 +824,24 @@ __device__ __forceinline__ bool run_units(Cx &cx, const Sched &S, int step, int 
                     tr_end(cx, ph);
                     continue;
                 }
-                if (t < cw) av[t] = gelu_f(v);
+                if (t < p.cw_fc) av[t] = gelu_f(v);
                 cons_sync();
-                rows = cw;
+                rows = p.cw_fc;
+                geo = kGeoDb;
                 dst = acc + (size_t)(u % kAccCopies) * E;
             } else {
-                if (!attention(cx, u / p.nq, step, l, pos)) return false;
+                const int h = mdiv(u, cf[kCfgMnq]), j = u - h * cf[kCfgNq];
+                if (!attention(cx, h, step, l, pos)) return false;
                 rows = 64;
-                dst = acc + (u % p.nq) * NB;
+                geo = kGeoB;
+                dst = acc + j * cf[kGeoB + 4];
             }
-            block_unit(cx, av, rows, NB, dst);
+            block_unit(cx, av, rows, geo, dst);
             tr_end(cx, ph);
         }
-        if (!cons_and(!cx.failed)) return false;
+        // An expired wait inside a unit is caught at the next poll, whose exit
+        // barrier also carries the failure flag.
+        tr_stamp(cx);
     }
     return true;
 }
@@ -817,7 +861,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     cx.chunk_i = 0;
     cx.upar = 0;
     cx.tr = p.trace != nullptr && threadIdx.x == 0;
-    cx.tl = cx.tr && blockIdx.x == 0;
+    cx.tl = false;
     cx.t0 = cx.tr ? gtime() : 0;
     const int G = gridDim.x, E = p.E, L = p.L;
     unsigned char *sp = smem_raw;
@@ -840,7 +884,9 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     sp += kPart * sizeof(float);
     cx.s.xres = reinterpret_cast<float *>(sp);
     sp += (size_t)E * sizeof(float);
-    cx.s.xs = reinterpret_cast<float *>(sp);
+    cx.s.xs = reinterpret_cast<float *>(sp);   // 16-byte aligned: the LM rows read it as float4
+    sp += (size_t)(E + 4) * sizeof(float);
+    cx.s.cfg = reinterpret_cast<int *>(sp);    // last, so that it moves no other array
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kSlots; ++i) {
@@ -850,7 +896,6 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     for (int i = threadIdx.x; i < kTraceSlots; i += kThreads) cx.s.trc[i] = 0;
-    __syncthreads();
 
     Sched S;
     S.nA = 3 * E / p.cw_qkv;
@@ -859,6 +904,36 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     S.nLM = (p.V + p.lm_rows - 1) / p.lm_rows;
     S.per_layer = S.nA + S.nB + S.nD;
     S.G = G;
+    if (threadIdx.x == 0) {   // the per-CTA constants: every runtime division of the units, once
+        int *cf = cx.s.cfg;
+        for (int s = 0; s < 2; ++s) {   // strips of width cw over E rows (+ bias and column-sum rows)
+            const int cw = s ? p.cw_fc : p.cw_qkv, CG = cw >> 2, RPC = kSlotBytes / (cw * 4);
+            int *g = cf + (s ? kGeoDs : kGeoA);
+            g[0] = CG;
+            g[1] = kCons / CG;
+            g[2] = RPC;
+            g[3] = E / RPC;
+            g[4] = magic20(CG);
+            g[5] = cw;
+        }
+        for (int b = 0; b < 2; ++b) {   // blocks of NB columns
+            const int NB = b ? E : E / p.nq, CG = NB >> 2;
+            int *g = cf + (b ? kGeoDb : kGeoB);
+            g[0] = CG;
+            g[1] = kCons / CG;
+            g[2] = kSlotBytes / (NB * 4);
+            g[3] = magic20(CG);
+            g[4] = NB;
+            g[5] = (kCons / CG) * CG;
+        }
+        cf[kCfgMnq] = magic20(p.nq);
+        cf[kCfgNq] = p.nq;
+        cf[kCfgOffB] = S.nA % G;
+        cf[kCfgOffD] = (S.nA + S.nB) % G;
+        cf[kCfgInvE] = __float_as_int(1.0f / (float)E);
+        for (int l = 0; l <= L; ++l) cf[kCfgFirst + l] = S.first(l * S.per_layer, cx.cta);
+    }
+    __syncthreads();
 
     if (cx.warp == kWarps) {   // producer warp: one thread issues, the rest are idle
         if (cx.lane == 0) producer(cx, S);
@@ -870,6 +945,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     int tok = p.state->token, pos = p.state->pos;
     const int step_base = p.state->step, min_new = p.state->min_new;
     for (int step = 0; step < p.n_steps; ++step) {
+        cx.tl = cx.tr && cx.cta == 0 && step == min(3, p.n_steps - 1);
         // x = wte[tok] + wpe[pos] (embed, math.cl:333)
         for (int i = cx.ctid; i < E; i += kCons) {
             const float x = p.wte[(size_t)tok * E + i] + p.wpe[(size_t)pos * E + i];
@@ -896,7 +972,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
         }
         // ---------------- LN_f + LM head + greedy argmax ----------------
         {
-            int u = S.lm_first(L, cx.cta);
+            int u = cx.s.cfg[kCfgFirst + L];   // the first LM unit of this CTA
             const bool forbid = (step_base + step) < min_new;
             float best = -FLT_MAX;
             int besti = INT_MAX;
@@ -1012,7 +1088,6 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
             pos += 1;
             cons_sync();
             tr_end(cx, 6);
-            cx.tl = false;
         }
     }
     if (cx.cta == 0 && cx.ctid == 0) {
@@ -1031,7 +1106,7 @@ out:
 
 size_t mega_smem_bytes(int E) {
     return (size_t)kSlots * kSlotBytes + 2 * kSlots * sizeof(unsigned long long) + kTraceSlots * sizeof(unsigned long long) +
-           (kRedFloats + kMaxKeys + 192 + 64 + kPart) * sizeof(float) + (size_t)(2 * E + 4) * sizeof(float);
+           (kRedFloats + kMaxKeys + 192 + 64 + kPart + kCfgInts) * sizeof(float) + (size_t)(2 * E + 4) * sizeof(float);
 }
 int mega_threads() { return kThreads; }
 const void *mega_kernel_ptr() { return (const void *)mega_decode_kernel; }
