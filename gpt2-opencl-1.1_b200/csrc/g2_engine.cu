@@ -590,11 +590,14 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
         if (r == cudaSuccess)
             r = cudaMemcpy(e->d_layer_off, e->layer_off.data(), sizeof(long long) * e->layer_off.size(),
                            cudaMemcpyHostToDevice);
-        if (r == cudaSuccess)
-            r = cudaFuncSetAttribute(mega_kernel_ptr(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->mega_smem);
+        const bool traced = getenv("G2_MEGA_TRACE") != nullptr;
+        for (int k = 0; k < 2 && r == cudaSuccess; ++k)
+            r = cudaFuncSetAttribute(mega_kernel_ptr(k == 1), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)e->mega_smem);
         int per_sm = 0;
         if (r == cudaSuccess)
-            r = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mega_kernel_ptr(), mega_threads(), e->mega_smem);
+            r = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mega_kernel_ptr(traced), mega_threads(),
+                                                              e->mega_smem);
         if (r != cudaSuccess) {
             free_engine(e);
             return set_err(G2_ERR_CUDA, "decode kernel setup: %s", cudaGetErrorString(r));
@@ -986,8 +989,8 @@ static int launch_mega(g2_engine *e, int slot, int n_steps) {
         P.epoch0 = e->mega_epoch + 1;
         e->mega_epoch += mega_epochs(c.n_layer, n);
         void *args[] = {&P};
-        CK(cudaLaunchCooperativeKernel(mega_kernel_ptr(), dim3(e->mega_grid), dim3(mega_threads()), args, e->mega_smem,
-                                       e->st));
+        CK(cudaLaunchCooperativeKernel(mega_kernel_ptr(e->d_trace != nullptr), dim3(e->mega_grid), dim3(mega_threads()),
+                                       args, e->mega_smem, e->st));
         e->launches += 1;
         done += n;
     }

@@ -209,6 +209,19 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
     return v1 > v2 || (v1 == v2 && i1 < i2);
 }
+// Butterfly argmax over a warp under the order of better(): every lane ends
+// with the unique maximum of the lanes' (value, index) pairs.
+__device__ __forceinline__ void warp_argmax(float &v, int &i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (better(ov, oi, v, i)) {
+            v = ov;
+            i = oi;
+        }
+    }
+}
 __device__ __forceinline__ float gelu_f(float v) {
     return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
 }
@@ -250,7 +263,7 @@ struct Smem {
 };
 
 // Trace layout in shared memory (u64): see g2_mega.h; [20] phase-begin stamp,
-// [21] inputs stamp, [24] timeline count, [32..160) timeline stamps (CTA 0, one step).
+// [21] inputs stamp, [22] timeline count, [32..160) timeline stamps (CTA 0, one step).
 struct Cx {
     const MegaParams *p;
     Smem s;
@@ -259,16 +272,16 @@ struct Cx {
     unsigned upar;      // parity of the next strip unit's reduction scratch
     int failed;         // this thread saw an expired wait
     bool tr;            // tracing (consumer thread 0)
-    bool tl;            // timeline stamps (CTA 0, step 0)
+    bool tl;            // timeline stamps (CTA 0, one step)
     u64 t0;
 };
 
 __device__ __forceinline__ void tr_stamp(Cx &cx) {
     if (cx.tl) {
-        const u64 n = cx.s.trc[24];
+        const u64 n = cx.s.trc[22];
         if (n < (u64)(kTraceSlots - 32)) {
             cx.s.trc[32 + n] = gtime() - cx.t0;
-            cx.s.trc[24] = n + 1;
+            cx.s.trc[22] = n + 1;
         }
     }
 }
@@ -574,17 +587,10 @@ __device__ __forceinline__ void block_unit(Cx &cx, const float *a, int rows, int
     float *part = cx.s.part;   // [RG][NB], RG * NB <= 4 * kCons <= kPart
     if (act) reinterpret_cast<float4 *>(part)[t] = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
     cons_sync();
-    for (int n = t; n < NB; n += kCons) {   // four independent partial sums, then a fixed tree
-        float y0 = part[n], y1 = 0.0f, y2 = 0.0f, y3 = 0.0f;
-        int g = 1;
-        for (; g + 3 < RG; g += 4) {
-            y0 += part[g * NB + n];
-            y1 += part[(g + 1) * NB + n];
-            y2 += part[(g + 2) * NB + n];
-            y3 += part[(g + 3) * NB + n];
-        }
-        for (; g < RG; ++g) y0 += part[g * NB + n];
-        acc_add(dst + n, (y0 + y1) + (y2 + y3));
+    for (int n = t; n < NB; n += kCons) {
+        float y = part[n];
+        for (int g = 1; g < RG; ++g) y += part[g * NB + n];
+        acc_add(dst + n, y);
     }
 }
 
@@ -848,6 +854,9 @@ __device__ __forceinline__ bool run_units(Cx &cx, const Sched &S, int step, int 
 
 }  // namespace
 
+// kTr: the traced instantiation (phase stamps when P.trace is set); in the
+// other one every trace branch folds away at compile time.
+template <bool kTr>
 __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const MegaParams &p = P;
@@ -860,7 +869,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     cx.failed = 0;
     cx.chunk_i = 0;
     cx.upar = 0;
-    cx.tr = p.trace != nullptr && threadIdx.x == 0;
+    cx.tr = kTr && p.trace != nullptr && threadIdx.x == 0;
     cx.tl = false;
     cx.t0 = cx.tr ? gtime() : 0;
     const int G = gridDim.x, E = p.E, L = p.L;
@@ -945,7 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     int tok = p.state->token, pos = p.state->pos;
     const int step_base = p.state->step, min_new = p.state->min_new;
     for (int step = 0; step < p.n_steps; ++step) {
-        cx.tl = cx.tr && cx.cta == 0 && step == min(3, p.n_steps - 1);
+        cx.tl = kTr && cx.tr && cx.cta == 0 && step == min(3, p.n_steps - 1);
         // x = wte[tok] + wpe[pos] (embed, math.cl:333)
         for (int i = cx.ctid; i < E; i += kCons) {
             const float x = p.wte[(size_t)tok * E + i] + p.wpe[(size_t)pos * E + i];
@@ -1045,17 +1054,17 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
             // when that CTA writes step s + 1; step s + 2 needs its step s + 1 partial.
             const unsigned ep = epoch_of(p, step, L, 0);
             u64 *tb = p.t_best + (size_t)(step & 1) * 2 * G;
-            if (cx.ctid == 0) {
-                for (int w = 0; w < kWarps; ++w)
-                    if (better(rv[w], ri[w], best, besti)) {
-                        best = rv[w];
-                        besti = ri[w];
-                    }
-                // release: this CTA's K/V rows of the step (ordered before this
-                // thread by the barrier above) become visible with the partial
-                __threadfence();
-                st_tag(tb + 2 * cx.cta, best, ep);
-                st_tag(tb + 2 * cx.cta + 1, __int_as_float(besti), ep);
+            if (cx.warp == 0) {   // the CTA's best of its warps' bests
+                best = cx.lane < kWarps ? rv[cx.lane] : -FLT_MAX;
+                besti = cx.lane < kWarps ? ri[cx.lane] : INT_MAX;
+                warp_argmax(best, besti);
+                if (cx.lane == 0) {
+                    // release: this CTA's K/V rows of the step (ordered before this
+                    // thread by the barrier above) become visible with the partial
+                    __threadfence();
+                    st_tag(tb + 2 * cx.cta, best, ep);
+                    st_tag(tb + 2 * cx.cta + 1, __int_as_float(besti), ep);
+                }
             }
             float *bv = cx.s.part;                                  // 2 * G <= kPart floats
             int *bi = reinterpret_cast<int *>(cx.s.attq);           // [0] token
@@ -1063,19 +1072,20 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
             if (!poll_vec(cx, tb, bv, 2 * G, ep, 3)) goto out;
             __threadfence();   // acquire: every CTA's K/V rows of this step, for the steps that follow
             tr_inputs(cx, 6);
-            if (cx.ctid == 0) {
+            if (cx.warp == 0) {   // the best of all CTAs' bests: lanes take CTAs c = lane mod 32
                 float gb = -FLT_MAX;
                 int gi = INT_MAX;
-                for (int c = 0; c < G; ++c) {
+                for (int c = cx.lane; c < G; c += 32) {
                     const int ix = __float_as_int(bv[2 * c + 1]);
                     if (better(bv[2 * c], ix, gb, gi)) {
                         gb = bv[2 * c];
                         gi = ix;
                     }
                 }
+                warp_argmax(gb, gi);
                 if (gi == INT_MAX) gi = 0;   // every logit NaN: never hand an invalid id to the next step
-                bi[0] = gi;
-                if (cx.cta == 0) {
+                if (cx.lane == 0) bi[0] = gi;
+                if (cx.cta == 0 && cx.lane == 0) {
                     p.out_tokens[step_base + step] = gi;
                     if (step == p.n_steps - 1) {
                         p.result[0] = gi;
@@ -1109,7 +1119,9 @@ size_t mega_smem_bytes(int E) {
            (kRedFloats + kMaxKeys + 192 + 64 + kPart + kCfgInts) * sizeof(float) + (size_t)(2 * E + 4) * sizeof(float);
 }
 int mega_threads() { return kThreads; }
-const void *mega_kernel_ptr() { return (const void *)mega_decode_kernel; }
+const void *mega_kernel_ptr(bool traced) {
+    return traced ? (const void *)mega_decode_kernel<true> : (const void *)mega_decode_kernel<false>;
+}
 int mega_slot_bytes() { return kSlotBytes; }
 int mega_max_keys() { return kMaxKeys; }
 

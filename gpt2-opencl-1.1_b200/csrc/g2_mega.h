@@ -39,15 +39,14 @@ struct MegaParams {
 constexpr int kTraceSlots = 160;
 // Trace words per CTA: [0..8) ns spent waiting for inputs: [1] B (q, k, v), [2] x after
 // the MLP, [4] x after attention, [5] LM head, [6] argmax; [8..16) ns of work after the
-// inputs arrived: [8] A, [9] B, [11] D, [13] LM head, [14] argmax; [16] ns waiting for ring
-// chunks, [17] kernel ns, [18] units, [19] chunks; SM cycles of D units in the c_fc strip
-// [22] and the mlp.c_proj block [23] over [25] units, of B units in attention [26] and the
-// attn.c_proj block [27] over [28] units; [32..160) CTA 0 only: the timeline of one step (step 3,
-// or the last step of a shorter launch): phase start/end stamps relative to kernel start.
+// inputs arrived: [8] A, [9] B, [11] D, [13] LM head, [14] argmax; [17] kernel ns; [22]
+// timeline stamps taken; [32..160) CTA 0 only: the timeline of one step (step 3, or the last
+// step of a shorter launch): phase start/end stamps relative to kernel start.
 
 size_t mega_smem_bytes(int E);
 int mega_threads();
-const void *mega_kernel_ptr();
+// The kernel; `traced` selects the instantiation that records the phase trace.
+const void *mega_kernel_ptr(bool traced);
 int mega_slot_bytes();
 int mega_max_keys();
 // Steps per launch (the accumulators of one launch are sized for this many).
