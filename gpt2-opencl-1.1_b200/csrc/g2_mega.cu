@@ -35,9 +35,10 @@
 //    rstd (x W' - mean colsum(W')) + b', so the statistics are reduced in the
 //    same pass as the products.  q, k, v reach the B units as 64-bit words
 //    (epoch << 32 | float bits): readiness costs one L2 round trip.
-//  * LM-head units are 16-row blocks of wte.  Unit g of a layer belongs to CTA
-//    g % gridDim.x, counting A, then B, then D units; the LM-head units
-//    continue the count.  The producer warp streams the CTA's units, in
+//  * Unit g of a layer belongs to CTA g % gridDim.x, counting A, then B, then
+//    D units.  For the LM head every CTA takes an equal contiguous share of
+//    the wte rows, in units of up to 15 rows (one per consumer warp), so all
+//    CTAs finish it together.  The producer warp streams the CTA's units, in
 //    consumption order, through an 8-slot shared-memory ring with
 //    cp.async.bulk (mbarrier full/empty, L2 evict-first).  The stream waits on
 //    no activation, so it runs ahead across layer and token boundaries.
@@ -85,8 +86,9 @@ constexpr int kGeoB = 16, kGeoDb = 24;     // block: CG, RG, RPC, magic(CG), NB,
 constexpr int kCfgMnq = 32, kCfgNq = 33;   // magic(nq), nq
 constexpr int kCfgOffB = 34, kCfgOffD = 35;   // nA % G, (nA + nB) % G
 constexpr int kCfgInvE = 36;               // 1 / E (float bits)
-constexpr int kCfgFirst = 40;              // [l] = first unit of layer l's count on this CTA, l <= L
-constexpr int kCfgInts = (kCfgFirst + kMegaMaxLayers + 1 + 3) / 4 * 4;   // a whole number of 16-byte words
+constexpr int kCfgLm0 = 37, kCfgLm1 = 38;  // this CTA's wte rows [lm0, lm1)
+constexpr int kCfgFirst = 40;              // [l] = first unit of layer l's count on this CTA, l < L
+constexpr int kCfgInts = (kCfgFirst + kMegaMaxLayers + 3) / 4 * 4;   // a whole number of 16-byte words
 constexpr int kMaxJ = 4;                   // vector words per consumer thread (E <= kMaxJ * kCons)
 // n / d for 0 <= n < 2048 and 1 <= d <= 480 as (n * magic(d)) >> 20, with
 // magic(d) = ceil(2^20 / d) (exact in that range: n (magic * d - 2^20) < 2^20).
@@ -123,25 +125,12 @@ __device__ __forceinline__ void acc_add(u64 *dst, float v) {
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(dst), "l"(c) : "memory");
 }
 __device__ __forceinline__ unsigned acc_count(u64 w) { return (unsigned)((w + (1ull << 54)) >> 55); }
-__device__ __forceinline__ float acc_value(u64 w, unsigned n) {
-    const long long s = (long long)(w - ((u64)n << 55));
-    return __ll2float_rn(s) * 2.3283064365386963e-10f;   // one rounding, then exact scaling by 2^-32
-}
 
 __device__ __forceinline__ void cons_sync() { asm volatile("bar.sync %0, %1;" ::"n"(kConsBar), "n"(kCons) : "memory"); }
 __device__ __forceinline__ int cons_and(int pred) {
     int r;
     asm volatile(
         "{ .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.s32 %0, 1, 0, q; }"
-        : "=r"(r)
-        : "r"(pred), "n"(kConsBar), "n"(kCons)
-        : "memory");
-    return r;
-}
-__device__ __forceinline__ int cons_or(int pred) {
-    int r;
-    asm volatile(
-        "{ .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.s32 %0, 1, 0, q; }"
         : "=r"(r)
         : "r"(pred), "n"(kConsBar), "n"(kCons)
         : "memory");
@@ -234,7 +223,7 @@ __device__ __forceinline__ void fma4(float4 &acc, float x, const float4 &w) {
 
 // ---- the per-step unit schedule (the same in producer and consumers) ------------------
 struct Sched {
-    int nA, nB, nD, nLM;   // units per phase
+    int nA, nB, nD;        // units per phase
     int per_layer;         // nA + nB + nD
     int G;                 // CTAs
     // first unit of a phase starting at global unit index g0 that belongs to CTA c
@@ -245,7 +234,6 @@ struct Sched {
     __device__ __forceinline__ int a_first(int l, int c) const { return first(l * per_layer, c); }
     __device__ __forceinline__ int b_first(int l, int c) const { return first(l * per_layer + nA, c); }
     __device__ __forceinline__ int d_first(int l, int c) const { return first(l * per_layer + nA + nB, c); }
-    __device__ __forceinline__ int lm_first(int L, int c) const { return first(L * per_layer, c); }
 };
 
 struct Smem {
@@ -311,23 +299,22 @@ __device__ __forceinline__ void fail(Cx &cx, int code) {
     atomicCAS(cx.p->err, 0, code);
 }
 
-// Uniform deadline check of a polling loop, every 64 rounds (a barrier round).
-__device__ __forceinline__ bool poll_expired(Cx &cx, unsigned round, u64 limit, int code) {
-    if ((round & 63u) != 63u) return false;
-    if (cons_or(gtime() > limit || cx.failed)) {
-        fail(cx, code);
-        return true;
-    }
-    return false;
-}
-
 // Poll n tagged words into dst until all carry `ep`.  All consumer threads.
+// Each warp polls its own words round after round with no barrier in between
+// (a warp leaves when all of its lanes have their words); one barrier at the
+// end, which also carries the failure flag.  The deadline is checked every 64
+// rounds.
 __device__ __forceinline__ bool poll_vec(Cx &cx, const u64 *src, float *dst, int n, unsigned ep, int code) {
     const u64 limit = gtime() + kTimeoutNs;
     // bit j of `pending`: word ctid + j * kCons not yet seen with the right epoch (n <= 32 * kCons)
     unsigned pending = 0;
-    for (int j = 0, i = cx.ctid; i < n; ++j, i += kCons) pending |= 1u << j;
-    for (unsigned round = 0;; ++round) {
+    if (!cx.failed)
+        for (int j = 0, i = cx.ctid; i < n; ++j, i += kCons) pending |= 1u << j;
+    for (unsigned round = 0; __any_sync(0xffffffffu, pending != 0); ++round) {
+        if ((round & 63u) == 63u && __any_sync(0xffffffffu, gtime() > limit)) {
+            fail(cx, code);
+            break;
+        }
         for (unsigned m = pending; m; m &= m - 1) {
             const int j = __ffs(m) - 1, i = cx.ctid + j * kCons;
             const u64 w = ld_tag(src + i);
@@ -336,16 +323,17 @@ __device__ __forceinline__ bool poll_vec(Cx &cx, const u64 *src, float *dst, int
                 pending &= ~(1u << j);
             }
         }
-        if (cons_and(pending == 0 && !cx.failed)) return true;
-        if (poll_expired(cx, round, limit, code)) return false;
     }
+    return cons_and(!cx.failed);
 }
 
 // Poll the accumulator at src (ncopy copies of E words; copy c collects the
 // units u with u % ncopy == c of the nunits contributors) until every word
 // holds its count, then x[i] = x[i] + (sum over copies in order + bias[i]) in
 // xres and xs.  The bias is loaded before the first round, so no load waits
-// after the accumulator turns ready.  All consumer threads.
+// after the accumulator turns ready.  The copies' fixed-point values are added
+// as integers (exact), then rounded to float once.  Rounds per warp, one
+// barrier at the end, as in poll_vec.  All consumer threads.
 __device__ __forceinline__ bool poll_acc(Cx &cx, const u64 *src, int ncopy, int nunits, const float *bias, int E,
                                          int code) {
     const u64 limit = gtime() + kTimeoutNs;
@@ -357,7 +345,12 @@ __device__ __forceinline__ bool poll_acc(Cx &cx, const u64 *src, int ncopy, int 
         bv[j] = i < E ? __ldg(bias + i) : 0.0f;
         if (i < E) pending |= 1u << j;
     }
-    for (unsigned round = 0;; ++round) {
+    if (cx.failed) pending = 0;
+    for (unsigned round = 0; __any_sync(0xffffffffu, pending != 0); ++round) {
+        if ((round & 63u) == 63u && __any_sync(0xffffffffu, gtime() > limit)) {
+            fail(cx, code);
+            break;
+        }
 #pragma unroll
         for (int j = 0; j < kMaxJ; ++j) {
             if (!(pending & (1u << j))) continue;
@@ -370,20 +363,20 @@ __device__ __forceinline__ bool poll_acc(Cx &cx, const u64 *src, int ncopy, int 
                 w[c] = ld_tag(src + (size_t)c * E + i);
                 ready = ready && acc_count(w[c]) == (unsigned)((nunits - c + ncopy - 1) / ncopy);
             }
-            if (ready) {
-                float v = acc_value(w[0], acc_count(w[0]));
+            if (ready) {   // the copies' fixed-point values summed exactly, then one rounding
+                long long s = (long long)(w[0] - ((u64)acc_count(w[0]) << 55));
 #pragma unroll
                 for (int c = 1; c < kAccCopies; ++c)
-                    if (c < ncopy) v += acc_value(w[c], acc_count(w[c]));
+                    if (c < ncopy) s += (long long)(w[c] - ((u64)acc_count(w[c]) << 55));
+                const float v = __ll2float_rn(s) * 2.3283064365386963e-10f;
                 const float x = cx.s.xres[i] + (v + bv[j]);
                 cx.s.xres[i] = x;
                 cx.s.xs[i] = x;
                 pending &= ~(1u << j);
             }
         }
-        if (cons_and(pending == 0 && !cx.failed)) return true;
-        if (poll_expired(cx, round, limit, code)) return false;
     }
+    return cons_and(!cx.failed);
 }
 
 // Per-thread sums of xs[0..n) and of its squares, in a fixed order.
@@ -657,9 +650,10 @@ __device__ __forceinline__ void producer(Cx &cx, const Sched &S) {
             }
         }
         const char *lm = reinterpret_cast<const char *>(p.lm);
-        for (int u = S.lm_first(L, cx.cta); u < S.nLM && ok; u += G) {
-            const size_t bytes = (size_t)min(p.lm_rows, p.V - u * p.lm_rows) * E * sizeof(float);
-            ok = produce(cx, lm + (size_t)u * p.lm_rows * E * sizeof(float), bytes, (size_t)E * 4, i, policy);
+        const int r1 = (int)((long long)(cx.cta + 1) * p.V / G);
+        for (int v0 = (int)((long long)cx.cta * p.V / G); v0 < r1 && ok; v0 += p.lm_rows) {
+            const size_t bytes = (size_t)min(p.lm_rows, r1 - v0) * E * sizeof(float);
+            ok = produce(cx, lm + (size_t)v0 * E * sizeof(float), bytes, (size_t)E * 4, i, policy);
         }
     }
     // Every copy issued must land before the CTA may exit (the ring is its destination).
@@ -692,8 +686,12 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
     }
     {   // q, k, v of head h at pos
         const u64 limit = gtime() + kTimeoutNs;
-        bool pend = cx.ctid < 192;
-        for (unsigned round = 0;; ++round) {
+        bool pend = cx.ctid < 192 && !cx.failed;
+        for (unsigned round = 0; __any_sync(0xffffffffu, pend); ++round) {
+            if ((round & 63u) == 63u && __any_sync(0xffffffffu, gtime() > limit)) {
+                fail(cx, 5);
+                break;
+            }
             if (pend) {
                 const u64 w = ld_tag(p.t_qkv + (cx.ctid >> 6) * E + h * 64 + (cx.ctid & 63));
                 if (tag_is(w, ep_in)) {
@@ -701,9 +699,8 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
                     pend = false;
                 }
             }
-            if (cons_and(!pend && !cx.failed)) break;
-            if (poll_expired(cx, round, limit, 5)) return false;
         }
+        if (!cons_and(!cx.failed)) return false;
     }
     tr_inputs(cx, 1);
     // scores s_j = q . k_j / 8 (the key at pos comes from the qkv vector)
@@ -910,7 +907,6 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     S.nA = 3 * E / p.cw_qkv;
     S.nB = p.NH * p.nq;
     S.nD = p.F / p.cw_fc;
-    S.nLM = (p.V + p.lm_rows - 1) / p.lm_rows;
     S.per_layer = S.nA + S.nB + S.nD;
     S.G = G;
     if (threadIdx.x == 0) {   // the per-CTA constants: every runtime division of the units, once
@@ -940,7 +936,9 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
         cf[kCfgOffB] = S.nA % G;
         cf[kCfgOffD] = (S.nA + S.nB) % G;
         cf[kCfgInvE] = __float_as_int(1.0f / (float)E);
-        for (int l = 0; l <= L; ++l) cf[kCfgFirst + l] = S.first(l * S.per_layer, cx.cta);
+        cf[kCfgLm0] = (int)((long long)cx.cta * p.V / G);
+        cf[kCfgLm1] = (int)((long long)(cx.cta + 1) * p.V / G);
+        for (int l = 0; l < L; ++l) cf[kCfgFirst + l] = S.first(l * S.per_layer, cx.cta);
     }
     __syncthreads();
 
@@ -964,11 +962,20 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
         cons_sync();
         // Per layer: A and B units on x; x += attention; D units; x += MLP.
         // The last pass (l == L) only takes in the MLP output of the last layer.
+        float lg[kMaxJ], lb[kMaxJ];   // LN_f gamma and beta, loaded before the last layer's exchange
         for (int l = 0; l <= L; ++l) {
             for (int half = 0; half < 2; ++half) {
                 if (l == L && half == 1) break;
                 if (l > 0 || half == 1) {   // x += (MLP of layer l - 1 | attention of layer l) + bias
                     const int lp = half ? l : l - 1;
+                    if (l == L) {
+#pragma unroll
+                        for (int j = 0; j < kMaxJ; ++j) {
+                            const int i = cx.ctid + j * kCons;
+                            lg[j] = i < E ? __ldg(p.lnf_g + i) : 0.0f;
+                            lb[j] = i < E ? __ldg(p.lnf_b + i) : 0.0f;
+                        }
+                    }
                     tr_begin(cx);
                     if (!poll_acc(cx, acc_of(p, step, lp, 1 - half), half ? 1 : kAccCopies, half ? p.NH : S.nD,
                                   half ? p.layers[lp].proj_b : p.layers[lp].fc2_b, E, half ? 6 : 2))
@@ -981,26 +988,31 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
         }
         // ---------------- LN_f + LM head + greedy argmax ----------------
         {
-            int u = cx.s.cfg[kCfgFirst + L];   // the first LM unit of this CTA
+            // this CTA's wte rows [v0, r1): an equal share, in units of up to lm_rows rows
+            int v0 = cx.s.cfg[kCfgLm0];
+            const int r1 = cx.s.cfg[kCfgLm1];
             const bool forbid = (step_base + step) < min_new;
             float best = -FLT_MAX;
             int besti = INT_MAX;
-            if (u < S.nLM) {
+            if (v0 < r1) {
                 tr_begin(cx);
                 tr_inputs(cx, 5);
                 float mean, rstd;
                 ln_stats(cx, E, mean, rstd);
                 // normalise in place with gamma / beta (math.cl:310); the rows read it 16 times
-                for (int i = cx.ctid; i < E; i += kCons)
-                    xs[i] = (xs[i] - mean) * rstd * __ldg(p.lnf_g + i) + __ldg(p.lnf_b + i);
+#pragma unroll
+                for (int j = 0; j < kMaxJ; ++j) {
+                    const int i = cx.ctid + j * kCons;
+                    if (i < E) xs[i] = (xs[i] - mean) * rstd * lg[j] + lb[j];
+                }
                 cons_sync();
                 // A unit holds up to kWarps rows over one or more chunks: all of its
                 // chunks are waited for, then warp w takes row w.
                 const int RPC = kSlotBytes / (E * 4);
                 const int E4 = E / 4;
                 const float4 *x4 = reinterpret_cast<const float4 *>(xs);
-                for (; u < S.nLM; u += G) {
-                    const int v0 = u * p.lm_rows, rows = min(p.lm_rows, p.V - v0);
+                for (; v0 < r1; v0 += p.lm_rows) {
+                    const int rows = min(p.lm_rows, r1 - v0);
                     const int nch = (rows + RPC - 1) / RPC;
                     for (int k = 0; k < nch; ++k) chunk_wait(cx, k);
                     if (cx.warp < rows) {
