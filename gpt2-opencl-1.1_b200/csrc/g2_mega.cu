@@ -756,11 +756,11 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
     for (int w = 1; w < kWarps; ++w) Lt += rb[16 + w];
     // P.V: thread (grp, dq) sums keys grp, grp + kPvGroups, ... of dims 4 dq .. 4 dq + 3
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j0 = grp; j0 < T; j0 += 4 * kPvGroups) {
-        float4 vv[4];
-        float pp[4];
+    for (int j0 = grp; j0 < T; j0 += 8 * kPvGroups) {   // eight keys per round: their rows in flight together
+        float4 vv[8];
+        float pp[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 8; ++u) {
             const int j = j0 + u * kPvGroups;
             const bool in = j < T;
             vv[u] = (in && j != pos) ? V4[(size_t)j * 16 + dq] : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -769,7 +769,7 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
             pp[u] = in ? pr[j] : 0.0f;
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) fma4(o, pp[u], vv[u]);
+        for (int u = 0; u < 8; ++u) fma4(o, pp[u], vv[u]);
     }
     reinterpret_cast<float4 *>(part)[grp * 16 + dq] = o;   // [kPvGroups][64]
     cons_sync();
