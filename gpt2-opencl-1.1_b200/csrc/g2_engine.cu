@@ -827,8 +827,14 @@ static int forward_rows(g2_engine *e, int nrows, int max_pos, bool decode_rows =
             rows_gemm<WT>(e, l, 0, e->xln, nrows, e->w<WT>(o.qkv_w), e->w<WT>(o.qkv_b), nullptr, e->qkv, 3 * E, E,
                           EPI_BIAS | EPI_KV, &e->kv, rows);
         }
-        launch_attention<WT>(e->qkv, 3 * E, e->kv, l, rows, nrows, e->attn, E, e->attn_partial, e->attn_ctr, max_pos,
-                             st, ope, qp);
+        // A prompt of more than 64 rows: causal attention in 64 x 64 tiles (each K/V tile read once per
+        // 64 queries).  Decode rows (one query per sequence) and short prompts (whose tiles would
+        // give one CTA per head): one CTA per (head, 128-key chunk, row).
+        if (!decode_rows && nrows > 64)
+            launch_prefill_attention<WT>(e->qkv, 3 * E, e->kv, l, rows, nrows, e->attn, E, st, ope);
+        else
+            launch_attention<WT>(e->qkv, 3 * E, e->kv, l, rows, nrows, e->attn, E, e->attn_partial, e->attn_ctr,
+                                 max_pos, st, ope, qp);
         e->launches += 1;
         const bool ln2_done = rows_gemm<WT>(e, l, 1, e->attn, nrows, e->w<WT>(o.proj_w), e->w<WT>(o.proj_b), e->h,
                                             e->h, E, E, EPI_BIAS | EPI_RESID, nullptr, rows, OperandOut(),

@@ -127,6 +127,14 @@ void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int 
                       float *out, int out_stride, float *partial, unsigned *counters, int max_pos_hint,
                       cudaStream_t st, OperandOut op = OperandOut(), QkvPartials qp = QkvPartials());
 
+// Causal attention of a prompt's rows (prefill of one slot: every row has the
+// same slot, row r attends to positions 0..pos[r], whose K and V are already in
+// the cache).  Tiles of 64 query rows x 64 keys with K and V staged in shared
+// memory; out[r][h*64 + d] (and `op`, the next GEMM's operand).
+template <typename KT>
+void launch_prefill_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
+                              float *out, int out_stride, cudaStream_t st, OperandOut op = OperandOut());
+
 // LM head on one row x (fp32 [E]) with the final LayerNorm fused:
 // logits[v] = LN_f(x) . wte[v]; argmax over v < V (first index on ties,
 // EOS excluded while state->step < state->min_new when state != NULL, or

@@ -113,6 +113,22 @@ __device__ __forceinline__ void fma_vec(float *acc, uint4 w, float x, __half) {
         acc[2 * i + 1] = fmaf(x, f.y, acc[2 * i + 1]);
     }
 }
+// 16 bytes of cache elements as fp32
+__device__ __forceinline__ void unpack_vec(uint4 w, float *f, float) {
+    f[0] = __uint_as_float(w.x);
+    f[1] = __uint_as_float(w.y);
+    f[2] = __uint_as_float(w.z);
+    f[3] = __uint_as_float(w.w);
+}
+__device__ __forceinline__ void unpack_vec(uint4 w, float *f, __half) {
+    const __half2 *h = reinterpret_cast<const __half2 *>(&w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 v = __half22float2(h[i]);
+        f[2 * i] = v.x;
+        f[2 * i + 1] = v.y;
+    }
+}
 // dot of 16 bytes of weights with xs[0..n)
 __device__ __forceinline__ float dot_vec(uint4 w, const float *xs, float) {
     return __uint_as_float(w.x) * xs[0] + __uint_as_float(w.y) * xs[1] + __uint_as_float(w.z) * xs[2] +
@@ -511,6 +527,202 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
 }
 
 // ------------------------------------------------------------------------------
+// Causal attention of a prompt (prefill): the per-query loop of prefill()
+// (main.c:1759-1763 over attn_scores_1q, attn_softmax_1q, attn_out_1q,
+// math.cl:388-476) for all query rows of one slot in one launch.
+// ------------------------------------------------------------------------------
+struct PrefillAttnArgs {
+    const float *qkv;    // [rows][qkv_stride]; q of head h at column 64 h
+    int qkv_stride;
+    KVLayout kv;         // the rows' K and V are in the cache already
+    int layer;
+    Rows rows;           // pos[r]: the row's position; slot: the same for every row of the pass
+    int nrows;
+    float *out;
+    int out_stride;
+    OperandOut op;
+};
+constexpr int kPaTile = 64;                 // query rows and keys per tile
+constexpr int kPaLd = kHeadDim + 4;         // row stride of the shared-memory tiles (floats)
+constexpr size_t kPaSmem = 4ull * kPaTile * kPaLd * sizeof(float);   // Q, K, V and P tiles
+
+// CTA (h, t) takes query rows 64 t .. 64 t + 63 of head h and walks the keys
+// 0 .. (largest position of its rows) in tiles of 64.  Each K and V tile is
+// staged in shared memory once for the 64 queries (the single-query kernel
+// reads it again for every row); thread (ty, tx) holds the scores of rows
+// 4 ty .. 4 ty + 3 for keys tx + 16 j (j < 4) and the outputs of the same rows
+// for dims 4 tx .. 4 tx + 3.  The softmax of each row is merged online across
+// the key tiles.  Keys after a row's position are masked (causal); keys past
+// the tile's largest position are staged as zeros.  All arithmetic in fp32.
+template <typename KT>
+__global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillAttnArgs a) {
+    pdl_wait();
+    pdl_launch();
+    constexpr int QT = kPaTile, LD = kPaLd;
+    constexpr int VN = 16 / sizeof(KT);   // cache elements per 16-byte load
+    constexpr int G = kHeadDim / VN;      // 16-byte loads per key row
+    extern __shared__ __align__(16) float pa_sm[];
+    float *Qs = pa_sm, *Ks = Qs + QT * LD, *Vs = Ks + QT * LD, *Ps = Vs + QT * LD;
+    __shared__ int spos[QT];
+    const int h = blockIdx.x, r0 = blockIdx.y * QT, tid = threadIdx.x;
+    const int ty = tid >> 4, tx = tid & 15;
+    const int nr = min(QT, a.nrows - r0);
+    if (tid < QT) spos[tid] = tid < nr ? a.rows.pos[r0 + tid] : -1;
+    for (int i = tid; i < QT * (kHeadDim / 4); i += blockDim.x) {   // q / sqrt(64)
+        const int row = i / (kHeadDim / 4), c4 = i % (kHeadDim / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < nr) v = reinterpret_cast<const float4 *>(a.qkv + (size_t)(r0 + row) * a.qkv_stride + h * kHeadDim)[c4];
+        reinterpret_cast<float4 *>(Qs + row * LD)[c4] = make_float4(v.x * 0.125f, v.y * 0.125f, v.z * 0.125f, v.w * 0.125f);
+    }
+    __syncthreads();
+    int pmax = -1;
+    for (int i = 0; i < nr; ++i) pmax = max(pmax, spos[i]);
+    int mypos[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mypos[i] = spos[ty * 4 + i];
+    const long long base = (long long)a.rows.slot[r0] * a.kv.slot_stride + (long long)a.layer * a.kv.layer_stride +
+                           (long long)h * a.kv.max_seq * kHeadDim;
+    const KT *K = reinterpret_cast<const KT *>(a.kv.k) + base;
+    const KT *V = reinterpret_cast<const KT *>(a.kv.v) + base;
+    float m[4], l[4], o[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[i][c] = 0.0f;
+    }
+    for (int j0 = 0; j0 <= pmax; j0 += QT) {
+        for (int i = tid; i < QT * G; i += blockDim.x) {   // stage keys j0 .. j0 + 63 as fp32
+            const int row = i / G, g = i % G;
+            float f[VN];
+            if (j0 + row <= pmax) {
+                const uint4 kw = *reinterpret_cast<const uint4 *>(K + (size_t)(j0 + row) * kHeadDim + g * VN);
+                const uint4 vw = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + row) * kHeadDim + g * VN);
+                unpack_vec(kw, f, KT());
+#pragma unroll
+                for (int e = 0; e < VN; ++e) Ks[row * LD + g * VN + e] = f[e];
+                unpack_vec(vw, f, KT());
+#pragma unroll
+                for (int e = 0; e < VN; ++e) Vs[row * LD + g * VN + e] = f[e];
+            } else {
+#pragma unroll
+                for (int e = 0; e < VN; ++e) Ks[row * LD + g * VN + e] = Vs[row * LD + g * VN + e] = 0.0f;
+            }
+        }
+        __syncthreads();
+        float s[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[i][j] = 0.0f;
+#pragma unroll 4
+        for (int k = 0; k < kHeadDim; k += 4) {
+            float4 qv[4], kv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4 *>(Qs + (ty * 4 + i) * LD + k);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4 *>(Ks + (tx + 16 * j) * LD + k);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
+                    s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
+                    s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
+                    s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
+                }
+        }
+        // online softmax per row: the row's 64 keys are spread over the 16 lanes of a half-warp
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float mt = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (j0 + tx + 16 * j > mypos[i]) s[i][j] = -INFINITY;
+                mt = fmaxf(mt, s[i][j]);
+            }
+#pragma unroll
+            for (int x = 8; x > 0; x >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, x));
+            const float mn = fmaxf(m[i], mt);
+            const bool none = mn == -INFINITY;   // no key of this row yet (or a padding row)
+            const float sc = none ? 1.0f : expf(m[i] - mn);
+            float ls = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float pj = s[i][j] == -INFINITY ? 0.0f : expf(s[i][j] - mn);
+                s[i][j] = pj;
+                ls += pj;
+            }
+#pragma unroll
+            for (int x = 8; x > 0; x >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, x);
+            l[i] = l[i] * sc + ls;
+            m[i] = mn;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) o[i][c] *= sc;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) Ps[(ty * 4 + i) * LD + tx + 16 * j] = s[i][j];
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int j = 0; j < QT; j += 4) {   // O += P V
+            float4 pv[4], vv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4 *>(Ps + (ty * 4 + i) * LD + j);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) vv[u] = *reinterpret_cast<const float4 *>(Vs + (j + u) * LD + tx * 4);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float pp[4] = {pv[i].x, pv[i].y, pv[i].z, pv[i].w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    o[i][0] = fmaf(pp[u], vv[u].x, o[i][0]);
+                    o[i][1] = fmaf(pp[u], vv[u].y, o[i][1]);
+                    o[i][2] = fmaf(pp[u], vv[u].z, o[i][2]);
+                    o[i][3] = fmaf(pp[u], vv[u].w, o[i][3]);
+                }
+            }
+        }
+        __syncthreads();   // the next tile overwrites K, V and P
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int row = ty * 4 + i;
+        if (row >= nr) continue;
+        const float inv = 1.0f / l[i];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const size_t oi = (size_t)(r0 + row) * a.out_stride + h * kHeadDim + tx * 4 + c;
+            const float v = o[i][c] * inv;
+            a.out[oi] = v;
+            put_operand(a.op, oi, v);
+        }
+    }
+}
+
+template <typename KT>
+void launch_prefill_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
+                              float *out, int out_stride, cudaStream_t st, OperandOut op) {
+    static const bool attr = [] {   // more than 48 KB of dynamic shared memory: opt in once per type
+        return cudaFuncSetAttribute(prefill_attn_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kPaSmem) == cudaSuccess;
+    }();
+    (void)attr;
+    PrefillAttnArgs a;
+    a.qkv = qkv;
+    a.qkv_stride = qkv_stride;
+    a.kv = kv;
+    a.layer = layer;
+    a.rows = rows;
+    a.nrows = nrows;
+    a.out = out;
+    a.out_stride = out_stride;
+    a.op = op;
+    dim3 grid(kv.n_head, (nrows + kPaTile - 1) / kPaTile);
+    launch_pdl(prefill_attn_kernel<KT>, grid, dim3(256), kPaSmem, st, a);
+}
+
+// ------------------------------------------------------------------------------
 // LM head (one row) with the final LayerNorm and greedy argmax fused
 // ------------------------------------------------------------------------------
 template <typename WT>
@@ -893,6 +1105,8 @@ void launch_step_advance(int *step_ptr, cudaStream_t st) { launch_pdl(step_advan
                                   const int *, const int *, cudaStream_t);                                           \
     template void launch_gemm_rows<WT>(const float *, const WT *, const WT *, const float *, float *, int, int, int, \
                                        int, const KVLayout *, int, Rows, cudaStream_t);                              \
+    template void launch_prefill_attention<WT>(const float *, int, const KVLayout &, int, Rows, int, float *, int,   \
+                                               cudaStream_t, OperandOut);                                              \
     template void launch_attention<WT>(const float *, int, const KVLayout &, int, Rows, int, float *, int, float *,  \
                                        unsigned *, int, cudaStream_t, OperandOut, QkvPartials);                       \
     template void launch_lm_head<WT>(const float *, const WT *, const WT *, const WT *, float *, int, int, int, int, \

@@ -129,6 +129,38 @@ def test_prefill_decode_vs_oracle_affine(g2, tiny_affine_model):
     ref.close()
 
 
+@pytest.mark.parametrize("n", [1, 63, 64, 65, 130, 200])
+def test_prefill_attention_tiles_vs_oracle(g2, tiny_affine_model, n):
+    """Prompt lengths on both sides of the prefill attention's 64-row / 64-key
+    tiles (prompts of up to 64 rows take the per-row kernel, longer ones the
+    tiled one).  The last row's logits depend on every row's layer-0 attention
+    (through layer 1's keys and values); the decode step after it reads the
+    cache the prefill wrote."""
+    ref = oracle.RefModel(tiny_affine_model)
+    prompt = synth.prompt_ids(40 + n, n)
+    ref.prefill(prompt)
+    with g2.Engine(tiny_affine_model) as eng:
+        eng.prefill(prompt)
+        assert rel(eng.logits(), ref.logits()) <= 1e-4
+        tok = int(np.argmax(ref.logits()[:50257]))
+        ref.decode(tok, n)
+        eng.decode(tok, n)
+        assert rel(eng.logits(), ref.logits()) <= 1e-4
+    ref.close()
+
+
+def test_prefill_attention_tiles_fp16(g2, tmp_path):
+    """The same over three query tiles with an fp16 cache, against the fp32 oracle on the rounded weights."""
+    d = synth.make_model(str(tmp_path / "f16t"), synth.TINY, seed=5, dtype="f16", affine=True)
+    ref = oracle.RefModel(d)
+    prompt = synth.prompt_ids(13, 150)
+    ref.prefill(prompt)
+    with g2.Engine(d, dtype=g2.G2_F16) as eng:
+        eng.prefill(prompt)
+        assert rel(eng.logits(), ref.logits()) <= FP16_TOL
+    ref.close()
+
+
 def test_persistent_and_graph_decode_agree(g2, tiny_affine_model, monkeypatch):
     """The persistent decode kernel (default for fp32) and the per-kernel graph
     path (G2_NO_MEGA=1) give the same greedy stream and matching logits, and
