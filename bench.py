@@ -17,6 +17,12 @@ weights, no collective on the data path): weak scaling.
 it -- g2_prefill, then per token g2_decode (token + position copied from
 pinned host memory) and g2_argmax (the token read back) -- wall-clock.
 
+``batched`` (on by default, ``--no-batched`` skips it) measures the two
+batched configurations on the same GPUs in the same run, each with its own
+tok/s, roofline, e2e and clocks: c5 (GPT-2 XL fp32, 32 sequences per GPU,
+weak scaling) and c4 (GPT-2 medium fp16, 32 sequences in total split over
+the GPUs, strong scaling); min(K, 5) timed steps each after W warm-up steps.
+
 ``--impl reference`` runs the reference's own prefill()/decode()/
 sample_next_token() (main.c + math.cl compiled for the host CPU,
 oracle/_ref) on this machine's cores, for a bounded sample of the workload.
@@ -47,7 +53,8 @@ CONFIGS = {
     "c5": dict(shape="XL", dtype="f32", batch=32, prompt=128, steps=384, desc="GPT-2 XL fp32, 32 sequences per GPU, prompt 128 + 384 greedy steps"),
 }
 README_DECODE_MS = 40.2   # reference, GT 730, GPT-2 small fp32 B=1 (README.md:59)
-MODEL_CACHE = os.environ.get("G2_MODEL_CACHE", os.path.join(ROOT, "_work", "models"))
+METRIC = "decode tok/s (B=1 ms/token; batched) + HBM GB/s % of peak"
+DATA = "synthetic (seeded N(0,0.02) weights, seeded uniform prompt ids)"
 
 
 def peaks():
@@ -69,8 +76,8 @@ class Clocks:
 
     def __init__(self, gpu: int):
         self.gpu = gpu
-        self.path = os.path.join(ROOT, "_work", f"clocks_{os.getpid()}.csv")
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        import tempfile
+        self.path = os.path.join(tempfile.gettempdir(), f"g2_clocks_{os.getpid()}.csv")
         self.p = None
 
     def start(self):
@@ -117,7 +124,7 @@ def model_for(cfg):
     from gpt2b200 import synth
     shape = getattr(synth, cfg["shape"])
     name = f"{cfg['shape'].lower()}_{cfg['dtype']}_s0"
-    return synth.ensure_model(os.path.join(MODEL_CACHE, name), shape, seed=0, dtype=cfg["dtype"]), shape
+    return synth.ensure_model(os.path.join(synth.default_cache(), name), shape, seed=0, dtype=cfg["dtype"]), shape
 
 
 def kv_bytes(shape, elem, prompt, steps, batch):
@@ -261,10 +268,36 @@ def run_c2(args):
     print(json.dumps(line), flush=True)
 
 
+def weight_bytes(shape, elem):
+    """Weights, biases and LayerNorm parameters streamed per decode step (the engine's
+    g2_config.weight_bytes): elem * [L (4E^2 + 2EF) + E V_pad] + elem * [L (9E + F) + 2E]."""
+    L, E, F = shape.n_layer, shape.n_embd, shape.ffn
+    return elem * (L * (4 * E * E + 2 * E * F) + E * shape.padded_vocab) + elem * (L * (9 * E + F) + 2 * E)
+
+
+def workload_config(name, cfg, ws, rank=0):
+    """The `config` object of a line for workload `name` on `ws` GPUs (the same in both arms)."""
+    from gpt2b200 import replicas, synth
+    shape = getattr(synth, cfg["shape"])
+    scaling = "strong" if name == "c4" else "weak"
+    B = len(replicas.shard(cfg["batch"], ws, rank, scaling))
+    wb = weight_bytes(shape, 2 if cfg["dtype"] == "f16" else 4)
+    return {"workload": name, "description": cfg["desc"], "sequences_per_gpu": B,
+            "sequences_total": cfg["batch"] * (ws if scaling == "weak" else 1), "decode_steps_per_step": cfg["steps"],
+            "parallelism": f"replicas x{ws} (independent sequences)",
+            "l2": f"weights {wb / 1e6:.0f} MB per decode step > 126 MB L2 (no flush needed)"}
+
+
 def run_reference(args, cfg):
+    """The reference's own code (oracle/_ref: main.c + math.cl compiled for the host
+    CPU) on this machine's cores.  Under torchrun only rank 0 runs; it takes every
+    host core (OMP_NUM_THREADS is set before the library loads, overriding
+    torchrun's 1).  N GPUs' worth of sequences would run one after another on
+    those cores, so the job's rate equals the single-sequence rate measured here."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
+    os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
     try:
         import oracle
         if not oracle.ref_available():
@@ -280,35 +313,33 @@ def run_reference(args, cfg):
         if i >= args.warmup:
             per.append(r)
     val = statistics.mean(p["value"] for p in per)
-    line = {"metric": "decode tok/s (B=1 ms/token; batched) + HBM GB/s % of peak", "value": round(val, 4),
+    line = {"metric": METRIC, "value": round(val, 4),
             "unit": "tok/s", "impl": "reference", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 / val, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": round(val / (1000.0 / README_DECODE_MS), 4), "dtype": "f32", "data": "synthetic",
-            "config": {"workload": args.config, "description": cfg["desc"], "sequences_per_gpu": 1},
+            "vs_baseline": None, "dtype": "f32", "data": DATA,
+            "config": workload_config(args.config, cfg, ws),
             "cpu_baseline": {k: per[-1][k] for k in ("kind", "cores", "sample")} | {"value": round(val, 4), "unit": "tok/s"},
-            "e2e": {"value": round(val, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(val, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": (f"{ws} GPU(s)' worth of sequences run one after another on all {os.cpu_count()} host threads: "
+                     "the job's rate is the single-sequence rate" if ws > 1 else None)}
     print(json.dumps(line))
 
 
-def run_ours(args, cfg):
-    import torch
-    ws, rank, local = dist_env()
-    if ws > 1:
-        import datetime
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    import gpt2b200 as g2
-    from gpt2b200 import synth
-    d, shape = model_for(cfg)
-    from gpt2b200 import replicas
-    # sequences of this rank: c4 splits 32 in total over the ranks (strong), the others
-    # give every rank its own `batch` sequences (weak); prompts are seeded by global index
-    scaling = "strong" if args.config == "c4" else "weak"
+class Measured(dict):
+    pass
+
+
+def measure(name, cfg, args, steps, warmup, ws, rank, local, dist, torch, g2, synth, replicas, loaded):
+    """One workload on this rank's engine: `warmup` untimed generations, then `steps`
+    timed ones (device time of the decode phases, CUDA events on the engine's
+    stream), then the e2e runs through the C ABI with host buffers.  Returns the
+    line's fields (on every rank; timings are max over ranks)."""
+    d, shape = loaded[name]
+    scaling = "strong" if name == "c4" else "weak"
     mine = replicas.shard(cfg["batch"], ws, rank, scaling)
     B = len(mine)
     dtype = g2.G2_F16 if cfg["dtype"] == "f16" else g2.G2_F32
-    eng = g2.Engine(d, device=local if ws > 1 else 0, max_batch=B, dtype=dtype)
+    eng = g2.Engine(d, device=local if ws > 1 else 0, max_batch=max(B, 1), dtype=dtype)
     n_new = cfg["steps"] + 1
     prompts = [synth.prompt_ids(i, cfg["prompt"]) for i in mine]
 
@@ -317,10 +348,9 @@ def run_ours(args, cfg):
             eng.generate(prompts[0], n_new)
         else:
             eng.generate_batch(prompts, n_new)
-        pre, dec, nd = eng.last_timing()
-        return pre, dec, nd
+        return eng.last_timing()
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         one_step()
     barrier = (lambda: (dist.barrier(), torch.cuda.synchronize())) if ws > 1 else torch.cuda.synchronize
     clocks = Clocks(local)
@@ -330,7 +360,7 @@ def run_ours(args, cfg):
     t0 = time.perf_counter()
     pre_ms = dec_ms = 0.0
     dec_steps = 0
-    for _ in range(args.steps):
+    for _ in range(steps):
         p, dm, nd = one_step()
         pre_ms += p
         dec_ms += dm
@@ -340,13 +370,11 @@ def run_ours(args, cfg):
     barrier()
     clk = clocks.stop()
     launches = eng.launch_count() - l0
-    # e2e: the same workload through the C ABI with host buffers, wall-clock: g2_generate
+    # e2e: the same workload through the C ABI with host buffers, wall-clock: g2_generate(_batch)
     # (prompt ids copied from host memory, generated ids copied back), and for B = 1 also
     # the reference's host loop (g2_prefill, then per token g2_decode + g2_argmax).
-    e2e_t = 0.0
-    e2e_tokens = 0
-    loop_t, loop_tokens = 0.0, 0
-    reps = max(1, min(args.steps, 3))
+    e2e_t, loop_t, loop_tokens = 0.0, 0.0, 0
+    reps = max(1, min(steps, 3))
     for _ in range(reps):
         t1 = time.perf_counter()
         if B == 1:
@@ -354,17 +382,14 @@ def run_ours(args, cfg):
         else:
             eng.generate_batch(prompts, n_new)
         e2e_t += time.perf_counter() - t1
-        e2e_tokens += cfg["steps"] * B
-    h2d = 4 * B * cfg["prompt"] + 12 * B
-    d2h = 4 * B * n_new
     if B == 1:
         for _ in range(reps):
             t1 = time.perf_counter()
             eng.prefill(prompts[0])
             tok, _ = eng.argmax(forbid_eos=True)
             pos = cfg["prompt"]
-            for s in range(cfg["steps"]):
-                eng.decode(tok, pos + s)
+            for s_ in range(cfg["steps"]):
+                eng.decode(tok, pos + s_)
                 tok, _ = eng.argmax(forbid_eos=True)
             loop_t += time.perf_counter() - t1
             loop_tokens += cfg["steps"]
@@ -372,59 +397,98 @@ def run_ours(args, cfg):
     elem = 2 if cfg["dtype"] == "f16" else 4
     per_seq_kv = kv_bytes(shape, elem, cfg["prompt"], cfg["steps"], 1)
     bytes_per_step = cfgd.weight_bytes + per_seq_kv * B / cfg["steps"] + B * (2 * shape.n_embd * elem + 4 * shape.padded_vocab)
-    dec_max, pre_max, wall_max = replicas.max_over_ranks([dec_ms, pre_ms, wall], device="cuda")
-    e2e_local = replicas.max_over_ranks([e2e_t, loop_t], device="cuda")
+    persistent = bool(cfgd.persistent) and B == 1
+    eng.close()
+    dec_max, pre_max, wall_max, e2e_max, loop_max = replicas.max_over_ranks([dec_ms, pre_ms, wall, e2e_t, loop_t],
+                                                                           device="cuda")
+    n_total = cfg["batch"] * (ws if scaling == "weak" else 1)    # sequences over all ranks
+    total_tokens = dec_steps * n_total
+    value = total_tokens / (dec_max / 1000.0)
+    step_s = dec_max / 1000.0 / max(dec_steps, 1)            # seconds per decode step (all B rows of a rank)
+    achieved = bytes_per_step / step_s / 1e9
+    peak, peak_kind = peaks()
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", f"traffic_{name}.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get("bytes_per_decode_step")
+    kernel = ("mega_decode_kernel (persistent: every layer, LM head and greedy argmax of all decode steps "
+              "in one launch)" if persistent else
+              "decode step kernels (embed, 5-7 per layer on the tensor cores, LM head + argmax) in a CUDA graph")
+    h2d = 4 * B * cfg["prompt"] + 12 * B
+    d2h = 4 * B * n_new
+    m = Measured(
+        value=round(value, 3), unit="tok/s", steps=steps, warmup=warmup, scaling=scaling,
+        ms_per_step=round((dec_max + pre_max) / max(steps, 1), 4),
+        ms_per_token=round(1000.0 * step_s, 5) if B == 1 else None,
+        ms_per_decode_step=round(1000.0 * step_s, 5),
+        prefill_ms=round(pre_max / max(steps, 1), 4),
+        dtype=cfg["dtype"],
+        config=workload_config(name, cfg, ws),
+        roofline={"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                  "frac": round(achieved / peak, 4), "peak_source": peak_kind, "bytes_per_step": int(bytes_per_step),
+                  "traffic": traffic},
+        e2e={"value": round(cfg["steps"] * n_total / e2e_max * reps, 3) if e2e_max > 0 else None, "unit": "tok/s",
+             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+             "path": ("g2_generate" if B == 1 else "g2_generate_batch") + " (C ABI, host buffers, wall-clock, "
+                     "prefill included)",
+             "host_loop": ({"value": round(loop_tokens * ws / loop_max, 3), "unit": "tok/s",
+                            "path": "g2_prefill + per-token g2_decode/g2_argmax (the reference's host loop)"}
+                           if loop_max > 0 else None)},
+        gpu_launches=int(launches) * ws, wall_s=round(wall_max, 4))
+    if clk:
+        m["clocks"] = clk
+    return m
+
+
+def run_ours(args, cfg):
+    import torch
+    ws, rank, local = dist_env()
+    dist = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    import gpt2b200 as g2
+    from gpt2b200 import replicas, synth
+    names = [args.config] + ([b for b in ("c4", "c5") if b != args.config] if args.batched else [])
+    # The synthetic checkpoints are written once per node (local rank 0) before any rank reads them.
+    loaded = {}
+    for n in names:
+        c = dict(CONFIGS[n])
+        if local == 0:
+            loaded[n] = model_for(c)
+        if ws > 1:
+            dist.barrier()
+        if local != 0:
+            loaded[n] = model_for(c)
+    main = measure(args.config, cfg, args, args.steps, args.warmup, ws, rank, local, dist, torch, g2, synth,
+                   replicas, loaded)
+    batched = {}
+    for n in names[1:]:
+        c = dict(CONFIGS[n])
+        k = min(args.steps, 5)
+        batched[n] = measure(n, c, args, k, args.warmup, ws, rank, local, dist, torch, g2, synth, replicas, loaded)
     if rank == 0:
-        n_total = cfg["batch"] * (ws if scaling == "weak" else 1)    # sequences over all ranks
-        total_tokens = dec_steps * n_total
-        value = total_tokens / (dec_max / 1000.0)
-        step_s = dec_max / 1000.0 / max(dec_steps, 1)            # seconds per decode step (all B rows)
-        achieved = bytes_per_step / step_s / 1e9
-        peak, peak_kind = peaks()
-        traffic = None
-        tp = os.path.join(ROOT, "profiles", f"traffic_{args.config}.json")
-        if os.path.exists(tp):
-            traffic = json.load(open(tp)).get("bytes_per_decode_step")
-        persistent = bool(cfgd.persistent) and B == 1
-        kernel = ("mega_decode_kernel (persistent: every layer, LM head and greedy argmax of all decode steps "
-                  "in one launch)" if persistent else
-                  "decode step kernels (embed, 5 per layer, LM head + argmax)" + (" in a CUDA graph" if B == 1 else ""))
-        e2e_max, loop_max = e2e_local
-        line = {
-            "metric": "decode tok/s (B=1 ms/token; batched) + HBM GB/s % of peak",
-            "value": round(value, 3), "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round((dec_max + pre_max) / max(args.steps, 1), 4),
-            "ms_per_token": round(1000.0 * step_s, 5),
-            "prefill_ms": round(pre_max / max(args.steps, 1), 4),
-            "higher_is_better": True, "scaling": scaling,
-            "vs_baseline": round((value / ws) / (1000.0 / README_DECODE_MS), 2) if args.config in ("c1", "c3") else None,
-            "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,0.02) weights, seeded uniform prompt ids)",
-            "config": {"workload": args.config, "description": cfg["desc"], "sequences_per_gpu": B,
-                       "decode_steps_per_step": cfg["steps"], "parallelism": f"replicas x{ws} (independent sequences)",
-                       "l2": f"weights {cfgd.weight_bytes / 1e6:.0f} MB per decode step > 126 MB L2 (no flush needed)"},
-            "roofline": {"bound": "hbm", "kernel": kernel,
-                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "bytes_per_step": int(bytes_per_step), "traffic": traffic},
-            "e2e": {"value": round(e2e_tokens / B * n_total / e2e_max, 3) if e2e_max > 0 else None, "unit": "tok/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": ("g2_generate" if B == 1 else "g2_generate_batch") + " (C ABI, host buffers, wall-clock, "
-                            "prefill included)",
-                    "host_loop": ({"value": round(loop_tokens * ws / loop_max, 3), "unit": "tok/s",
-                                   "path": "g2_prefill + per-token g2_decode/g2_argmax (the reference's host loop)"}
-                                  if loop_max > 0 else None)},
-            "gpu_launches": int(launches) * ws,
-            "wall_s": round(wall_max, 4),
-        }
-        if clk:
-            line["clocks"] = clk
+        line = {"metric": METRIC, "value": main["value"], "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": main["ms_per_step"], "ms_per_token": main["ms_per_token"],
+                "prefill_ms": main["prefill_ms"], "higher_is_better": True, "scaling": main["scaling"],
+                "vs_baseline": (round((main["value"] / ws) / (1000.0 / README_DECODE_MS), 2)
+                                if args.config in ("c1", "c3") else None),
+                "dtype": cfg["dtype"], "data": DATA, "config": main["config"],
+                "roofline": main["roofline"], "e2e": main["e2e"], "gpu_launches": main["gpu_launches"],
+                "wall_s": main["wall_s"]}
+        if "clocks" in main:
+            line["clocks"] = main["clocks"]
+        if batched:
+            line["batched"] = {n: dict(b) for n, b in batched.items()}
+            line["gpu_launches"] += sum(b["gpu_launches"] for b in batched.values())
         if ws == 1 and not args.no_cpu_baseline:
             try:
                 line["cpu_baseline"] = cpu_sample(cfg)
             except Exception as ex:   # reported, never fatal
                 line["cpu_baseline"] = {"error": str(ex)}
         print(json.dumps(line), flush=True)
-    eng.close()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -438,6 +502,8 @@ def main():
     ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["c2"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", dest="batched", action="store_false",
+                    help="skip the batched sub-object (c4 and c5 on the same GPUs)")
     ap.add_argument("--decode-steps", type=int, default=0,
                     help="override the workload's decode steps (short runs for profiler captures; not a bench number)")
     args = ap.parse_args()

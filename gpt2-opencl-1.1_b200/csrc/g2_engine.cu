@@ -125,6 +125,12 @@ struct g2_engine {
     unsigned long long *d_trace = nullptr;   // phase trace, when G2_MEGA_TRACE names an output file
     std::string trace_path;
     unsigned mega_epoch = 0;
+    // Limit of every device-side wait (G2_WAIT_LIMIT_MS overrides the 2 s default;
+    // tests shorten it to exercise the expiry path quickly).
+    unsigned long long wait_ns = kMegaTimeoutNs;
+    // Test hook (G2_TEST_STALL=acc at open): the next persistent launch gets one
+    // accumulator word that can never turn ready, so its waits expire; one-shot.
+    int test_stall = 0;
     int mega_inflight = 3;   // outstanding bulk copies per CTA (G2_MEGA_INFLIGHT overrides)
     int mega_grid = 0;
     int mega_cw[2] = {0, 0};   // strip widths of c_attn and c_fc
@@ -207,25 +213,32 @@ static int dalloc(g2_engine *e, T **p, size_t count) {
     return G2_OK;
 }
 
-// One projection W [K][N] packed for the persistent decode kernel: unit u
-// (columns u*CW .. u*CW + CW - 1) is (K + 1) rows x CW, rows k < K holding
-// g[k] * W[k][n] and row K holding b[n] + sum_k beta[k] * W[k][n].  With g and
-// beta the preceding LayerNorm's parameters this folds the LayerNorm's affine
-// part into the projection: (norm(x) * g + beta) W + b = norm(x) (diag(g) W) +
+// Element (k, n) of a projection W with K inputs and N outputs, stored either
+// Conv1D [K][N] (lin false) or nn.Linear [N][K] (lin true).
+static inline float w_at(const float *W, int K, int N, bool lin, int k, int n) {
+    return lin ? W[(size_t)n * K + k] : W[(size_t)k * N + n];
+}
+
+// One projection W (K inputs, N outputs) packed for the persistent decode
+// kernel: unit u (columns u*CW .. u*CW + CW - 1) is (K + 2) rows x CW, rows
+// k < K holding g[k] * W[k][n], row K holding b[n] + sum_k beta[k] * W[k][n]
+// and row K + 1 the column sums of the stored rows.  With g and beta the
+// preceding LayerNorm's parameters this folds the LayerNorm's affine part into
+// the projection: (norm(x) * g + beta) W + b = norm(x) (diag(g) W) +
 // (beta W + b).  Without a LayerNorm (g = beta = nullptr) the rows are W and b.
-static void pack_strips(const float *W, const float *b, const float *g, const float *beta, int K, int N, int CW,
-                        float *out) {
+static void pack_strips(const float *W, bool lin, const float *b, const float *g, const float *beta, int K, int N,
+                        int CW, float *out) {
     for (int u = 0; u < N / CW; ++u) {
         float *o = out + (size_t)u * (K + 2) * CW;
         for (int k = 0; k < K; ++k) {
             const float gk = g ? g[k] : 1.0f;
-            for (int cc = 0; cc < CW; ++cc) o[(size_t)k * CW + cc] = gk * W[(size_t)k * N + u * CW + cc];
+            for (int cc = 0; cc < CW; ++cc) o[(size_t)k * CW + cc] = gk * w_at(W, K, N, lin, k, u * CW + cc);
         }
         for (int cc = 0; cc < CW; ++cc) {
             const int n = u * CW + cc;
             double acc = b[n], cs = 0.0;
             if (beta)
-                for (int k = 0; k < K; ++k) acc += (double)beta[k] * (double)W[(size_t)k * N + n];
+                for (int k = 0; k < K; ++k) acc += (double)beta[k] * (double)w_at(W, K, N, lin, k, n);
             if (g)   // sums of the stored (rounded) W' column: x W' - mean * sum_k W'[k] = (x - mean) W'
                 for (int k = 0; k < K; ++k) cs += (double)o[(size_t)k * CW + cc];
             o[(size_t)K * CW + cc] = (float)acc;
@@ -237,32 +250,34 @@ static void pack_strips(const float *W, const float *b, const float *g, const fl
 // Units of one layer for the persistent decode kernel, part q (0: A, 1: B,
 // 2: D; layout in g2_mega.h).  T holds the layer's twelve tensors in file
 // order: ln_1.w/b, c_attn.w/b, attn.c_proj.w/b, ln_2.w/b, c_fc.w/b,
-// mlp.c_proj.w/b (Conv1D [in][out]).  The projection biases of B and D are
+// mlp.c_proj.w/b, the projections as stored in the file (Conv1D [in][out],
+// or nn.Linear [out][in] when lin).  The projection biases of B and D are
 // not packed: the kernel adds them when it reads the accumulators.
-static void pack_mega_layer(const std::vector<float> *T, int E, int F, int NH, int cwq, int cwf, int nq, int q,
-                            std::vector<float> &out) {
+static void pack_mega_layer(const std::vector<float> *T, bool lin, int E, int F, int NH, int cwq, int cwf, int nq,
+                            int q, std::vector<float> &out) {
     if (q == 0) {
         out.resize((size_t)mega_packed_a(E));
-        pack_strips(T[2].data(), T[3].data(), T[0].data(), T[1].data(), E, 3 * E, cwq, out.data());
+        pack_strips(T[2].data(), lin, T[3].data(), T[0].data(), T[1].data(), E, 3 * E, cwq, out.data());
     } else if (q == 1) {
         out.resize((size_t)mega_packed_b(E));
         const int NB = E / nq;
-        const float *W = T[4].data();   // [E][E]
+        const float *W = T[4].data();   // E x E
         float *o = out.data();
         for (int h = 0; h < NH; ++h)
             for (int j = 0; j < nq; ++j)
                 for (int d = 0; d < 64; ++d)
-                    for (int n = 0; n < NB; ++n) *o++ = W[(size_t)(h * 64 + d) * E + j * NB + n];
+                    for (int n = 0; n < NB; ++n) *o++ = w_at(W, E, E, lin, h * 64 + d, j * NB + n);
     } else {
         out.resize((size_t)mega_packed_d(E, F));
         std::vector<float> strips((size_t)(E + 2) * F);
-        pack_strips(T[8].data(), T[9].data(), T[6].data(), T[7].data(), E, F, cwf, strips.data());
-        const float *W2 = T[10].data();   // [F][E]
+        pack_strips(T[8].data(), lin, T[9].data(), T[6].data(), T[7].data(), E, F, cwf, strips.data());
+        const float *W2 = T[10].data();   // F inputs x E outputs
         float *o = out.data();
         for (int u = 0; u < F / cwf; ++u) {
             const float *st = strips.data() + (size_t)u * (E + 2) * cwf;
             o = std::copy(st, st + (size_t)(E + 2) * cwf, o);
-            o = std::copy(W2 + (size_t)u * cwf * E, W2 + (size_t)(u + 1) * cwf * E, o);
+            for (int f = u * cwf; f < (u + 1) * cwf; ++f)
+                for (int n = 0; n < E; ++n) *o++ = w_at(W2, F, E, lin, f, n);
         }
     }
 }
@@ -348,8 +363,19 @@ static int load_weights(g2_engine *e, const std::string &dir) {
     std::vector<std::vector<float>> layer_t(12);
     int layer_have = 0;
 
-    std::vector<float> tmp, tr, pk;
+    std::vector<float> tmp, pk;
     std::vector<uint16_t> hv;
+    // nn.Linear [out][in] projections (and an [E][V] lm_head) are transposed on
+    // the device: the file's values go to this staging buffer, and a transpose
+    // kernel writes them into the weight buffer in the kernels' layout.
+    float *stage = nullptr;
+    size_t stage_n = 0;
+    struct StageFree {
+        float *&p;
+        ~StageFree() {
+            if (p) cudaFree(p);
+        }
+    } stage_free{stage};
     for (auto &it : items) {
         const StTensor *t = sf.find(it.name);
         if (!t) return set_err(G2_ERR_FORMAT, "tensor '%s' not found", it.name.c_str());
@@ -360,6 +386,7 @@ static int load_weights(g2_engine *e, const std::string &dir) {
         rc = sf.read_f32(*t, tmp.data(), err);
         if (rc) return set_err(rc, "%s", err.c_str());
         const float *src = tmp.data();
+        int tr_rows = 0, tr_cols = 0;   // > 0: transpose [tr_rows][tr_cols] on the device
         if (it.kind == 1) {
             // Conv1D [in,out] is kept; nn.Linear [out,in] is transposed (main.c:1252-1300)
             const int in = it.rows, out = it.cols;
@@ -370,19 +397,15 @@ static int load_weights(g2_engine *e, const std::string &dir) {
             } else {
                 if (t->shape[0] != out || t->shape[1] != in)
                     return set_err(G2_ERR_FORMAT, "tensor '%s': expected [%d,%d]", it.name.c_str(), out, in);
-                tr.resize(n);
-                for (int o = 0; o < out; ++o)
-                    for (int i = 0; i < in; ++i) tr[(size_t)i * out + o] = tmp[(size_t)o * in + i];
-                src = tr.data();
+                tr_rows = out;
+                tr_cols = in;
             }
         } else if (it.kind == 2) {
             // lm_head.weight [V,E] is kept; [E,V] is transposed (main.c:1387-1410)
             if (t->shape.size() != 2) return set_err(G2_ERR_FORMAT, "lm_head.weight is not 2-D");
             if (t->shape[0] == E && t->shape[1] == V) {
-                tr.resize(n);
-                for (int k = 0; k < E; ++k)
-                    for (int v = 0; v < V; ++v) tr[(size_t)v * E + k] = tmp[(size_t)k * V + v];
-                src = tr.data();
+                tr_rows = E;
+                tr_cols = V;
             } else if (!(t->shape[0] == V && t->shape[1] == E)) {
                 return set_err(G2_ERR_FORMAT, "lm_head.weight: unexpected shape");
             }
@@ -395,7 +418,7 @@ static int load_weights(g2_engine *e, const std::string &dir) {
                 const int l = atoi(it.name.c_str() + 2);   // "h.<l>.mlp.c_proj.bias"
                 const std::vector<float> *T = layer_t.data();
                 for (int q = 0; q < 3; ++q) {
-                    pack_mega_layer(T, E, F, c.n_head, cw[0], cw[1], e->mega_nq, q, pk);
+                    pack_mega_layer(T, !conv1d, E, F, c.n_head, cw[0], cw[1], e->mega_nq, q, pk);
                     r = cudaMemcpy(e->packed + e->layer_off[(size_t)l * 3 + q], pk.data(), pk.size() * 4,
                                    cudaMemcpyHostToDevice);
                     if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "upload packed layer %d: %s", l, cudaGetErrorString(r));
@@ -404,7 +427,22 @@ static int load_weights(g2_engine *e, const std::string &dir) {
             }
         }
         void *dst = (char *)e->wbuf + *it.off * e->esize;
-        if (e->dtype == G2_F32) {
+        if (tr_rows > 0) {
+            if (n > stage_n) {
+                if (stage) cudaFree(stage);
+                stage = nullptr;
+                r = cudaMalloc(&stage, n * 4);
+                if (r != cudaSuccess) return set_err(G2_ERR_OOM, "cudaMalloc transpose staging: %s", cudaGetErrorString(r));
+                stage_n = n;
+            }
+            r = cudaMemcpy(stage, src, n * 4, cudaMemcpyHostToDevice);
+            if (r == cudaSuccess) {
+                if (e->dtype == G2_F32) launch_transpose<float>(stage, (float *)dst, tr_rows, tr_cols, 0);
+                else launch_transpose<__half>(stage, (__half *)dst, tr_rows, tr_cols, 0);
+                r = cudaGetLastError();
+            }
+            if (r == cudaSuccess) r = cudaDeviceSynchronize();   // the staging buffer is reused by the next tensor
+        } else if (e->dtype == G2_F32) {
             r = cudaMemcpy(dst, src, n * 4, cudaMemcpyHostToDevice);
         } else {
             hv.resize(n);
@@ -493,6 +531,10 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
                   cw[1] && e->mega_nq && E * 4 <= mega_slot_bytes() && E / 4 <= 480 && e->c.n_ctx <= mega_max_keys() &&
                   e->c.n_head * 64 == E && e->c.n_layer <= kMegaMaxLayers;
         e->mega_smem = smem;
+        if (const char *w = getenv("G2_WAIT_LIMIT_MS"))
+            if (atoi(w) > 0) e->wait_ns = (unsigned long long)atoi(w) * 1000000ull;
+        if (const char *t = getenv("G2_TEST_STALL"))
+            if (!strcmp(t, "acc")) e->test_stall = 1;
     }
     TRY(load_weights(e, model_dir));
     const ModelConfig &c = e->c;
@@ -987,10 +1029,18 @@ static int launch_mega(g2_engine *e, int slot, int n_steps) {
     P.err = e->d_err;
     P.trace = e->d_trace;
     P.max_inflight = e->mega_inflight;
+    P.timeout_ns = e->wait_ns;
     // launches of at most kMegaMaxSteps steps, each on zeroed accumulators
     for (int done = 0; done < n_steps;) {
         const int n = std::min(kMegaMaxSteps, n_steps - done);
         CK(cudaMemsetAsync(e->mega_acc, 0, mega_acc_words(n, c.n_layer, c.n_embd) * 8, e->st));
+        if (e->test_stall) {
+            // Word 0 of step 0's layer-0 attention accumulator starts with 128 in its
+            // count field: its NH contributions never bring it to NH, so every CTA's
+            // wait for that vector expires (the kernel then returns G2_ERR_TIMEOUT).
+            CK(cudaMemsetAsync(reinterpret_cast<char *>(e->mega_acc) + 7, 0x40, 1, e->st));
+            e->test_stall = 0;
+        }
         P.n_steps = n;
         P.epoch0 = e->mega_epoch + 1;
         e->mega_epoch += mega_epochs(c.n_layer, n);
@@ -1034,6 +1084,8 @@ static int check_mega_err(g2_engine *e) {
     CK(cudaMemcpy(&code, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code) {
         CK(cudaMemset(e->d_err, 0, sizeof(int)));
+        if (code == kErrClamp)
+            return set_err(G2_ERR_RANGE, "decode kernel: an accumulator contribution exceeded +-2^21 and was clamped");
         return set_err(G2_ERR_TIMEOUT, "decode kernel: a bounded device-side wait expired (site %d)", code);
     }
     return G2_OK;
@@ -1403,6 +1455,8 @@ extern "C" int g2k_matvec(const float *x, const float *W, const float *bias, con
     if (workspace_bytes < g2k_matvec_workspace(N, K)) return set_err(G2_ERR_ARG, "g2k_matvec: workspace too small");
     if ((uintptr_t)workspace % 256) return set_err(G2_ERR_ARG, "g2k_matvec: workspace not 256-byte aligned");
     GemvPlan p = gemv_plan<float>(N, K, current_sms());
+    if (p.smem_bytes > kGemvMaxSmem)
+        return set_err(G2_ERR_RANGE, "g2k_matvec: K = %d is too long for one column tile's shared memory at N = %d", K, N);
     unsigned *ctr = reinterpret_cast<unsigned *>(workspace);
     float *partial = reinterpret_cast<float *>((char *)workspace + align_up((size_t)p.tiles * 4, 256));
     const int epi = (bias ? EPI_BIAS : 0) | (apply_gelu ? EPI_GELU : 0) | (residual ? EPI_RESID : 0);

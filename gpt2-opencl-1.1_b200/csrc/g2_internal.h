@@ -94,7 +94,11 @@ void launch_layernorm(const float *x, float *out, const WT *g, const WT *b, int 
 struct GemvPlan {
     int ksplit;
     int tiles;
+    // dynamic shared memory of one CTA: its x slice plus the column-tile partials
+    // (the launch keeps the default 48 KB limit; entry points refuse larger shapes)
+    size_t smem_bytes;
 };
+constexpr size_t kGemvMaxSmem = 48 * 1024;
 template <typename WT>
 GemvPlan gemv_plan(int N, int K, int sms);
 template <typename WT>
@@ -156,6 +160,12 @@ void launch_argmax_rows(const float *logits, int V, int Vp, int nrows, int forbi
                         cudaStream_t st);
 
 void launch_copy_row(const float *src, float *dst, int n, cudaStream_t st);
+
+// dst[c][r] = src[r][c] for a [rows][cols] fp32 matrix, converted to WT: the
+// load-time transpose of an nn.Linear [out][in] weight into the Conv1D
+// [in][out] layout the kernels read (main.c:1252-1300 does it on the host).
+template <typename WT>
+void launch_transpose(const float *src, WT *dst, int rows, int cols, cudaStream_t st);
 
 // Record `msg` as the calling thread's g2_last_error(); returns `code`.
 int set_error(int code, const char *msg);

@@ -703,11 +703,15 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillAttnArgs a) {
 template <typename KT>
 void launch_prefill_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
                               float *out, int out_stride, cudaStream_t st, OperandOut op) {
-    static const bool attr = [] {   // more than 48 KB of dynamic shared memory: opt in once per type
-        return cudaFuncSetAttribute(prefill_attn_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)kPaSmem) == cudaSuccess;
-    }();
-    (void)attr;
+    // More than 48 KB of dynamic shared memory: the opt-in is a per-device attribute,
+    // so it is made once on every device this process launches on.
+    static unsigned long long attr_set = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !(__atomic_load_n(&attr_set, __ATOMIC_ACQUIRE) >> dev & 1ull)) {
+        cudaFuncSetAttribute(prefill_attn_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPaSmem);
+        if (dev < 64) __atomic_fetch_or(&attr_set, 1ull << dev, __ATOMIC_RELEASE);
+    }
     PrefillAttnArgs a;
     a.qkv = qkv;
     a.qkv_stride = qkv_stride;
@@ -924,6 +928,7 @@ GemvPlan gemv_plan(int N, int K, int sms) {
         if (p.tiles * d <= target) best = d;
     }
     p.ksplit = best;
+    p.smem_bytes = (size_t)(K / p.ksplit + 16 * BN) * sizeof(float);
     return p;
 }
 
@@ -951,9 +956,8 @@ void launch_gemv(const float *x, const WT *W, const WT *bias, const float *resid
     a.e.pos = pos_ptr;
     a.e.slot = slot_ptr;
     a.e.E = N / 3;
-    const size_t smem = (size_t)(K / plan.ksplit + 16 * BN) * sizeof(float);
     dim3 grid(plan.tiles, plan.ksplit);
-    launch_pdl(gemv_kernel<WT>, grid, dim3(256), smem, st, a);
+    launch_pdl(gemv_kernel<WT>, grid, dim3(256), plan.smem_bytes, st, a);
 }
 
 template <typename WT>
@@ -1094,6 +1098,30 @@ void launch_copy_row(const float *src, float *dst, int n, cudaStream_t st) {
 }
 void launch_step_advance(int *step_ptr, cudaStream_t st) { launch_pdl(step_advance_kernel, dim3(1), dim3(1), 0, st, step_ptr); }
 
+// 32 x 32 tiles through shared memory (one padding column against bank
+// conflicts): both the reads of src rows and the writes of dst rows are
+// coalesced.  Block (32, 8); each thread moves four elements.
+template <typename WT>
+__global__ void transpose_kernel(const float *__restrict__ src, WT *__restrict__ dst, int rows, int cols) {
+    __shared__ float tile[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[i][threadIdx.x] = src[(size_t)r * cols + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        const int c = c0 + i, r = r0 + threadIdx.x;   // dst row c, column r
+        if (r < rows && c < cols) dst[(size_t)c * rows + r] = fromf<WT>(tile[threadIdx.x][i]);
+    }
+}
+
+template <typename WT>
+void launch_transpose(const float *src, WT *dst, int rows, int cols, cudaStream_t st) {
+    dim3 grid((cols + 31) / 32, (rows + 31) / 32);
+    transpose_kernel<WT><<<grid, dim3(32, 8), 0, st>>>(src, dst, rows, cols);
+}
+
 // explicit instantiations
 #define G2_INST(WT)                                                                                                   \
     template void launch_embed<WT>(const WT *, const WT *, Rows, float *, int, int, int, int, cudaStream_t);         \
@@ -1111,7 +1139,8 @@ void launch_step_advance(int *step_ptr, cudaStream_t st) { launch_pdl(step_advan
                                        unsigned *, int, cudaStream_t, OperandOut, QkvPartials);                       \
     template void launch_lm_head<WT>(const float *, const WT *, const WT *, const WT *, float *, int, int, int, int, \
                                      float *, unsigned *, int *, StepState *, int *, cudaStream_t);                  \
-    template void launch_lm_head_rows<WT>(const float *, const WT *, float *, int, int, int, int, cudaStream_t);
+    template void launch_lm_head_rows<WT>(const float *, const WT *, float *, int, int, int, int, cudaStream_t);  \
+    template void launch_transpose<WT>(const float *, WT *, int, int, cudaStream_t);
 G2_INST(float)
 G2_INST(__half)
 

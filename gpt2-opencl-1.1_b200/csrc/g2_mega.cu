@@ -46,10 +46,13 @@
 //    partials and derives the next token.  The K/V rows a step appends are
 //    read by later steps only; one fence pair per step at that exchange
 //    orders them.
-//  * Every wait is bounded (globaltimer, 2 s per wait).  On expiry the thread
+//  * Every wait is bounded (globaltimer, MegaParams::timeout_ns per wait, 2 s
+//    unless the engine was opened with a shorter limit).  On expiry the thread
 //    records an error code; the consumer warps leave together at the next
 //    uniform check, the producer stops issuing and drains its in-flight
-//    copies, and the host reports G2_ERR_TIMEOUT.
+//    copies, and the host reports G2_ERR_TIMEOUT.  A contribution clamped at
+//    +-2^21 is recorded the same way (kErrClamp) and reported as
+//    G2_ERR_RANGE.
 #include <cfloat>
 #include <climits>
 #include <cstdint>
@@ -65,7 +68,6 @@ constexpr int kCons = kWarps * 32;         // consumer threads
 constexpr int kThreads = kCons + 32;       // + producer warp
 constexpr int kSlots = 8;
 constexpr int kSlotBytes = 24832;          // 194 * 128: whole rows at every strip width (16 to 128 B)
-constexpr unsigned long long kTimeoutNs = 2000000000ull;
 constexpr int kConsBar = 1;                // named barrier of the consumer warps
 constexpr int kMaxKeys = 1024;             // attention keys (positions) per head
 constexpr int kKeysPerPass = kCons / 4;    // 4 threads per key in the score pass
@@ -118,7 +120,10 @@ __device__ __forceinline__ bool tag_is(u64 w, unsigned ep) { return (unsigned)(w
 __device__ __forceinline__ float tag_val(u64 w) { return __uint_as_float((unsigned)w); }
 
 // Accumulator words: count * 2^55 + sum of round(v * 2^32), modulo 2^64.
-__device__ __forceinline__ void acc_add(u64 *dst, float v) {
+// A contribution beyond +-2^21 is clamped and recorded in *err (kErrClamp),
+// so that a lost range is reported rather than silent.
+__device__ __forceinline__ void acc_add(u64 *dst, float v, int *err) {
+    if (!(fabsf(v) <= kAccMax)) atomicCAS(err, 0, kErrClamp);
     v = fminf(fmaxf(v, -kAccMax), kAccMax);
     const long long q = __float2ll_rn(v * 4294967296.0f);   // exact scaling by 2^32, one rounding
     const u64 c = kAccOne + (u64)q;
@@ -157,10 +162,10 @@ __device__ __forceinline__ bool mbar_try(u64 *b, unsigned parity) {
         : "memory");
     return ok != 0;
 }
-// Wait for the phase of parity `parity` to complete, for at most kTimeoutNs.
-__device__ __forceinline__ bool mbar_wait(u64 *b, unsigned parity) {
+// Wait for the phase of parity `parity` to complete, for at most ns.
+__device__ __forceinline__ bool mbar_wait(u64 *b, unsigned parity, u64 ns) {
     if (mbar_try(b, parity)) return true;
-    const u64 limit = gtime() + kTimeoutNs;
+    const u64 limit = gtime() + ns;
     for (;;) {
         if (mbar_try(b, parity)) return true;
         if (gtime() > limit) return false;
@@ -168,9 +173,9 @@ __device__ __forceinline__ bool mbar_wait(u64 *b, unsigned parity) {
 }
 // The producer's wait: the same, sleeping between tries so that the waiting
 // warp leaves its scheduler's issue slots to the consumer warps.
-__device__ __forceinline__ bool mbar_wait_idle(u64 *b, unsigned parity) {
+__device__ __forceinline__ bool mbar_wait_idle(u64 *b, unsigned parity, u64 ns) {
     if (mbar_try(b, parity)) return true;
-    const u64 limit = gtime() + kTimeoutNs;
+    const u64 limit = gtime() + ns;
     for (;;) {
         __nanosleep(64);
         if (mbar_try(b, parity)) return true;
@@ -305,7 +310,7 @@ __device__ __forceinline__ void fail(Cx &cx, int code) {
 // end, which also carries the failure flag.  The deadline is checked every 64
 // rounds.
 __device__ __forceinline__ bool poll_vec(Cx &cx, const u64 *src, float *dst, int n, unsigned ep, int code) {
-    const u64 limit = gtime() + kTimeoutNs;
+    const u64 limit = gtime() + cx.p->timeout_ns;
     // bit j of `pending`: word ctid + j * kCons not yet seen with the right epoch (n <= 32 * kCons)
     unsigned pending = 0;
     if (!cx.failed)
@@ -336,7 +341,7 @@ __device__ __forceinline__ bool poll_vec(Cx &cx, const u64 *src, float *dst, int
 // barrier at the end, as in poll_vec.  All consumer threads.
 __device__ __forceinline__ bool poll_acc(Cx &cx, const u64 *src, int ncopy, int nunits, const float *bias, int E,
                                          int code) {
-    const u64 limit = gtime() + kTimeoutNs;
+    const u64 limit = gtime() + cx.p->timeout_ns;
     unsigned pending = 0;
     float bv[kMaxJ];
 #pragma unroll
@@ -425,7 +430,7 @@ __device__ __forceinline__ void ln_stats(Cx &cx, int n, float &mean, float &rstd
 // phase's uniform check discards the result.
 __device__ __forceinline__ const float4 *chunk_wait(Cx &cx, unsigned k = 0) {
     const unsigned i = cx.chunk_i + k, slot = i % kSlots, par = (i / kSlots) & 1u;
-    if (!mbar_wait(&cx.s.full[slot], par)) fail(cx, 4);
+    if (!mbar_wait(&cx.s.full[slot], par, cx.p->timeout_ns)) fail(cx, 4);
     return reinterpret_cast<const float4 *>(cx.s.ring + (size_t)slot * kSlotBytes);
 }
 // Release the next n chunks to the producer (each consumer warp arrives once).
@@ -583,7 +588,7 @@ __device__ __forceinline__ void block_unit(Cx &cx, const float *a, int rows, int
     for (int n = t; n < NB; n += kCons) {
         float y = part[n];
         for (int g = 1; g < RG; ++g) y += part[g * NB + n];
-        acc_add(dst + n, y);
+        acc_add(dst + n, y, cx.p->err);
     }
 }
 
@@ -607,14 +612,14 @@ __device__ __forceinline__ bool produce(Cx &cx, const char *src, size_t bytes, s
     for (size_t off = 0; off < bytes; off += chunk) {
         const unsigned nb = (unsigned)(bytes - off < chunk ? bytes - off : chunk);
         const unsigned slot = i % kSlots;
-        if (!mbar_wait_idle(&cx.s.empty[slot], ((i / kSlots) & 1u) ^ 1u)) {
+        if (!mbar_wait_idle(&cx.s.empty[slot], ((i / kSlots) & 1u) ^ 1u, p.timeout_ns)) {
             fail(cx, 1);
             return false;
         }
         // Keep at most max_inflight copies outstanding.
         if (i >= (unsigned)p.max_inflight) {
             const unsigned j = i - p.max_inflight;
-            if (!mbar_wait_idle(&cx.s.full[j % kSlots], (j / kSlots) & 1u)) {
+            if (!mbar_wait_idle(&cx.s.full[j % kSlots], (j / kSlots) & 1u, p.timeout_ns)) {
                 fail(cx, 1);
                 return false;
             }
@@ -657,7 +662,8 @@ __device__ __forceinline__ void producer(Cx &cx, const Sched &S) {
         }
     }
     // Every copy issued must land before the CTA may exit (the ring is its destination).
-    for (unsigned j = i > kSlots ? i - kSlots : 0; j < i; ++j) mbar_wait(&cx.s.full[j % kSlots], (j / kSlots) & 1u);
+    for (unsigned j = i > kSlots ? i - kSlots : 0; j < i; ++j)
+        mbar_wait(&cx.s.full[j % kSlots], (j / kSlots) & 1u, p.timeout_ns);
 }
 
 // ---- consumer units --------------------------------------------------------------------
@@ -685,7 +691,7 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
         for (int t = 0; t < 4; ++t) kr[t] = c ? K4[(size_t)key * 16 + k4 * 4 + t] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     {   // q, k, v of head h at pos
-        const u64 limit = gtime() + kTimeoutNs;
+        const u64 limit = gtime() + cx.p->timeout_ns;
         bool pend = cx.ctid < 192 && !cx.failed;
         for (unsigned round = 0; __any_sync(0xffffffffu, pend); ++round) {
             if ((round & 63u) == 63u && __any_sync(0xffffffffu, gtime() > limit)) {

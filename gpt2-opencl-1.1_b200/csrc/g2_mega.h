@@ -29,12 +29,17 @@ struct MegaParams {
     int *out_tokens;                        // this slot's token row
     int *result;                            // [0] last token, [1] its logit bits
     StepState *state;                       // token / pos / step / min_new in and out
-    int *err;                               // 0, or the code of the first expired wait
+    int *err;                               // 0, or the code of the first expired wait (or kErrClamp)
+    unsigned long long timeout_ns;          // limit of every device-side wait
     unsigned epoch0;
     int max_inflight;   // bulk copies a CTA keeps outstanding (1..8); the ring holds 8 slots regardless
     // Optional phase trace (nullptr = off): per CTA kTraceSlots words, see g2_mega.cu.
     unsigned long long *trace;
 };
+
+// MegaParams::err code of a clamped accumulator contribution (wait sites use 1..6).
+constexpr int kErrClamp = 16;
+constexpr unsigned long long kMegaTimeoutNs = 2000000000ull;   // default wait limit: 2 s
 
 constexpr int kTraceSlots = 160;
 // Trace words per CTA: [0..8) ns spent waiting for inputs: [1] B (q, k, v), [2] x after

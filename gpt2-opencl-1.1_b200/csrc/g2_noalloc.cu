@@ -14,7 +14,10 @@
 // exits.  Host code cannot use the array's name as a device address, so the
 // first call on each device, with that device current, looks the address up
 // with cudaGetSymbolAddress and caches it; make that first call on a device
-// before any stream capture.  All calls share the array: each call clears the
+// before any stream capture.  The cached address belongs to the device's
+// current context: after cudaDeviceReset on a device the library's module is
+// loaded afresh at another address, so do not call this entry point again on
+// that device in the same process.  All calls share the array: each call clears the
 // split-K counters (cudaMemsetAsync, no allocation) before its kernel, and
 // calls that overlap on the GPU (concurrent streams, or several host
 // threads) race on the array and must be serialised by the caller.
@@ -55,6 +58,13 @@ extern "C" int g2k_matvec_noalloc(const float *x, const float *W, const float *b
     if (need > kNoallocScratchBytes)
         return g2::set_error(G2_ERR_RANGE, "g2k_matvec_noalloc: this N x K needs more than the 256 KiB of fixed "
                                            "scratch; use g2k_matvec with a caller-provided workspace");
+    if (p.smem_bytes > g2::kGemvMaxSmem)
+        return g2::set_error(G2_ERR_RANGE, "g2k_matvec_noalloc: K is too long for one column tile's shared memory "
+                                           "at this N");
+    // An error left pending by earlier work of the caller is reported as such,
+    // not as this call's launch failure.
+    if (cudaPeekAtLastError() != cudaSuccess)
+        return g2::set_error(G2_ERR_CUDA, "g2k_matvec_noalloc: a CUDA error was already pending before this call");
     void *base;
     {
         std::lock_guard<std::mutex> lk(g_mu);

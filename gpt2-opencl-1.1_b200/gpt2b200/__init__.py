@@ -1,9 +1,11 @@
 """Python binding of the B200 GPT-2 engine's C ABI (include/gpt2b200.h).
 
 A thin ctypes layer over ``libgpt2b200.so`` (built in-tree by the package
-Makefile / ``__graft_entry__.build()``).  There is no fallback: importing
-raises if the library is missing, and every call raises ``G2Error`` on a
-non-zero status.
+Makefile / ``__graft_entry__.build()``).  The library is mapped on the first
+call into it (or by ``load()``), so that importing the package's pure-Python
+helpers (``synth``, ``replicas``) maps no engine code.  There is no fallback:
+that first call raises ``ImportError`` if the library is missing, and every
+call raises ``G2Error`` on a non-zero status.
 """
 from __future__ import annotations
 
@@ -77,7 +79,25 @@ def _load():
     return L
 
 
-lib = _load()
+class _Lib:
+    """The engine library, mapped on first attribute access."""
+
+    def __init__(self):
+        self._L = None
+
+    def __getattr__(self, name):
+        if self._L is None:
+            self._L = _load()
+        return getattr(self._L, name)
+
+
+lib = _Lib()
+
+
+def load():
+    """Map libgpt2b200.so now (raises ImportError if it is missing)."""
+    lib.g2_last_error
+    return lib._L
 
 
 def check(rc: int) -> int:

@@ -10,7 +10,11 @@ Conv1D ``[in, out]`` layout (``main.c:1234-1250``), and no
 Weights are N(0, 0.02) for ``wte``, ``wpe`` and every projection; LayerNorm
 gamma = 1, beta = 0; biases 0.  ``affine=True`` draws LN and bias values too,
 so tests exercise the bias and LN arithmetic.  ``dtype="f16"`` stores every
-tensor as IEEE half (the engine's fp16 path; the reference only loads F32).
+tensor as IEEE half (the engine's fp16 path; the reference only loads F32);
+``dtype="bf16"`` stores bfloat16 (the fp32 values rounded to nearest even).
+``outliers=True`` adds a few large residual-stream columns, as real GPT-2
+checkpoints have: a large constant in two ``wpe`` columns and those columns
+of every ``mlp.c_proj.weight`` scaled up, so the stream reaches ~10^3 there.
 
 The stream of random numbers is fixed by ``seed`` and the tensor order
 below, so the same directory is produced on every machine with this numpy.
@@ -20,6 +24,7 @@ from __future__ import annotations
 import json
 import os
 import struct
+import tempfile
 from dataclasses import dataclass, asdict
 
 import numpy as np
@@ -50,7 +55,26 @@ XL = GPT2Shape(n_layer=48, n_embd=1600, n_head=25)
 # A two-layer model with the full vocabulary (EOS id 50256 exists) for fast tests.
 TINY = GPT2Shape(n_layer=2, n_embd=128, n_head=2, n_ctx=1024, vocab_size=50257)
 
-_DT = {"f32": ("F32", np.float32), "f16": ("F16", np.float16)}
+_DT = {"f32": ("F32", np.float32), "f16": ("F16", np.float16), "bf16": ("BF16", None)}
+OUTLIER_COLS = (5, 77)   # residual-stream columns made large by outliers=True
+
+
+def default_cache() -> str:
+    """Directory for generated synthetic checkpoints: $G2_MODEL_CACHE, else one
+    under the system's temporary directory."""
+    return os.environ.get("G2_MODEL_CACHE", os.path.join(tempfile.gettempdir(), "g2_models"))
+
+
+def to_bf16(a: np.ndarray) -> np.ndarray:
+    """float32 -> bfloat16 bits (uint16), rounded to nearest even (finite inputs)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return u.astype(np.uint16)
+
+
+def from_bf16(b: np.ndarray) -> np.ndarray:
+    """bfloat16 bits (uint16) -> float32."""
+    return (b.astype(np.uint32) << 16).view(np.float32)
 
 
 def tensor_plan(s: GPT2Shape):
@@ -85,7 +109,7 @@ def write_safetensors(path: str, tensors):
     """Write (name, np.ndarray) pairs as a safetensors file (8-byte LE header length + JSON + data)."""
     header, off = {}, 0
     for name, arr in tensors:
-        tag = {np.dtype(np.float32): "F32", np.dtype(np.float16): "F16"}[arr.dtype]
+        tag = {np.dtype(np.float32): "F32", np.dtype(np.float16): "F16", np.dtype(np.uint16): "BF16"}[arr.dtype]
         n = arr.nbytes
         header[name] = {"dtype": tag, "shape": list(arr.shape), "data_offsets": [off, off + n]}
         off += n
@@ -108,42 +132,66 @@ def write_config(d: str, s: GPT2Shape):
         json.dump(cfg, f, indent=1)
 
 
+def _outliers(name: str, a: np.ndarray) -> np.ndarray:
+    """The outlier columns: +500 in wpe (every position), x40 in mlp.c_proj's output columns."""
+    if name == "wpe.weight":
+        a = a.copy()
+        a[:, list(OUTLIER_COLS)] += np.float32(500.0)
+    elif name.endswith("mlp.c_proj.weight"):
+        a = a.copy()
+        a[:, list(OUTLIER_COLS)] *= np.float32(40.0)
+    return a
+
+
 def make_model(d: str, s: GPT2Shape, seed: int = 0, dtype: str = "f32", affine: bool = False,
-               layout: str = "conv1d") -> str:
+               layout: str = "conv1d", outliers: bool = False, round_to: str = None) -> str:
     """Create ``d`` with config.json and model.safetensors; return ``d``.
 
     ``layout="linear"`` stores projections as ``[out, in]`` (nn.Linear), which
     the loader must detect and transpose (``main.c:1252-1300``).
+    ``round_to="bf16"`` stores the bf16-rounded values in the file's dtype (the
+    F32 twin of a bf16 file).
     """
     os.makedirs(d, exist_ok=True)
     rng = np.random.default_rng(seed)
-    np_dt = _DT[dtype][1]
     out = []
     for name, shape, kind in tensor_plan(s):
         a = _draw(rng, shape, kind, affine)
+        if outliers:
+            a = _outliers(name, a)
+        if round_to == "bf16":
+            a = from_bf16(to_bf16(a))
         if layout == "linear" and a.ndim == 2 and name.startswith("h."):
             a = np.ascontiguousarray(a.T)
-        out.append((name, a.astype(np_dt)))
+        out.append((name, to_bf16(a) if dtype == "bf16" else a.astype(_DT[dtype][1])))
     write_safetensors(os.path.join(d, "model.safetensors"), out)
     write_config(d, s)
     with open(os.path.join(d, "synth.json"), "w") as f:
-        json.dump({"shape": asdict(s), "seed": seed, "dtype": dtype, "affine": affine,
-                   "layout": layout}, f)
+        json.dump(_tag(s, seed, dtype, affine, layout, outliers, round_to), f)
     return d
 
 
+def _tag(s, seed, dtype, affine, layout, outliers, round_to):
+    t = {"shape": asdict(s), "seed": seed, "dtype": dtype, "affine": affine, "layout": layout}
+    if outliers:
+        t["outliers"] = True
+    if round_to:
+        t["round_to"] = round_to
+    return t
+
+
 def ensure_model(d: str, s: GPT2Shape, seed: int = 0, dtype: str = "f32", affine: bool = False,
-                 layout: str = "conv1d") -> str:
+                 layout: str = "conv1d", outliers: bool = False, round_to: str = None) -> str:
     """make_model unless ``d`` already holds the same synthetic model."""
     tag = os.path.join(d, "synth.json")
-    want = {"shape": asdict(s), "seed": seed, "dtype": dtype, "affine": affine, "layout": layout}
+    want = _tag(s, seed, dtype, affine, layout, outliers, round_to)
     try:
         with open(tag) as f:
             if json.load(f) == want and os.path.exists(os.path.join(d, "model.safetensors")):
                 return d
     except (OSError, ValueError):
         pass
-    return make_model(d, s, seed, dtype, affine, layout)
+    return make_model(d, s, seed, dtype, affine, layout, outliers, round_to)
 
 
 def prompt_ids(seed: int, n: int, vocab: int = 50257) -> np.ndarray:

@@ -148,7 +148,9 @@ size_t g2k_matvec_workspace(int N, int K);
  * y[n] = sum_k x'[k] * W[k*N + n] (+bias[n]) (+residual[n]) (then GELU),
  * where x' = LayerNorm(x; ln_gamma, ln_beta, eps 1e-5) when ln_gamma is not
  * NULL (the decode layernorm, main.c:1620, fused in), else x.  residual may
- * alias y.  N % 4 == 0, K % 16 == 0.  `workspace` must hold
+ * alias y.  N % 4 == 0, K % 16 == 0; a K slice that would not fit one
+ * CTA's 48 KB of shared memory (very wide N with K over ~11,000) gives
+ * G2_ERR_RANGE.  `workspace` must hold
  * g2k_matvec_workspace(N, K) bytes, 256-byte aligned, and be zero-filled
  * before its first use; the call leaves it ready for the next one. */
 int g2k_matvec(const float *x, const float *W, const float *bias, const float *residual, float *y,
@@ -163,8 +165,10 @@ int g2k_matvec(const float *x, const float *W, const float *bias, const float *r
  * array inside this library (held on every GPU that loads it until exit);
  * shapes whose split-K scratch would exceed it return G2_ERR_RANGE.  The
  * first call on a device looks the array up (make it before any stream
- * capture); every call clears the array's counters before its kernel; calls
- * that overlap on the GPU share the array and race, so serialise them.
+ * capture); that address does not survive cudaDeviceReset, so make no call
+ * on a device after resetting it in the same process.  Every call clears the
+ * array's counters before its kernel; calls that overlap on the GPU share
+ * the array and race, so serialise them.
  * Same arguments and results as g2k_matvec otherwise. */
 int g2k_matvec_noalloc(const float *x, const float *W, const float *bias, const float *residual, float *y,
                        int N, int K, int apply_gelu, const float *ln_gamma, const float *ln_beta, void *stream);

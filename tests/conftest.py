@@ -10,7 +10,9 @@ for p in (PKG, os.path.join(ROOT, "oracle")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-MODEL_CACHE = os.environ.get("G2_MODEL_CACHE", os.path.join(ROOT, "_work", "models"))
+from gpt2b200 import synth as _synth  # noqa: E402
+
+MODEL_CACHE = _synth.default_cache()
 
 
 def pytest_configure(config):

@@ -9,11 +9,16 @@ g2k_matvec_noalloc uses a fixed scratch array inside the library instead.
 These tests call it through the C ABI and require its output to equal
 g2k_matvec's (same kernel and split-K plan, so within the kernel tests'
 tolerance and in practice bit for bit), on two calls in a row, since every
-call reuses the scratch the previous call left behind.  The file is named
-to be collected last; it passes alone in a fresh process and after the rest.
+call reuses the scratch the previous call left behind.  One shape is also
+checked directly against the oracle's launch_matvec_splitk restatement
+(main.c:1578, math.cl:229-270), so the entry point is pinned on its own.
+The file is named to be collected last; it passes alone in a fresh process
+and after the rest.
 """
 import numpy as np
 import pytest
+
+import oracle
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -72,3 +77,41 @@ def test_noalloc_rejects_oversized_scratch(g2):
     with pytest.raises(g2.G2Error) as ei:
         g2.matvec_noalloc(x, x, y, N, K)
     assert ei.value.code == -6 and "256 KiB" in str(ei.value)
+
+
+def test_noalloc_matches_oracle(g2):
+    """attn_proj's shape (768 x 768, split-K 8 in the reference) with bias and an
+    in-place residual, against the oracle's split-K matvec + reduce_partial."""
+    N, K, ks = 768, 768, 8
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal(K).astype(np.float32) * 2
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    bias = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    res = rng.standard_normal(N).astype(np.float32)
+    want = res.copy()
+    scratch = np.zeros(ks * N, np.float32)
+    fp = oracle.fptr
+    oracle.cpu_lib().ref_launch_matvec_splitk(fp(x), fp(W), fp(bias), fp(res), fp(want), N, K, ks, 0, fp(scratch))
+    dx, dW, db = (torch.from_numpy(a).cuda() for a in (x, W, bias))
+    for call in range(2):
+        y = torch.from_numpy(res).cuda()
+        g2.matvec_noalloc(dx, dW, y, N, K, bias=db, residual=y)
+        torch.cuda.synchronize()
+        close(y.cpu().numpy(), want)
+
+
+def test_noalloc_rejects_oversized_shared_memory(g2):
+    """A very wide N with a long K: the split-K scratch fits the fixed array, but one
+    column tile's K slice would not fit a CTA's 48 KB of shared memory.  The call is
+    refused with G2_ERR_RANGE before any launch (the buffers are full-size all the
+    same, so no read could leave them)."""
+    N, K = 40000, 12288
+    assert g2.matvec_workspace(N, K) <= 256 * 1024
+    x = torch.zeros(K, device="cuda")
+    W = torch.zeros(K * N, device="cuda")
+    y = torch.zeros(N, device="cuda")
+    with pytest.raises(g2.G2Error) as ei:
+        g2.matvec_noalloc(x, W, y, N, K)
+    assert ei.value.code == -6 and "shared memory" in str(ei.value)
+    del W
+    torch.cuda.empty_cache()
