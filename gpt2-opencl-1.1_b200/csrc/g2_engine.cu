@@ -119,7 +119,8 @@ struct g2_engine {
     std::vector<long long> layer_off;   // [L][3] float offsets into packed (A, B, D units)
     long long *d_layer_off = nullptr;
     LayerPtrs *d_layers = nullptr;
-    unsigned long long *t_qkv = nullptr, *t_best = nullptr;
+    unsigned long long *t_qkv = nullptr, *t_best = nullptr, *t_att = nullptr;
+    int mega_split_t = 320;   // positions past which a head's keys are split over its units (G2_MEGA_SPLIT_T)
     unsigned long long *mega_acc = nullptr;   // mega_acc_words(kMegaMaxSteps, L, E) accumulator words
     int *d_err = nullptr;
     unsigned long long *d_trace = nullptr;   // phase trace, when G2_MEGA_TRACE names an output file
@@ -140,7 +141,6 @@ struct g2_engine {
     // tensor-core GEMMs of the many-row passes (prefill, batched decode)
     bool tc = false;
     int tc_kind = TC_TF32X3;
-    float *tc_w = nullptr;                    // fp32 engine: tf32 hi / lo copies of the projections
     float *tc_xhi = nullptr, *tc_xlo = nullptr;     // GEMM input rows with K = E: hi / lo (fp32) or fp16 (in tc_xhi)
     float *tc_x2hi = nullptr, *tc_x2lo = nullptr;   // fc2's input rows (K = F), written by the fc GEMM
     unsigned *tc_ctr = nullptr;                    // split-K tile counters
@@ -153,7 +153,6 @@ struct g2_engine {
     int *h_ctx = nullptr;           // pinned staging of the context ids
     std::vector<TcWeights> tc_maps;           // [L][4]: qkv, proj, fc, fc2
     TcWeights tc_lm{};                        // the tied LM head: wte [V][E] as a K-major operand
-    float *tc_lm_w = nullptr;                 // fp32 engine: tf32 hi / lo copies of wte
     TcRowsOperand tc_x_e{}, tc_x_f{};         // input rows with K = E (tc_x*) and K = F (tc_x2*)
 
     template <typename WT>
@@ -183,8 +182,8 @@ static void free_engine(g2_engine *e) {
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
     for (auto &kv : e->prefill_graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_lm_w, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
-                        e->t_best, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
+    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
+                        e->t_best, e->t_att, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
                         e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
                         e->argmax_out, e->batch_step, e->out_tokens, e->state};
@@ -531,6 +530,8 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
                   cw[1] && e->mega_nq && E * 4 <= mega_slot_bytes() && E / 4 <= 480 && e->c.n_ctx <= mega_max_keys() &&
                   e->c.n_head * 64 == E && e->c.n_layer <= kMegaMaxLayers;
         e->mega_smem = smem;
+        if (const char *st = getenv("G2_MEGA_SPLIT_T"))
+            if (atoi(st) >= 64) e->mega_split_t = atoi(st);   // >= 64: every slice then has keys
         if (const char *w = getenv("G2_WAIT_LIMIT_MS"))
             if (atoi(w) > 0) e->wait_ns = (unsigned long long)atoi(w) * 1000000ull;
         if (const char *t = getenv("G2_TEST_STALL"))
@@ -619,6 +620,7 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
         TRY(dalloc(e, &e->t_qkv, (size_t)3 * E));
         TRY(dalloc(e, &e->mega_acc, mega_acc_words(kMegaMaxSteps, c.n_layer, E)));
         TRY(dalloc(e, &e->t_best, (size_t)4 * e->sms));
+        TRY(dalloc(e, &e->t_att, (size_t)c.n_head * e->mega_nq * 66));
         TRY(dalloc(e, &e->d_err, 1));
         TRY(dalloc(e, &e->d_layer_off, e->layer_off.size()));
         TRY(dalloc(e, &e->d_layers, (size_t)c.n_layer));
@@ -667,42 +669,24 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
         if (e->tc) {
             e->tc_kind = dtype == G2_F32 ? TC_TF32X3 : TC_F16;
             const int Ks[4] = {E, E, E, F}, Ns[4] = {3 * E, E, F, E};
-            size_t per_layer = 0;
-            for (int q = 0; q < 4; ++q) per_layer += align_up((size_t)Ks[q] * Ns[q], 64);
-            if (e->tc_kind == TC_TF32X3) TRY(dalloc(e, &e->tc_w, 2 * per_layer * c.n_layer));
+            // The GEMMs read the engine's weights in place: fp16 as they are, fp32
+            // split into tf32 hi / lo tile by tile inside the kernel.
             e->tc_maps.resize((size_t)c.n_layer * 4);
-            size_t o = 0;
             for (int l = 0; l < c.n_layer; ++l) {
                 const LayerOff &lo = e->L[l];
                 const size_t wo[4] = {lo.qkv_w, lo.proj_w, lo.fc_w, lo.fc2_w};
                 for (int q = 0; q < 4; ++q) {
-                    const size_t n = (size_t)Ks[q] * Ns[q];
-                    int rc;
-                    if (e->tc_kind == TC_TF32X3) {
-                        float *hi = e->tc_w + o, *lo_ = e->tc_w + per_layer * c.n_layer + o;
-                        launch_tc_prep(TC_TF32X3, e->w<float>(wo[q]), hi, lo_, nullptr, (long long)n, e->st);
-                        rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_TF32X3, hi, lo_, Ks[q], Ns[q]);
-                    } else {
-                        rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_F16, e->w<__half>(wo[q]), nullptr, Ks[q], Ns[q]);
-                    }
+                    const void *W = e->tc_kind == TC_TF32X3 ? (const void *)e->w<float>(wo[q]) : (const void *)e->w<__half>(wo[q]);
+                    const int rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], e->tc_kind, W, Ks[q], Ns[q]);
                     if (rc) {
                         free_engine(e);
                         return set_err(rc, "tensor map of layer %d projection %d", l, q);
                     }
-                    o += align_up(n, 64);
                 }
             }
             {
-                const size_t n = (size_t)c.vocab_size * E;
-                int rc;
-                if (e->tc_kind == TC_TF32X3) {
-                    TRY(dalloc(e, &e->tc_lm_w, 2 * align_up(n, 64)));
-                    float *hi = e->tc_lm_w, *lo_ = e->tc_lm_w + align_up(n, 64);
-                    launch_tc_prep(TC_TF32X3, e->w<float>(e->lm), hi, lo_, nullptr, (long long)n, e->st);
-                    rc = tc_weights_kmajor(&e->tc_lm, TC_TF32X3, hi, lo_, E, c.vocab_size);
-                } else {
-                    rc = tc_weights_kmajor(&e->tc_lm, TC_F16, e->w<__half>(e->lm), nullptr, E, c.vocab_size);
-                }
+                const void *W = e->tc_kind == TC_TF32X3 ? (const void *)e->w<float>(e->lm) : (const void *)e->w<__half>(e->lm);
+                int rc = tc_weights_kmajor(&e->tc_lm, e->tc_kind, W, E, c.vocab_size);
                 if (rc) {
                     free_engine(e);
                     return set_err(rc, "tensor map of the LM head");
@@ -994,6 +978,7 @@ static int launch_mega(g2_engine *e, int slot, int n_steps) {
     if (e->mega_epoch > 0xF0000000u) {   // epochs are 32-bit: restart them on cleared buffers
         CK(cudaMemsetAsync(e->t_qkv, 0, (size_t)3 * c.n_embd * 8, e->st));
         CK(cudaMemsetAsync(e->t_best, 0, (size_t)4 * e->sms * 8, e->st));
+        CK(cudaMemsetAsync(e->t_att, 0, (size_t)c.n_head * e->mega_nq * 66 * 8, e->st));
         e->mega_epoch = 0;
     }
     MegaParams P;
@@ -1022,6 +1007,8 @@ static int launch_mega(g2_engine *e, int slot, int n_steps) {
     P.t_qkv = e->t_qkv;
     P.acc = e->mega_acc;
     P.t_best = e->t_best;
+    P.t_att = e->t_att;
+    P.split_t = e->mega_split_t;
     P.logits = e->logits + (size_t)slot * c.padded_vocab;
     P.out_tokens = e->out_tokens + (size_t)slot * c.n_ctx;
     P.result = e->result;
@@ -1477,13 +1464,13 @@ extern "C" int g2k_matmul(const float *A, const float *B, const float *bias, con
     return G2_OK;
 }
 
-// Workspace of g2k_matmul_tc: [err + tile counters | A hi | A lo | B hi | B lo | partial sums],
-// 256-byte aligned parts.
+// Workspace of g2k_matmul_tc: [err + tile counters | A hi | A lo | B fp16 (G2_F16 only) | (unused) |
+// partial sums], 256-byte aligned parts.
 static size_t tc_ws_layout(int M, int N, int K, int precision, int sms, size_t off[6]) {
     const int kind = precision == G2_F16 ? TC_F16 : TC_TF32X3;
     const size_t es = kind == TC_F16 ? 2 : 4;
     const size_t sz[6] = {256 + (size_t)kTcMaxTiles * 4, (size_t)M * K * es, kind == TC_F16 ? 0 : (size_t)M * K * 4,
-                          (size_t)K * N * es, kind == TC_F16 ? 0 : (size_t)K * N * 4,
+                          kind == TC_F16 ? (size_t)K * N * 2 : 0, 0,
                           tc_partial_floats(M, N, K, kind, sms) * 4};
     size_t o = 0;
     for (int i = 0; i < 6; ++i) {
@@ -1524,12 +1511,12 @@ extern "C" int g2k_matmul_tc(const float *A, const float *B, const float *bias, 
     unsigned *ctr = reinterpret_cast<unsigned *>(ws + 256);
     CK(cudaMemsetAsync(ws, 0, 256 + (size_t)kTcMaxTiles * 4, st));
     float *ahi = reinterpret_cast<float *>(ws + off[1]), *alo = reinterpret_cast<float *>(ws + off[2]);
-    float *bhi = reinterpret_cast<float *>(ws + off[3]), *blo = reinterpret_cast<float *>(ws + off[4]);
+    float *bhi = reinterpret_cast<float *>(ws + off[3]);   // fp16 weights (G2_F16); fp32 weights are read in place
     launch_tc_prep(kind, A, ahi, alo, reinterpret_cast<__half *>(ahi), (long long)M * K, st);
-    launch_tc_prep(kind, B, bhi, blo, reinterpret_cast<__half *>(bhi), (long long)K * N, st);
+    if (kind == TC_F16) launch_tc_prep(kind, B, nullptr, nullptr, reinterpret_cast<__half *>(bhi), (long long)K * N, st);
     TcWeights w;
     TcRowsOperand x;
-    int rc = tc_weights(&w, kind, bhi, blo, K, N);
+    int rc = tc_weights(&w, kind, kind == TC_F16 ? (const void *)bhi : (const void *)B, K, N);
     if (!rc) rc = tc_rows_operand(&x, kind, ahi, alo, K, M);
     if (rc) return set_err(rc, "g2k_matmul_tc: tensor map encoding failed");
     const int epi = (bias ? EPI_BIAS : 0) | (apply_gelu ? EPI_GELU : 0) | (residual ? EPI_RESID : 0);

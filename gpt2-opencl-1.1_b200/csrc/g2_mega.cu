@@ -673,9 +673,26 @@ __device__ __forceinline__ void producer(Cx &cx, const Sched &S) {
 // cached keys and values are read from the cache (L2); the first pass of keys
 // is loaded before the wait for q.  The key and value at pos come from the
 // qkv vector.
-__device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int pos) {
+//
+// Up to p.split_t positions, every B unit of head h (slice j of nq) runs the
+// whole attention of the head.  Past it (long contexts, where one SM reading
+// the head's whole K and V is the slow part) unit j takes only keys
+// [j c, (j + 1) c), c = ceil(T / nq), and publishes its partial (running max
+// m_j, sum l_j of exp(s - m_j), unnormalised output o_j) as tagged words;
+// each unit then polls the head's nq partials and merges them in slice order
+// (M = max m_j, out = sum_j o_j e^(m_j - M) / sum_j l_j e^(m_j - M)), so every
+// unit of the head derives the same output (flash-decoding).
+__device__ __forceinline__ bool attention(Cx &cx, int h, int jslice, int step, int l, int pos) {
     const MegaParams &p = *cx.p;
     const int E = p.E, T = pos + 1;
+    const bool split = T > p.split_t;
+    const int nq = p.nq;
+    int k0 = 0, k1 = T;
+    if (split) {
+        const int c = (T + nq - 1) / nq;
+        k0 = min(T, jslice * c);
+        k1 = min(T, k0 + c);
+    }
     const unsigned ep_in = epoch_of(p, step, l, 0);
     float *q = cx.s.attq, *pr = cx.s.attp, *a = cx.s.atta, *part = cx.s.part;
     float *rb = cx.s.red + kRedAtt;   // [0, 15) warp maxima, [16, 31) warp sums
@@ -686,9 +703,10 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
     const float4 *V4 = reinterpret_cast<const float4 *>(p.vc + hb);
     float4 kr[4];
     {
-        const bool c = key < T && key != pos;
+        const int j = k0 + key;
+        const bool c = j < k1 && j != pos;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) kr[t] = c ? K4[(size_t)key * 16 + k4 * 4 + t] : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int t = 0; t < 4; ++t) kr[t] = c ? K4[(size_t)j * 16 + k4 * 4 + t] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     {   // q, k, v of head h at pos
         const u64 limit = gtime() + cx.p->timeout_ns;
@@ -711,10 +729,10 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
     tr_inputs(cx, 1);
     // scores s_j = q . k_j / 8 (the key at pos comes from the qkv vector)
     float mloc = -FLT_MAX;
-    for (int j0 = 0; j0 < T; j0 += kKeysPerPass) {
+    for (int j0 = k0; j0 < k1; j0 += kKeysPerPass) {
         const int j = j0 + key;
-        if (j0 > 0) {
-            const bool c = j < T && j != pos;
+        if (j0 > k0) {
+            const bool c = j < k1 && j != pos;
 #pragma unroll
             for (int t = 0; t < 4; ++t) kr[t] = c ? K4[(size_t)j * 16 + k4 * 4 + t] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
@@ -736,8 +754,8 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
         s += __shfl_xor_sync(0xffffffffu, s, 1);
         s += __shfl_xor_sync(0xffffffffu, s, 2);
         s *= 0.125f;   // 1 / sqrt(64)
-        if (j < T) {
-            if (k4 == 0) pr[j] = s;
+        if (j < k1) {
+            if (k4 == 0) pr[j - k0] = s;
             mloc = fmaxf(mloc, s);
         }
     }
@@ -748,9 +766,9 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
 #pragma unroll
     for (int w = 1; w < kWarps; ++w) m = fmaxf(m, rb[w]);
     float lsum = 0.0f;
-    for (int j = cx.ctid; j < T; j += kCons) {
-        const float e = expf(pr[j] - m);
-        pr[j] = e;
+    for (int j = k0 + cx.ctid; j < k1; j += kCons) {
+        const float e = expf(pr[j - k0] - m);
+        pr[j - k0] = e;
         lsum += e;
     }
     lsum = warp_sum(lsum);
@@ -762,26 +780,49 @@ __device__ __forceinline__ bool attention(Cx &cx, int h, int step, int l, int po
     for (int w = 1; w < kWarps; ++w) Lt += rb[16 + w];
     // P.V: thread (grp, dq) sums keys grp, grp + kPvGroups, ... of dims 4 dq .. 4 dq + 3
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j0 = grp; j0 < T; j0 += 8 * kPvGroups) {   // eight keys per round: their rows in flight together
+    for (int j0 = k0 + grp; j0 < k1; j0 += 8 * kPvGroups) {   // eight keys per round: their rows in flight together
         float4 vv[8];
         float pp[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             const int j = j0 + u * kPvGroups;
-            const bool in = j < T;
+            const bool in = j < k1;
             vv[u] = (in && j != pos) ? V4[(size_t)j * 16 + dq] : make_float4(0.f, 0.f, 0.f, 0.f);
             if (j == pos)
                 vv[u] = make_float4(q[128 + 4 * dq], q[128 + 4 * dq + 1], q[128 + 4 * dq + 2], q[128 + 4 * dq + 3]);
-            pp[u] = in ? pr[j] : 0.0f;
+            pp[u] = in ? pr[j - k0] : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) fma4(o, pp[u], vv[u]);
     }
     reinterpret_cast<float4 *>(part)[grp * 16 + dq] = o;   // [kPvGroups][64]
     cons_sync();
+    float y = 0.0f;
     if (cx.ctid < 64) {
-        float y = part[cx.ctid];
+        y = part[cx.ctid];
         for (int g = 1; g < kPvGroups; ++g) y += part[g * 64 + cx.ctid];
+    }
+    if (split) {
+        // publish this slice's (o, m, l); merge the head's nq slices in slice order.
+        // pr (the probabilities) is free again after the barrier above.
+        const unsigned ep1 = epoch_of(p, step, l, 1);
+        u64 *ta = p.t_att + (size_t)h * nq * 66;
+        if (cx.ctid < 64) st_tag(ta + jslice * 66 + cx.ctid, y, ep1);
+        else if (cx.ctid == 64) st_tag(ta + jslice * 66 + 64, m, ep1);
+        else if (cx.ctid == 65) st_tag(ta + jslice * 66 + 65, Lt, ep1);
+        if (!poll_vec(cx, ta, pr, nq * 66, ep1, 7)) return false;
+        if (cx.ctid < 64) {
+            float M = -FLT_MAX;
+            for (int jj = 0; jj < nq; ++jj) M = fmaxf(M, pr[jj * 66 + 64]);
+            float L = 0.0f, acc = 0.0f;
+            for (int jj = 0; jj < nq; ++jj) {
+                const float w = expf(pr[jj * 66 + 64] - M);
+                L = fmaf(pr[jj * 66 + 65], w, L);
+                acc = fmaf(pr[jj * 66 + cx.ctid], w, acc);
+            }
+            a[cx.ctid] = acc / L;
+        }
+    } else if (cx.ctid < 64) {
         a[cx.ctid] = y / Lt;
     }
     cons_sync();
@@ -840,7 +881,7 @@ __device__ __forceinline__ bool run_units(Cx &cx, const Sched &S, int step, int 
                 dst = acc + (size_t)(u % kAccCopies) * E;
             } else {
                 const int h = mdiv(u, cf[kCfgMnq]), j = u - h * cf[kCfgNq];
-                if (!attention(cx, h, step, l, pos)) return false;
+                if (!attention(cx, h, j, step, l, pos)) return false;
                 rows = 64;
                 geo = kGeoB;
                 dst = acc + j * cf[kGeoB + 4];

@@ -24,6 +24,8 @@ struct MegaParams {
     const float *wte, *wpe, *lnf_g, *lnf_b, *lm;
     float *kc, *vc;                         // this slot's KV cache bases
     unsigned long long *t_qkv, *t_best;     // tagged activations: q, k, v; argmax partials
+    unsigned long long *t_att;              // [NH][nq][66] tagged attention partials (o[64], m, l)
+    int split_t;                            // past this many positions a head's keys are split over its nq units
     unsigned long long *acc;                // mega_acc_words(n_steps, L, E) accumulator words, zero at launch
     float *logits;                          // [V_pad] of this slot
     int *out_tokens;                        // this slot's token row

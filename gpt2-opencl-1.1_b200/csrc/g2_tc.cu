@@ -22,7 +22,11 @@
 //
 // Warp roles: warp 0 lane 0 issues the TMA loads of a STAGES-deep ring,
 // warp 1 lane 0 issues the MMAs (tcgen05.commit releases a stage when the
-// MMAs that read it complete), all four warps run the epilogue.  Every wait
+// MMAs that read it complete), all four warps run the epilogue.  For 3xTF32
+// the weight tile arrives once, as fp32 (the weights in HBM are read once,
+// not as two copies): warps 2 and 3 split it in shared memory into the tf32
+// hi part (in place) and the lo part (x - hi, rounded), the same split the
+// activations get from their producer, before the MMAs read the stage.  Every wait
 // is bounded; on expiry the kernel records G2_ERR_TIMEOUT in *err, drains its
 // own copies, frees its tensor memory and returns.
 #include <cstdio>
@@ -50,6 +54,17 @@ __device__ __forceinline__ void mbar_init(u64 *b, unsigned count) {
 }
 __device__ __forceinline__ void mbar_expect_tx(u64 *b, unsigned bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(u64 *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+// x -> tf32 hi (round to nearest, ties away) and lo = x - hi rounded the same way.
+__device__ __forceinline__ void tf32_split(float x, float &h, float &l) {
+    unsigned t;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(x));
+    h = __uint_as_float(t);
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(x - h));
+    l = __uint_as_float(t);
 }
 __device__ __forceinline__ bool mbar_try(u64 *b, unsigned parity) {
     unsigned ok;
@@ -171,13 +186,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     using S = TcShape<KIND>;
     using C = TcCfg<KIND, BN>;
     constexpr int STAGES = C::STAGES;
+    // 3xTF32: the weight tile is loaded once (fp32) and split in shared memory.
+    constexpr bool kSplitW = KIND == TC_TF32X3;
+    constexpr int WPASS = kSplitW ? 1 : S::NPASS;                       // weight copies loaded by TMA
+    constexpr unsigned kTx = kSplitW ? C::STAGE - S::A_BYTES : C::STAGE;   // TMA bytes per stage
     extern __shared__ unsigned char smem_raw[];
     unsigned char *base =
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     u64 *full = reinterpret_cast<u64 *>(base + (size_t)STAGES * C::STAGE);
     u64 *empty = full + STAGES;
     u64 *done = empty + STAGES;
-    unsigned *tslot = reinterpret_cast<unsigned *>(done + 1);
+    u64 *conv = done + 1;   // [STAGES]: the stage's weight tile is split (kSplitW)
+    unsigned *tslot = reinterpret_cast<unsigned *>(conv + STAGES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int f0 = blockIdx.x * kTcTileF, r0 = blockIdx.y * BN;
     const int kb0 = blockIdx.z * a.kb_per;
@@ -187,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+            mbar_init(&conv[s], 2);   // one arrival per splitting warp
         }
         mbar_init(done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -210,9 +231,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < pre; ++i) {
             unsigned char *st = base + (size_t)i * C::STAGE;
             const int k = (kb0 + i) * S::BK;
-            mbar_expect_tx(&full[i], C::STAGE);
+            mbar_expect_tx(&full[i], kTx);
 #pragma unroll
-            for (int p = 0; p < S::NPASS; ++p) {
+            for (int p = 0; p < WPASS; ++p) {
                 if (AK) {
                     tma_load_2d(st + p * S::A_BYTES, p ? &mw_lo : &mw_hi, k, f0, &full[i]);
                 } else {
@@ -241,9 +262,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             unsigned char *st = base + (size_t)s * C::STAGE;
             const int k = (kb0 + i) * S::BK;
-            mbar_expect_tx(&full[s], C::STAGE);
+            mbar_expect_tx(&full[s], kTx);
 #pragma unroll
-            for (int p = 0; p < S::NPASS; ++p) {
+            for (int p = 0; p < WPASS; ++p) {
                 if (AK) {   // 128 rows x 128 bytes of K in one box
                     tma_load_2d(st + p * S::A_BYTES, p ? &mw_lo : &mw_hi, k, f0, &full[s]);
                 } else {
@@ -269,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr unsigned idesc = make_idesc<KIND, BN, AK>();
         for (int i = 0; i < nkb; ++i) {
             const int s = i % STAGES;
-            if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+            if (!mbar_wait(&full[s], (i / STAGES) & 1) || (kSplitW && !mbar_wait(&conv[s], (i / STAGES) & 1))) {
                 atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
                 break;
             }
@@ -294,6 +315,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(&empty[s]);
         }
         mma_commit(done);
+    }
+    if (kSplitW && warp >= 2) {
+        // ---- weight split: fp32 tile -> tf32 hi (in place) + lo, for every stage ----
+        const int ct = threadIdx.x - 64;   // 0..63
+        for (int i = 0; i < nkb; ++i) {
+            const int s = i % STAGES;
+            if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+                atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
+                break;
+            }
+            float4 *hi = reinterpret_cast<float4 *>(base + (size_t)s * C::STAGE);
+            float4 *lo = reinterpret_cast<float4 *>(base + (size_t)s * C::STAGE + S::A_BYTES);
+#pragma unroll 4
+            for (int k = ct; k < S::A_BYTES / 16; k += 64) {
+                const float4 w = hi[k];
+                float4 h, l;
+                tf32_split(w.x, h.x, l.x);
+                tf32_split(w.y, h.y, l.y);
+                tf32_split(w.z, h.z, l.z);
+                tf32_split(w.w, h.w, l.w);
+                hi[k] = h;
+                lo[k] = l;
+            }
+            // the generic-proxy writes become visible to the tensor cores' (async proxy) reads
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&conv[s]);
+        }
     }
     __syncwarp();
 
@@ -509,29 +558,27 @@ int tc_encode(CUtensorMap *map, CUtensorMapDataType dt, const void *base, unsign
     return r == CUDA_SUCCESS ? G2_OK : G2_ERR_CUDA;
 }
 
-int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N) {
+int tc_weights(TcWeights *w, int kind, const void *W, int K, int N) {
     const bool t = kind == TC_TF32X3;
     const CUtensorMapDataType dt = t ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const unsigned bf = t ? 32 : 64, bk = t ? 32 : 64;
     w->K = K;
     w->N = N;
     w->kmajor = false;
-    int rc = tc_encode(&w->hi, dt, hi, N, K, bf, bk, t);
-    if (!rc && t) rc = tc_encode(&w->lo, dt, lo, N, K, bf, bk, t);
-    if (!t) w->lo = w->hi;
+    const int rc = tc_encode(&w->hi, dt, W, N, K, bf, bk, t);
+    w->lo = w->hi;   // unused: the kernel splits the fp32 tile itself
     return rc;
 }
 
-int tc_weights_kmajor(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N) {
+int tc_weights_kmajor(TcWeights *w, int kind, const void *W, int K, int N) {
     const bool t = kind == TC_TF32X3;
     const CUtensorMapDataType dt = t ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const unsigned bk = t ? 32 : 64;
     w->K = K;
     w->N = N;
     w->kmajor = true;
-    int rc = tc_encode(&w->hi, dt, hi, K, N, bk, kTcTileF, false);
-    if (!rc && t) rc = tc_encode(&w->lo, dt, lo, K, N, bk, kTcTileF, false);
-    if (!t) w->lo = w->hi;
+    const int rc = tc_encode(&w->hi, dt, W, K, N, bk, kTcTileF, false);
+    w->lo = w->hi;   // unused: the kernel splits the fp32 tile itself
     return rc;
 }
 
