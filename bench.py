@@ -127,6 +127,24 @@ def model_for(cfg):
     return synth.ensure_model(os.path.join(synth.default_cache(), name), shape, seed=0, dtype=cfg["dtype"]), shape
 
 
+def wait_for_model(cfg, timeout_s=1800.0):
+    """The checkpoint model_for(cfg) names, once another process has finished writing it."""
+    from gpt2b200 import synth
+    shape = getattr(synth, cfg["shape"])
+    d = os.path.join(synth.default_cache(), f"{cfg['shape'].lower()}_{cfg['dtype']}_s0")
+    want = synth._tag(shape, 0, cfg["dtype"], False, "conv1d", False, None)
+    t0 = time.time()
+    while time.time() - t0 < timeout_s:
+        try:
+            with open(os.path.join(d, "synth.json")) as f:
+                if json.load(f) == want:
+                    return d, shape
+        except (OSError, ValueError):
+            pass
+        time.sleep(1.0)
+    raise RuntimeError(f"timed out waiting for {d}")
+
+
 def kv_bytes(shape, elem, prompt, steps, batch):
     """KV read + write bytes of `steps` decode steps after a `prompt`-token prefill (per sequence x batch)."""
     L, E = shape.n_layer, shape.n_embd
@@ -452,16 +470,16 @@ def run_ours(args, cfg):
     import gpt2b200 as g2
     from gpt2b200 import replicas, synth
     names = [args.config] + ([b for b in ("c4", "c5") if b != args.config] if args.batched else [])
-    # The synthetic checkpoints are written once per node (local rank 0) before any rank reads them.
+    # The synthetic checkpoints are written once per node, by local rank 0; the other
+    # ranks wait for each one's completion tag (written last) outside any collective.
     loaded = {}
     for n in names:
         c = dict(CONFIGS[n])
         if local == 0:
             loaded[n] = model_for(c)
-        if ws > 1:
-            dist.barrier()
+    for n in names:
         if local != 0:
-            loaded[n] = model_for(c)
+            loaded[n] = wait_for_model(dict(CONFIGS[n]))
     main = measure(args.config, cfg, args, args.steps, args.warmup, ws, rank, local, dist, torch, g2, synth,
                    replicas, loaded)
     batched = {}

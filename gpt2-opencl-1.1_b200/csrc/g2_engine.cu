@@ -13,6 +13,8 @@
 #include <map>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "g2_internal.h"
 #include "g2_loader.h"
 #include "g2_mega.h"
@@ -20,6 +22,15 @@
 #include "gpt2b200.h"
 
 using namespace g2;
+
+// NVTX range over an entry point (prefill, decode, sampling, generation), for
+// profiler timelines; header-only NVTX, a no-op unless a tool is attached.
+namespace {
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+};
+}  // namespace
 
 // ------------------------------------------------------------------------------
 // errors
@@ -1131,6 +1142,7 @@ static int prefill_impl(g2_engine *e, int slot, const int *ids, int n) {
 }
 
 extern "C" int g2_prefill(g2_engine *e, int slot, const int *ids, int n) {
+    NvtxRange nvtx_range("g2_prefill");
     if (!e) return set_err(G2_ERR_ARG, "null engine");
     CK(cudaSetDevice(e->device));
     int rc = prefill_impl(e, slot, ids, n);
@@ -1139,6 +1151,7 @@ extern "C" int g2_prefill(g2_engine *e, int slot, const int *ids, int n) {
 }
 
 extern "C" int g2_decode(g2_engine *e, int slot, int token, int pos) {
+    NvtxRange nvtx_range("g2_decode");
     if (!e) return set_err(G2_ERR_ARG, "null engine");
     int rc;
     if ((rc = check_slot(e, slot))) return rc;
@@ -1165,6 +1178,7 @@ extern "C" int g2_decode(g2_engine *e, int slot, int token, int pos) {
 }
 
 extern "C" int g2_decode_batch(g2_engine *e, int n, const int *slots, const int *tokens, const int *pos) {
+    NvtxRange nvtx_range("g2_decode_batch");
     if (!e || !slots || !tokens || !pos) return set_err(G2_ERR_ARG, "g2_decode_batch: null argument");
     if (n < 1 || n > e->max_batch) return set_err(G2_ERR_RANGE, "batch %d out of range [1,%d]", n, e->max_batch);
     int rc, maxp = 0;
@@ -1209,6 +1223,7 @@ extern "C" int g2_logits(g2_engine *e, int slot, float *host, int n) {
 }
 
 extern "C" int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, float *value) {
+    NvtxRange nvtx_range("g2_argmax");
     if (!e || !token) return set_err(G2_ERR_ARG, "g2_argmax: null argument");
     int rc;
     if ((rc = check_slot(e, slot))) return rc;
@@ -1240,6 +1255,7 @@ extern "C" int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, flo
 
 extern "C" int g2_sample_device(g2_engine *e, int slot, const int *context_ids, int n_context, int forbid_eos,
                                 float temperature, int top_k, float rep_penalty, double u01, int *out_token) {
+    NvtxRange nvtx_range("g2_sample_device");
     if (!e || !out_token || n_context < 0 || (n_context > 0 && !context_ids))
         return set_err(G2_ERR_ARG, "g2_sample_device: bad argument");
     int rc;
@@ -1280,6 +1296,7 @@ extern "C" int g2_last_timing(g2_engine *e, float *prefill_ms, float *decode_ms,
 
 extern "C" int g2_generate(g2_engine *e, int slot, const int *prompt, int n_prompt, int n_new, int min_new,
                            int *out_tokens) {
+    NvtxRange nvtx_range("g2_generate");
     if (!e || !prompt || !out_tokens) return set_err(G2_ERR_ARG, "g2_generate: null argument");
     if (n_new < 1) return set_err(G2_ERR_ARG, "g2_generate: n_new must be >= 1");
     int rc;
@@ -1341,6 +1358,7 @@ static int record_batch_step(g2_engine *e, int n) {
 
 extern "C" int g2_generate_batch(g2_engine *e, int n, const int *slots, const int *prompts, const int *prompt_lens,
                                  int n_new, int *out_tokens) {
+    NvtxRange nvtx_range("g2_generate_batch");
     if (!e || !slots || !prompts || !prompt_lens || !out_tokens) return set_err(G2_ERR_ARG, "g2_generate_batch: null argument");
     if (n < 1 || n > e->max_batch) return set_err(G2_ERR_RANGE, "batch %d out of range", n);
     if (n_new < 1) return set_err(G2_ERR_ARG, "n_new must be >= 1");
