@@ -1101,17 +1101,16 @@ static int check_ids(const g2_engine *e, const int *ids, int n) {
     return G2_OK;
 }
 
-static int prefill_impl(g2_engine *e, int slot, const int *ids, int n) {
+// One many-row prefill pass over `n` staged-ready rows (tok, pos, slot per row):
+// all layers, K/V appended to each row's slot.  The forward reads its rows from
+// device arrays, so one graph per row count serves every slot and prompt (a pass
+// of several prompts has the same kernels as one prompt of as many rows, since
+// passes of more than 64 rows use the tiled attention, whose tiles each take
+// the slot of their first row).
+static int prefill_rows(g2_engine *e, int n, const int *tok, const int *pos, const int *sl, int max_pos) {
     int rc;
-    if ((rc = check_slot(e, slot))) return rc;
-    if (!ids || n <= 0 || n > e->c.n_ctx) return set_err(G2_ERR_RANGE, "prefill length %d out of range [1,%d]", n, e->c.n_ctx);
-    if ((rc = check_ids(e, ids, n))) return rc;
-    std::vector<int> pos(n), sl(n, slot);
-    for (int i = 0; i < n; ++i) pos[i] = i;
-    if ((rc = stage_rows(e, n, ids, pos.data(), sl.data()))) return rc;
-    // The forward reads its rows (tokens, positions, slot) from device arrays,
-    // so one graph per length serves every slot and prompt.
-    auto run = [&]() { return e->dtype == G2_F32 ? forward_rows<float>(e, n, n - 1) : forward_rows<__half>(e, n, n - 1); };
+    if ((rc = stage_rows(e, n, tok, pos, sl))) return rc;
+    auto run = [&]() { return e->dtype == G2_F32 ? forward_rows<float>(e, n, max_pos) : forward_rows<__half>(e, n, max_pos); };
     g2_engine::PrefillGraph *pg = nullptr;
     if (e->prefill_graph_on && n > 1) {
         pg = &e->prefill_graphs[n];
@@ -1137,6 +1136,17 @@ static int prefill_impl(g2_engine *e, int slot, const int *ids, int n) {
     } else if ((rc = run())) {
         return rc;
     }
+    return G2_OK;
+}
+
+static int prefill_impl(g2_engine *e, int slot, const int *ids, int n) {
+    int rc;
+    if ((rc = check_slot(e, slot))) return rc;
+    if (!ids || n <= 0 || n > e->c.n_ctx) return set_err(G2_ERR_RANGE, "prefill length %d out of range [1,%d]", n, e->c.n_ctx);
+    if ((rc = check_ids(e, ids, n))) return rc;
+    std::vector<int> pos(n), sl(n, slot);
+    for (int i = 0; i < n; ++i) pos[i] = i;
+    if ((rc = prefill_rows(e, n, ids, pos.data(), sl.data(), n - 1))) return rc;
     e->filled[slot] = n;
     return G2_OK;
 }
@@ -1374,17 +1384,42 @@ extern "C" int g2_generate_batch(g2_engine *e, int n, const int *slots, const in
     CK(cudaStreamSynchronize(e->st));
     const ModelConfig &c = e->c;
     CK(cudaEventRecord(e->ev[0], e->st));
-    // prefill each sequence; its greedy token goes to row i of the batch
+    // Prefill; each sequence's greedy token goes to row i of the batch.  Prompts
+    // that are whole 64-row tiles share many-row passes of up to R rows (the
+    // tensor-core GEMMs then run on more rows at once); others go one by one.
     size_t off = 0;
-    for (int i = 0; i < n; ++i) {
-        if ((rc = prefill_impl(e, slots[i], prompts + off, prompt_lens[i]))) return rc;
-        off += prompt_lens[i];
-        rc = e->dtype == G2_F32 ? lm_head_row<float>(e, prompt_lens[i] - 1, slots[i], nullptr)
-                                : lm_head_row<__half>(e, prompt_lens[i] - 1, slots[i], nullptr);
-        if (rc) return rc;
-        launch_argmax_rows(e->logits + (size_t)slots[i] * c.padded_vocab, c.vocab_size, c.padded_vocab, 1, 1,
-                           e->argmax_out + i, nullptr, nullptr, nullptr, nullptr, 0, nullptr, e->st);
-        e->launches += 1;
+    bool tiles = e->tc;
+    for (int i = 0; i < n; ++i) tiles = tiles && prompt_lens[i] % 64 == 0;
+    for (int i = 0; i < n;) {
+        int j = i + 1, rows = prompt_lens[i];
+        if (tiles)
+            while (j < n && rows + prompt_lens[j] <= e->R) rows += prompt_lens[j++];
+        if (j == i + 1) {
+            if ((rc = prefill_impl(e, slots[i], prompts + off, prompt_lens[i]))) return rc;
+        } else {
+            std::vector<int> pos(rows), sl(rows);
+            int maxp = 0;
+            for (int q = i, r = 0; q < j; ++q) {
+                for (int t = 0; t < prompt_lens[q]; ++t, ++r) {
+                    pos[r] = t;
+                    sl[r] = slots[q];
+                }
+                maxp = std::max(maxp, prompt_lens[q] - 1);
+            }
+            if ((rc = check_ids(e, prompts + off, rows))) return rc;
+            if ((rc = prefill_rows(e, rows, prompts + off, pos.data(), sl.data(), maxp))) return rc;
+            for (int q = i; q < j; ++q) e->filled[slots[q]] = prompt_lens[q];
+        }
+        for (int q = i, r = 0; q < j; r += prompt_lens[q], ++q) {
+            rc = e->dtype == G2_F32 ? lm_head_row<float>(e, r + prompt_lens[q] - 1, slots[q], nullptr)
+                                    : lm_head_row<__half>(e, r + prompt_lens[q] - 1, slots[q], nullptr);
+            if (rc) return rc;
+            launch_argmax_rows(e->logits + (size_t)slots[q] * c.padded_vocab, c.vocab_size, c.padded_vocab, 1, 1,
+                               e->argmax_out + q, nullptr, nullptr, nullptr, nullptr, 0, nullptr, e->st);
+            e->launches += 1;
+        }
+        for (int q = i; q < j; ++q) off += prompt_lens[q];
+        i = j;
     }
     CKL();
     // rows for the decode steps: tok from the prefill argmax, pos = prompt length
