@@ -156,6 +156,8 @@ struct g2_engine {
     float *tc_x2hi = nullptr, *tc_x2lo = nullptr;   // fc2's input rows (K = F), written by the fc GEMM
     unsigned *tc_ctr = nullptr;                    // split-K tile counters
     float *tc_part = nullptr;                 // split-K partial sums
+    float *tc_w = nullptr;                    // fp32 engine without wsplit: tf32 hi / lo copies of the projections
+    float *tc_lm_w = nullptr;                 // fp32 engine without wsplit: tf32 hi / lo copies of wte
     size_t tc_part_floats = 0;
     int *tc_err = nullptr;
     // device sampler
@@ -193,7 +195,7 @@ static void free_engine(g2_engine *e) {
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
     for (auto &kv : e->prefill_graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
+    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_lm_w, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
                         e->t_best, e->t_att, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
                         e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
@@ -680,24 +682,51 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
         if (e->tc) {
             e->tc_kind = dtype == G2_F32 ? TC_TF32X3 : TC_F16;
             const int Ks[4] = {E, E, E, F}, Ns[4] = {3 * E, E, F, E};
-            // The GEMMs read the engine's weights in place: fp16 as they are, fp32
-            // split into tf32 hi / lo tile by tile inside the kernel.
+            // fp16 weights are read in place.  fp32 weights: two tf32 copies (hi, lo) made
+            // here, or with G2_TC_WSPLIT=1 the fp32 weights themselves, split tile by tile
+            // inside the GEMM (half the bytes streamed, more shared-memory traffic).
+            const char *ws_env = getenv("G2_TC_WSPLIT");
+            const bool wsplit = e->tc_kind == TC_TF32X3 && ws_env && ws_env[0] == '1';
+            size_t per_layer = 0;
+            for (int q = 0; q < 4; ++q) per_layer += align_up((size_t)Ks[q] * Ns[q], 64);
+            if (e->tc_kind == TC_TF32X3 && !wsplit) TRY(dalloc(e, &e->tc_w, 2 * per_layer * c.n_layer));
             e->tc_maps.resize((size_t)c.n_layer * 4);
+            size_t o = 0;
             for (int l = 0; l < c.n_layer; ++l) {
                 const LayerOff &lo = e->L[l];
                 const size_t wo[4] = {lo.qkv_w, lo.proj_w, lo.fc_w, lo.fc2_w};
                 for (int q = 0; q < 4; ++q) {
-                    const void *W = e->tc_kind == TC_TF32X3 ? (const void *)e->w<float>(wo[q]) : (const void *)e->w<__half>(wo[q]);
-                    const int rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], e->tc_kind, W, Ks[q], Ns[q]);
+                    const size_t n = (size_t)Ks[q] * Ns[q];
+                    int rc;
+                    if (e->tc_kind == TC_TF32X3 && !wsplit) {
+                        float *hi = e->tc_w + o, *lo_ = e->tc_w + per_layer * c.n_layer + o;
+                        launch_tc_prep(TC_TF32X3, e->w<float>(wo[q]), hi, lo_, nullptr, (long long)n, e->st);
+                        rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_TF32X3, hi, lo_, Ks[q], Ns[q]);
+                    } else if (wsplit) {
+                        rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_TF32X3, e->w<float>(wo[q]), nullptr, Ks[q], Ns[q]);
+                    } else {
+                        rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_F16, e->w<__half>(wo[q]), nullptr, Ks[q], Ns[q]);
+                    }
                     if (rc) {
                         free_engine(e);
                         return set_err(rc, "tensor map of layer %d projection %d", l, q);
                     }
+                    o += align_up(n, 64);
                 }
             }
             {
-                const void *W = e->tc_kind == TC_TF32X3 ? (const void *)e->w<float>(e->lm) : (const void *)e->w<__half>(e->lm);
-                int rc = tc_weights_kmajor(&e->tc_lm, e->tc_kind, W, E, c.vocab_size);
+                const size_t n = (size_t)c.vocab_size * E;
+                int rc;
+                if (e->tc_kind == TC_TF32X3 && !wsplit) {
+                    TRY(dalloc(e, &e->tc_lm_w, 2 * align_up(n, 64)));
+                    float *hi = e->tc_lm_w, *lo_ = e->tc_lm_w + align_up(n, 64);
+                    launch_tc_prep(TC_TF32X3, e->w<float>(e->lm), hi, lo_, nullptr, (long long)n, e->st);
+                    rc = tc_weights_kmajor(&e->tc_lm, TC_TF32X3, hi, lo_, E, c.vocab_size);
+                } else if (wsplit) {
+                    rc = tc_weights_kmajor(&e->tc_lm, TC_TF32X3, e->w<float>(e->lm), nullptr, E, c.vocab_size);
+                } else {
+                    rc = tc_weights_kmajor(&e->tc_lm, TC_F16, e->w<__half>(e->lm), nullptr, E, c.vocab_size);
+                }
                 if (rc) {
                     free_engine(e);
                     return set_err(rc, "tensor map of the LM head");
@@ -1517,13 +1546,13 @@ extern "C" int g2k_matmul(const float *A, const float *B, const float *bias, con
     return G2_OK;
 }
 
-// Workspace of g2k_matmul_tc: [err + tile counters | A hi | A lo | B fp16 (G2_F16 only) | (unused) |
-// partial sums], 256-byte aligned parts.
+// Workspace of g2k_matmul_tc: [err + tile counters | A hi | A lo | B hi | B lo | partial sums],
+// 256-byte aligned parts.
 static size_t tc_ws_layout(int M, int N, int K, int precision, int sms, size_t off[6]) {
     const int kind = precision == G2_F16 ? TC_F16 : TC_TF32X3;
     const size_t es = kind == TC_F16 ? 2 : 4;
     const size_t sz[6] = {256 + (size_t)kTcMaxTiles * 4, (size_t)M * K * es, kind == TC_F16 ? 0 : (size_t)M * K * 4,
-                          kind == TC_F16 ? (size_t)K * N * 2 : 0, 0,
+                          (size_t)K * N * es, kind == TC_F16 ? 0 : (size_t)K * N * 4,
                           tc_partial_floats(M, N, K, kind, sms) * 4};
     size_t o = 0;
     for (int i = 0; i < 6; ++i) {
@@ -1564,12 +1593,12 @@ extern "C" int g2k_matmul_tc(const float *A, const float *B, const float *bias, 
     unsigned *ctr = reinterpret_cast<unsigned *>(ws + 256);
     CK(cudaMemsetAsync(ws, 0, 256 + (size_t)kTcMaxTiles * 4, st));
     float *ahi = reinterpret_cast<float *>(ws + off[1]), *alo = reinterpret_cast<float *>(ws + off[2]);
-    float *bhi = reinterpret_cast<float *>(ws + off[3]);   // fp16 weights (G2_F16); fp32 weights are read in place
+    float *bhi = reinterpret_cast<float *>(ws + off[3]), *blo = reinterpret_cast<float *>(ws + off[4]);
     launch_tc_prep(kind, A, ahi, alo, reinterpret_cast<__half *>(ahi), (long long)M * K, st);
-    if (kind == TC_F16) launch_tc_prep(kind, B, nullptr, nullptr, reinterpret_cast<__half *>(bhi), (long long)K * N, st);
+    launch_tc_prep(kind, B, bhi, blo, reinterpret_cast<__half *>(bhi), (long long)K * N, st);
     TcWeights w;
     TcRowsOperand x;
-    int rc = tc_weights(&w, kind, kind == TC_F16 ? (const void *)bhi : (const void *)B, K, N);
+    int rc = tc_weights(&w, kind, bhi, blo, K, N);
     if (!rc) rc = tc_rows_operand(&x, kind, ahi, alo, K, M);
     if (rc) return set_err(rc, "g2k_matmul_tc: tensor map encoding failed");
     const int epi = (bias ? EPI_BIAS : 0) | (apply_gelu ? EPI_GELU : 0) | (residual ? EPI_RESID : 0);

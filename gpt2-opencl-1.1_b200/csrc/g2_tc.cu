@@ -23,10 +23,11 @@
 // Warp roles: warp 0 lane 0 issues the TMA loads of a STAGES-deep ring,
 // warp 1 lane 0 issues the MMAs (tcgen05.commit releases a stage when the
 // MMAs that read it complete), all four warps run the epilogue.  For 3xTF32
-// the weight tile arrives once, as fp32 (the weights in HBM are read once,
-// not as two copies): warps 2 and 3 split it in shared memory into the tf32
-// hi part (in place) and the lo part (x - hi, rounded), the same split the
-// activations get from their producer, before the MMAs read the stage.  Every wait
+// the weights are either two tf32 copies in HBM (hi and lo, both loaded by
+// TMA), or, with TcArgs::wsplit, the fp32 weights themselves: the tile then
+// arrives once and warps 2 and 3 split it in shared memory into hi =
+// x truncated to tf32 (in place) and lo = x - hi before the MMAs read the
+// stage (half the HBM bytes, more shared-memory traffic).  Every wait
 // is bounded; on expiry the kernel records G2_ERR_TIMEOUT in *err, drains its
 // own copies, frees its tensor memory and returns.
 #include <cstdio>
@@ -58,14 +59,7 @@ __device__ __forceinline__ void mbar_expect_tx(u64 *b, unsigned bytes) {
 __device__ __forceinline__ void mbar_arrive(u64 *b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
-// x -> tf32 hi (round to nearest, ties away) and lo = x - hi rounded the same way.
-__device__ __forceinline__ void tf32_split(float x, float &h, float &l) {
-    unsigned t;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(x));
-    h = __uint_as_float(t);
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(x - h));
-    l = __uint_as_float(t);
-}
+
 __device__ __forceinline__ bool mbar_try(u64 *b, unsigned parity) {
     unsigned ok;
     asm volatile(
@@ -150,6 +144,7 @@ struct TcArgs {
     int splits;
     float *part;            // [splits][R][N] when splits > 1
     int *err;
+    int wsplit;             // 3xTF32 only: the weight map is the fp32 weights, split in shared memory
     Epi<WT> e;              // bias / GELU / residual / K,V append, out
     OperandOut op;          // the output also as the next GEMM's operand (row stride N)
 };
@@ -186,10 +181,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     using S = TcShape<KIND>;
     using C = TcCfg<KIND, BN>;
     constexpr int STAGES = C::STAGES;
-    // 3xTF32: the weight tile is loaded once (fp32) and split in shared memory.
-    constexpr bool kSplitW = KIND == TC_TF32X3;
-    constexpr int WPASS = kSplitW ? 1 : S::NPASS;                       // weight copies loaded by TMA
-    constexpr unsigned kTx = kSplitW ? C::STAGE - S::A_BYTES : C::STAGE;   // TMA bytes per stage
+    // 3xTF32 with wsplit: the weight tile is loaded once (fp32) and split in shared memory.
+    const bool kSplitW = KIND == TC_TF32X3 && a.wsplit;
+    const int WPASS = kSplitW ? 1 : S::NPASS;                              // weight copies loaded by TMA
+    const unsigned kTx = kSplitW ? C::STAGE - S::A_BYTES : C::STAGE;        // TMA bytes per stage
     extern __shared__ unsigned char smem_raw[];
     unsigned char *base =
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -232,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             unsigned char *st = base + (size_t)i * C::STAGE;
             const int k = (kb0 + i) * S::BK;
             mbar_expect_tx(&full[i], kTx);
-#pragma unroll
+#pragma unroll 2
             for (int p = 0; p < WPASS; ++p) {
                 if (AK) {
                     tma_load_2d(st + p * S::A_BYTES, p ? &mw_lo : &mw_hi, k, f0, &full[i]);
@@ -263,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             unsigned char *st = base + (size_t)s * C::STAGE;
             const int k = (kb0 + i) * S::BK;
             mbar_expect_tx(&full[s], kTx);
-#pragma unroll
+#pragma unroll 2
             for (int p = 0; p < WPASS; ++p) {
                 if (AK) {   // 128 rows x 128 bytes of K in one box
                     tma_load_2d(st + p * S::A_BYTES, p ? &mw_lo : &mw_hi, k, f0, &full[s]);
@@ -317,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(done);
     }
     if (kSplitW && warp >= 2) {
-        // ---- weight split: fp32 tile -> tf32 hi (in place) + lo, for every stage ----
+        // ---- weight split: fp32 tile -> hi = x truncated to tf32 (in place), lo = x - hi ----
         const int ct = threadIdx.x - 64;   // 0..63
         for (int i = 0; i < nkb; ++i) {
             const int s = i % STAGES;
@@ -330,13 +325,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 4
             for (int k = ct; k < S::A_BYTES / 16; k += 64) {
                 const float4 w = hi[k];
-                float4 h, l;
-                tf32_split(w.x, h.x, l.x);
-                tf32_split(w.y, h.y, l.y);
-                tf32_split(w.z, h.z, l.z);
-                tf32_split(w.w, h.w, l.w);
+                const float4 h = make_float4(__uint_as_float(__float_as_uint(w.x) & 0xFFFFE000u),
+                                             __uint_as_float(__float_as_uint(w.y) & 0xFFFFE000u),
+                                             __uint_as_float(__float_as_uint(w.z) & 0xFFFFE000u),
+                                             __uint_as_float(__float_as_uint(w.w) & 0xFFFFE000u));
                 hi[k] = h;
-                lo[k] = l;
+                lo[k] = make_float4(w.x - h.x, w.y - h.y, w.z - h.z, w.w - h.w);   // exact
             }
             // the generic-proxy writes become visible to the tensor cores' (async proxy) reads
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -558,27 +552,31 @@ int tc_encode(CUtensorMap *map, CUtensorMapDataType dt, const void *base, unsign
     return r == CUDA_SUCCESS ? G2_OK : G2_ERR_CUDA;
 }
 
-int tc_weights(TcWeights *w, int kind, const void *W, int K, int N) {
+int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N) {
     const bool t = kind == TC_TF32X3;
     const CUtensorMapDataType dt = t ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const unsigned bf = t ? 32 : 64, bk = t ? 32 : 64;
     w->K = K;
     w->N = N;
     w->kmajor = false;
-    const int rc = tc_encode(&w->hi, dt, W, N, K, bf, bk, t);
-    w->lo = w->hi;   // unused: the kernel splits the fp32 tile itself
+    w->wsplit = t && !lo;
+    int rc = tc_encode(&w->hi, dt, hi, N, K, bf, bk, t);
+    if (!rc && t && lo) rc = tc_encode(&w->lo, dt, lo, N, K, bf, bk, t);
+    else w->lo = w->hi;
     return rc;
 }
 
-int tc_weights_kmajor(TcWeights *w, int kind, const void *W, int K, int N) {
+int tc_weights_kmajor(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N) {
     const bool t = kind == TC_TF32X3;
     const CUtensorMapDataType dt = t ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const unsigned bk = t ? 32 : 64;
     w->K = K;
     w->N = N;
     w->kmajor = true;
-    const int rc = tc_encode(&w->hi, dt, W, K, N, bk, kTcTileF, false);
-    w->lo = w->hi;   // unused: the kernel splits the fp32 tile itself
+    w->wsplit = t && !lo;
+    int rc = tc_encode(&w->hi, dt, hi, K, N, bk, kTcTileF, false);
+    if (!rc && t && lo) rc = tc_encode(&w->lo, dt, lo, K, N, bk, kTcTileF, false);
+    else w->lo = w->hi;
     return rc;
 }
 
@@ -655,6 +653,7 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
     a.splits = p.splits;
     a.part = partial;
     a.err = err;
+    a.wsplit = w.wsplit ? 1 : 0;
     (void)tile_ctr;
     a.e.bias = bias;
     a.e.resid = resid;

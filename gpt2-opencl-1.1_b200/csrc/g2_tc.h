@@ -14,7 +14,8 @@ namespace g2 {
 //             the rest rounded to tf32); three tf32 products hi*hi + hi*lo +
 //             lo*hi with fp32 accumulation, which keeps fp32-level accuracy.
 //             The activations arrive split (their producer writes hi and
-//             lo); the fp32 weights are split tile by tile in shared memory.
+//             lo); the weights are two tf32 copies made at load, or the fp32
+//             weights split tile by tile in shared memory (TcWeights::wsplit).
 //  TC_F16:    fp16 operands (fp16 weights of the fp16 engine; activations
 //             rounded to fp16), fp32 accumulation.
 enum TcKind { TC_F16 = 0, TC_TF32X3 = 1 };
@@ -28,16 +29,18 @@ constexpr int kTcTileF = 128;   // output features per CTA (the MMA's M)
 int tc_encode(CUtensorMap *map, CUtensorMapDataType dt, const void *base, unsigned long long inner,
               unsigned long long outer, unsigned box_inner, unsigned box_outer, bool atom32);
 
-// Weight operand of one projection W [K][N]: the tensor map of the fp32
-// weights (TC_TF32X3, split in the kernel) or of the fp16 weights (TC_F16).
+// Weight operand of one projection W [K][N]: tensor maps of its tf32 hi and lo
+// copies (TC_TF32X3), or with lo == nullptr of the fp32 weights themselves,
+// split in the kernel (wsplit), or of the fp16 weights (TC_F16, lo unused).
 struct TcWeights {
-    CUtensorMap hi, lo;   // lo == hi (kept for the kernel's signature)
+    CUtensorMap hi, lo;
     int K, N;
     bool kmajor;   // false: [K][N] (Conv1D, feature-contiguous); true: [N][K] (rows of wte)
+    bool wsplit;   // TC_TF32X3 with the fp32 weights in `hi`
 };
-int tc_weights(TcWeights *w, int kind, const void *W, int K, int N);
+int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N);
 // The same for a [N][K] row-major weight (K-contiguous), e.g. the tied LM head wte.
-int tc_weights_kmajor(TcWeights *w, int kind, const void *W, int K, int N);
+int tc_weights_kmajor(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N);
 
 // Activation operand X [R][K] (hi / lo fp32 copies, or fp16): maps for every
 // row-tile height the planner may pick.
