@@ -169,7 +169,8 @@ struct TcCfg {
     using S = TcShape<KIND>;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE = S::NPASS * (S::A_BYTES + B_BYTES);
-    static constexpr int STAGES = (196608 / STAGE) < 8 ? (196608 / STAGE) : 8;
+    // ring stages within 216 KB of shared memory (at most 8)
+    static constexpr int STAGES = (221184 / STAGE) < 8 ? (221184 / STAGE) : 8;
     static constexpr size_t SMEM = (size_t)STAGES * STAGE + 1024 + 256;
 };
 
@@ -634,7 +635,12 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
     // a plain reduce up to 3 (fp16) or 2 (3xTF32, twice the partial bytes
     // per weight byte).
     {
-        const int cap = ln_g ? 8 : kind == TC_TF32X3 ? 2 : 3;
+        // G2_TC_CAP / G2_TC_CAP_LN override the caps (measurement sweeps)
+        static const int cap_env = getenv("G2_TC_CAP") ? atoi(getenv("G2_TC_CAP")) : 0;
+        static const int cap_ln_env = getenv("G2_TC_CAP_LN") ? atoi(getenv("G2_TC_CAP_LN")) : 0;
+        int cap = ln_g ? 8 : kind == TC_TF32X3 ? 2 : 3;
+        if (ln_g && cap_ln_env > 0) cap = cap_ln_env;
+        if (!ln_g && cap_env > 0) cap = cap_env;
         if (p.splits > cap) {
             p.kb_per = (kb_total + cap - 1) / cap;
             p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
