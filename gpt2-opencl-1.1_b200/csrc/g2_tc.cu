@@ -368,6 +368,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((unsigned)BN));
 }
 
+// Sum of the split-K partials part[s][i .. i+3] in split order.  The loads of up
+// to kSumBatch splits are issued together (the sum stays in order), so the
+// reduce waits one memory latency per batch rather than one per split.
+constexpr int kSumBatch = 8;
+__device__ __forceinline__ float4 split_sum(const float *part, int splits, long long total, long long i) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < splits; s0 += kSumBatch) {
+        float4 p[kSumBatch];
+#pragma unroll
+        for (int k = 0; k < kSumBatch; ++k)
+            if (s0 + k < splits) p[k] = *reinterpret_cast<const float4 *>(part + (size_t)(s0 + k) * total + i);
+#pragma unroll
+        for (int k = 0; k < kSumBatch; ++k)
+            if (s0 + k < splits) {
+                if (s0 + k == 0) {
+                    acc = p[0];
+                } else {
+                    acc.x += p[k].x;
+                    acc.y += p[k].y;
+                    acc.z += p[k].z;
+                    acc.w += p[k].w;
+                }
+            }
+    }
+    return acc;
+}
+
 // Ordered sum of the splits + epilogue (+ the next GEMM's operand), 4 outputs
 // per thread (N % 4 == 0); used when a GEMM ran with split-K.
 template <typename WT>
@@ -377,14 +404,7 @@ __global__ void tc_reduce_kernel(const float *part, int splits, int R, int N, Ep
     const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
     const long long total = (long long)R * N;
     if (i >= total) return;
-    float4 acc = *reinterpret_cast<const float4 *>(part + i);
-    for (int s = 1; s < splits; ++s) {
-        const float4 p = *reinterpret_cast<const float4 *>(part + (size_t)s * total + i);
-        acc.x += p.x;
-        acc.y += p.y;
-        acc.z += p.z;
-        acc.w += p.w;
-    }
+    const float4 acc = split_sum(part, splits, total, i);
     const int r = (int)(i / N), n = (int)(i % N);
     put_operand(op, (size_t)i, e.apply(r, n, acc.x));
     put_operand(op, (size_t)i + 1, e.apply(r, n + 1, acc.y));
@@ -413,14 +433,7 @@ __global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, in
         const int n = (t + k * 256) * 4;
         if (n < N) {
             const long long i = (long long)r * N + n;
-            float4 acc = *reinterpret_cast<const float4 *>(part + i);
-            for (int sp = 1; sp < splits; ++sp) {
-                const float4 p = *reinterpret_cast<const float4 *>(part + (size_t)sp * total + i);
-                acc.x += p.x;
-                acc.y += p.y;
-                acc.z += p.z;
-                acc.w += p.w;
-            }
+            const float4 acc = split_sum(part, splits, total, i);
             v[4 * k] = e.apply(r, n, acc.x);
             v[4 * k + 1] = e.apply(r, n + 1, acc.y);
             v[4 * k + 2] = e.apply(r, n + 2, acc.z);
