@@ -371,13 +371,15 @@ struct AttnArgs {
 };
 
 template <typename KT>
-__global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
+__global__ void __launch_bounds__(128, sizeof(KT) == 4 ? 3 : 4) attn_kernel(AttnArgs<KT> a) {
     pdl_wait();
     pdl_launch();
     constexpr int CH = kAttnChunk;              // keys per chunk: one per thread in the score pass
     constexpr int VN = 16 / sizeof(KT);         // elements per 16-byte load
     constexpr int DG = kHeadDim / VN;           // 16-byte groups per 64-dim row (8 fp16, 16 fp32)
     constexpr int KG = 128 / DG;                // key groups of the P.V pass
+    constexpr int VPT = CH / KG;                // V slices per thread in the P.V pass
+    constexpr int VPF = VPT <= 8 ? VPT : 8;     // of which requested together with the keys
     static_assert(CH == 128, "one key per thread");
     __shared__ float q[kHeadDim];
     __shared__ float p[CH];
@@ -434,6 +436,17 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
 #pragma unroll
             for (int i = 0; i < DG; ++i) kw[i] = kr[i];
         }
+        // The V slices this thread multiplies in the P.V pass (keys kg, kg + KG, ... of dims
+        // dg * VN ..) do not depend on the scores: the first VPF of them are requested
+        // with the keys, the rest right after the scores, so the pass waits for no load.
+        // (With fused c_attn partials the value at pos comes from shared memory instead.)
+        const int jpos = fused ? pos - j0 : -1;
+        uint4 vw[VPT];
+#pragma unroll
+        for (int i = 0; i < VPF; ++i) {
+            const int jj = kg + i * KG;
+            if (jj < nj && jj != jpos) vw[i] = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN);
+        }
         __syncthreads();   // q (and k, v at pos); the previous chunk's readers of p and red are done
         float s = -FLT_MAX;
         if (tid < nj) {
@@ -446,6 +459,12 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
             }
             s = d;
         }
+        asm volatile("" ::: "memory");   // the second half of the V slices after the key rows are dead
+#pragma unroll
+        for (int i = VPF; i < VPT; ++i) {
+            const int jj = kg + i * KG;
+            if (jj < nj && jj != jpos) vw[i] = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN);
+        }
         const float m = block_max(s, sh);
         const float e = tid < nj ? expf(s - m) : 0.0f;
         p[tid] = e;
@@ -454,22 +473,17 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<KT> a) {
         float o[VN], o2[VN];
 #pragma unroll
         for (int i = 0; i < VN; ++i) o[i] = o2[i] = 0.0f;
-        // (with fused c_attn partials the value at pos is taken from shared memory, not the cache)
-        const int jpos = fused ? pos - j0 : -1;
-        int jj = kg;
-        for (; jj + KG < nj; jj += 2 * KG) {   // two keys in flight
-            if (jj == jpos || jj + KG == jpos) break;
-            const uint4 v0 = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN);
-            const uint4 v1 = *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj + KG) * kHeadDim + dg * VN);
-            fma_vec(o, v0, p[jj], KT());
-            fma_vec(o2, v1, p[jj + KG], KT());
-        }
-        for (; jj < nj; jj += KG) {
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int jj = kg + i * KG;
+            if (jj >= nj) continue;
             if (jj == jpos) {
 #pragma unroll
-                for (int i = 0; i < VN; ++i) o[i] = fmaf(p[jj], knew[1][dg * VN + i], o[i]);
+                for (int e = 0; e < VN; ++e) o[e] = fmaf(p[jj], knew[1][dg * VN + e], o[e]);
+            } else if (i & 1) {
+                fma_vec(o2, vw[i], p[jj], KT());
             } else {
-                fma_vec(o, *reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jj) * kHeadDim + dg * VN), p[jj], KT());
+                fma_vec(o, vw[i], p[jj], KT());
             }
         }
 #pragma unroll
