@@ -64,7 +64,7 @@ struct Epi {
         if (epi & EPI_BIAS) v += tof(bias[n]);
         if (epi & EPI_GELU) v = gelu_f(v);
         if (epi & EPI_RESID) v = resid[(size_t)r * N + n] + v;
-        out[(size_t)r * N + n] = v;
+        if (!(epi & EPI_NOSTORE)) out[(size_t)r * N + n] = v;
         if ((epi & EPI_KV) && n >= E) {
             const float stored = v;
             int m = n - E;

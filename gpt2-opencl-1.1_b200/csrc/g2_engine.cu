@@ -910,7 +910,8 @@ static int forward_rows(g2_engine *e, int nrows, int max_pos, bool decode_rows =
             e->launches += 1;
         }
         rows_gemm<WT>(e, l, 2, e->xln, nrows, e->w<WT>(o.fc_w), e->w<WT>(o.fc_b), nullptr, e->ffn, F, E,
-                      EPI_BIAS | EPI_GELU, nullptr, rows, opf);
+                      // on the tensor cores only fc2's operand is read, not the fp32 rows
+                      EPI_BIAS | EPI_GELU | (e->tc ? EPI_NOSTORE : 0), nullptr, rows, opf);
         // the next LayerNorm: ln_1 of layer l + 1, or ln_f after the last layer
         const bool last = l + 1 == c.n_layer;
         const WT *ng = e->w<WT>(last ? e->lnf_g : e->L[l + 1].ln1_g), *nb = e->w<WT>(last ? e->lnf_b : e->L[l + 1].ln1_b);

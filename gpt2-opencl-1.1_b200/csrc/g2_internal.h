@@ -63,7 +63,8 @@ struct Rows {
     const int *slot;
 };
 
-enum Epilogue { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_RESID = 4, EPI_KV = 8 };
+// EPI_NOSTORE: the result goes only to the next GEMM's operand (OperandOut), not to `out`.
+enum Epilogue { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_RESID = 4, EPI_KV = 8, EPI_NOSTORE = 16 };
 
 // A kernel's output also written as the next tensor-core GEMM's operand (row
 // stride = that GEMM's K): kind 1 = tf32 hi / lo pair (TC_TF32X3), 0 = fp16

@@ -41,7 +41,8 @@ namespace g2 {
 
 namespace {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;   // 8 warps: all run the epilogue, warps 2-7 split fp32 weights (wsplit)
+constexpr int kSplitWarps = 6;
 typedef unsigned long long u64;
 
 __device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
@@ -137,6 +138,20 @@ __device__ __forceinline__ void tmem_ld32(unsigned taddr, float (&v)[32]) {
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
+// 16 consecutive fp32 columns of this warp's 32 tensor-memory lanes.
+__device__ __forceinline__ void tmem_ld16(unsigned taddr, float (&v)[16]) {
+    unsigned r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+        "[%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+
 template <typename WT>
 struct TcArgs {
     int N, R;
@@ -169,8 +184,11 @@ struct TcCfg {
     using S = TcShape<KIND>;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE = S::NPASS * (S::A_BYTES + B_BYTES);
-    // ring stages within 216 KB of shared memory (at most 8)
-    static constexpr int STAGES = (221184 / STAGE) < 8 ? (221184 / STAGE) : 8;
+    // Ring stages within 216 KB of shared memory (at most 8).  The fp16 128-row tiles of
+    // prefill keep to ~100 KB so that two CTAs share an SM: one's epilogue then overlaps
+    // the other's main loop.
+    static constexpr int BUDGET = (KIND == TC_F16 && BN == 128) ? 102400 : 221184;
+    static constexpr int STAGES = (BUDGET / STAGE) < 8 ? (BUDGET / STAGE) : 8;
     static constexpr size_t SMEM = (size_t)STAGES * STAGE + 1024 + 256;
 };
 
@@ -200,10 +218,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nkb = min(a.kb_per, a.kb_total - kb0);   // >= 1 (the planner guarantees it)
 
     if (threadIdx.x == 0) {
+        // the TMA descriptors (kernel parameters) are fetched while the barriers are set up
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<u64>(&mw_hi)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<u64>(&mx_hi)) : "memory");
+        if (KIND == TC_TF32X3) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<u64>(&mw_lo)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<u64>(&mx_lo)) : "memory");
+        }
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&conv[s], 2);   // one arrival per splitting warp
+            mbar_init(&conv[s], kSplitWarps);   // one arrival per splitting warp
         }
         mbar_init(done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -314,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (kSplitW && warp >= 2) {
         // ---- weight split: fp32 tile -> hi = x truncated to tf32 (in place), lo = x - hi ----
-        const int ct = threadIdx.x - 64;   // 0..63
+        const int ct = threadIdx.x - 64;   // 0 .. 32 kSplitWarps - 1
         for (int i = 0; i < nkb; ++i) {
             const int s = i % STAGES;
             if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
@@ -324,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float4 *hi = reinterpret_cast<float4 *>(base + (size_t)s * C::STAGE);
             float4 *lo = reinterpret_cast<float4 *>(base + (size_t)s * C::STAGE + S::A_BYTES);
 #pragma unroll 4
-            for (int k = ct; k < S::A_BYTES / 16; k += 64) {
+            for (int k = ct; k < S::A_BYTES / 16; k += 32 * kSplitWarps) {
                 const float4 w = hi[k];
                 const float4 h = make_float4(__uint_as_float(__float_as_uint(w.x) & 0xFFFFE000u),
                                              __uint_as_float(__float_as_uint(w.y) & 0xFFFFE000u),
@@ -345,16 +370,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0));   // warp-uniform: tcgen05.ld is .sync.aligned
     if (!ok && lane == 0) atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int f = f0 + warp * 32 + lane;
+    // Warp w reads tensor-memory lanes 32 (w % 4) .. (its lane quarter: features f0 + 32 (w % 4) + lane)
+    // and columns (w / 4) BN / 2 .. of them (rows r0 + ...): two warps per quarter.
+    const int q = warp & 3, ch = warp >> 2;
+    const int f = f0 + q * 32 + lane;
     if (ok) {
         float *dst = a.part + (size_t)blockIdx.z * a.R * a.N;
+        constexpr int HALF = BN / 2;
+        constexpr int CW = HALF < 32 ? HALF : 32;   // columns per tensor-memory load
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = ch * HALF; c0 < (ch + 1) * HALF; c0 += CW) {
             float v[32];
-            tmem_ld32(tmem + ((unsigned)(warp * 32) << 16) + (unsigned)c0, v);
+            if (CW == 32) {
+                tmem_ld32(tmem + ((unsigned)(q * 32) << 16) + (unsigned)c0, v);
+            } else {
+                float v16[16];
+                tmem_ld16(tmem + ((unsigned)(q * 32) << 16) + (unsigned)c0, v16);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = v16[j];
+            }
             if (f < a.N) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
+                for (int j = 0; j < CW; ++j) {
                     const int r = r0 + c0 + j;
                     if (r >= a.R) continue;
                     if (a.splits == 1) put_operand(a.op, (size_t)r * a.N + f, a.e.apply(r, f, v[j]));
