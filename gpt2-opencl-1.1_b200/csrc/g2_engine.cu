@@ -687,13 +687,8 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
             // inside the GEMM (half the bytes streamed, more shared-memory traffic).
             const char *ws_env = getenv("G2_TC_WSPLIT");
             const bool wsplit = e->tc_kind == TC_TF32X3 && ws_env && ws_env[0] == '1';
-            // G2_TC_TILED=1: the tf32 copies in feature-tile-major order (each ring stage of a
-            // GEMM CTA then reads one contiguous block)
-            const char *tl_env = getenv("G2_TC_TILED");
-            const bool tiled = e->tc_kind == TC_TF32X3 && !wsplit && tl_env && tl_env[0] == '1';
             size_t per_layer = 0;
-            for (int q = 0; q < 4; ++q)
-                per_layer += align_up(tiled ? tc_tiled_elems(Ks[q], Ns[q]) : (size_t)Ks[q] * Ns[q], 64);
+            for (int q = 0; q < 4; ++q) per_layer += align_up((size_t)Ks[q] * Ns[q], 64);
             if (e->tc_kind == TC_TF32X3 && !wsplit) TRY(dalloc(e, &e->tc_w, 2 * per_layer * c.n_layer));
             e->tc_maps.resize((size_t)c.n_layer * 4);
             size_t o = 0;
@@ -703,11 +698,7 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
                 for (int q = 0; q < 4; ++q) {
                     const size_t n = (size_t)Ks[q] * Ns[q];
                     int rc;
-                    if (tiled) {
-                        float *hi = e->tc_w + o, *lo_ = e->tc_w + per_layer * c.n_layer + o;
-                        launch_tc_prep_tiled(TC_TF32X3, e->w<float>(wo[q]), hi, lo_, nullptr, Ks[q], Ns[q], e->st);
-                        rc = tc_weights_tiled(&e->tc_maps[(size_t)l * 4 + q], TC_TF32X3, hi, lo_, Ks[q], Ns[q]);
-                    } else if (e->tc_kind == TC_TF32X3 && !wsplit) {
+                    if (e->tc_kind == TC_TF32X3 && !wsplit) {
                         float *hi = e->tc_w + o, *lo_ = e->tc_w + per_layer * c.n_layer + o;
                         launch_tc_prep(TC_TF32X3, e->w<float>(wo[q]), hi, lo_, nullptr, (long long)n, e->st);
                         rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_TF32X3, hi, lo_, Ks[q], Ns[q]);
@@ -720,7 +711,7 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
                         free_engine(e);
                         return set_err(rc, "tensor map of layer %d projection %d", l, q);
                     }
-                    o += align_up(tiled ? tc_tiled_elems(Ks[q], Ns[q]) : n, 64);
+                    o += align_up(n, 64);
                 }
             }
             {

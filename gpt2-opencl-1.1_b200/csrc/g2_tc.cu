@@ -160,8 +160,6 @@ struct TcArgs {
     float *part;            // [splits][R][N] when splits > 1
     int *err;
     int wsplit;             // 3xTF32 only: the weight map is the fp32 weights, split in shared memory
-    int wtiled;             // the weights are stored feature-tile-major: [N / 128][K][128]
-    int K;
     Epi<WT> e;              // bias / GELU / residual / K,V append, out
     OperandOut op;          // the output also as the next GEMM's operand (row stride N)
 };
@@ -251,9 +249,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // tiles are requested before waiting for the previous kernel, the rows
         // (its output) after.
         const int pre = nkb < STAGES ? nkb : STAGES;
-        // weight coordinates: (feature, k) in [K][N], or (feature within the tile, tile K + k)
-        // in the feature-tile-major layout, where a stage's rows are one contiguous block
-        const int wx0 = a.wtiled ? 0 : f0, wy0 = a.wtiled ? blockIdx.x * a.K : 0;
         for (int i = 0; i < pre; ++i) {
             unsigned char *st = base + (size_t)i * C::STAGE;
             const int k = (kb0 + i) * S::BK;
@@ -265,8 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
 #pragma unroll
                     for (int b = 0; b < S::NBOX; ++b)
-                        tma_load_2d(st + p * S::A_BYTES + b * (S::BK * 128), p ? &mw_lo : &mw_hi, wx0 + b * S::BOX_F,
-                                    wy0 + k, &full[i]);
+                        tma_load_2d(st + p * S::A_BYTES + b * (S::BK * 128), p ? &mw_lo : &mw_hi, f0 + b * S::BOX_F,
+                                    k, &full[i]);
                 }
             }
         }
@@ -296,8 +291,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
 #pragma unroll
                     for (int b = 0; b < S::NBOX; ++b)
-                        tma_load_2d(st + p * S::A_BYTES + b * (S::BK * 128), p ? &mw_lo : &mw_hi, wx0 + b * S::BOX_F,
-                                    wy0 + k, &full[s]);
+                        tma_load_2d(st + p * S::A_BYTES + b * (S::BK * 128), p ? &mw_lo : &mw_hi, f0 + b * S::BOX_F,
+                                    k, &full[s]);
                 }
             }
 #pragma unroll
@@ -615,61 +610,11 @@ int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, in
     w->K = K;
     w->N = N;
     w->kmajor = false;
-    w->tiled = false;
     w->wsplit = t && !lo;
     int rc = tc_encode(&w->hi, dt, hi, N, K, bf, bk, t);
     if (!rc && t && lo) rc = tc_encode(&w->lo, dt, lo, N, K, bf, bk, t);
     else w->lo = w->hi;
     return rc;
-}
-
-int tc_weights_tiled(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N) {
-    const bool t = kind == TC_TF32X3;
-    const CUtensorMapDataType dt = t ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    const unsigned bf = t ? 32 : 64, bk = t ? 32 : 64;
-    const unsigned long long tiles = (N + kTcTileF - 1) / kTcTileF;
-    w->K = K;
-    w->N = N;
-    w->kmajor = false;
-    w->wsplit = false;
-    w->tiled = true;
-    int rc = tc_encode(&w->hi, dt, hi, kTcTileF, tiles * K, bf, bk, t);
-    if (!rc && t) rc = tc_encode(&w->lo, dt, lo, kTcTileF, tiles * K, bf, bk, t);
-    else w->lo = w->hi;
-    return rc;
-}
-
-// W [K][N] (fp32) -> feature-tile-major [N / 128][K][128] copies: tf32 hi and lo, or fp16
-// (features past N in the last tile are zero).
-__global__ void tc_prep_tiled_kernel(int kind, const float *W, float *hi, float *lo, __half *h16, int K, int N,
-                                     long long total) {
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int c = (int)(i % kTcTileF);
-        const long long rest = i / kTcTileF;
-        const int k = (int)(rest % K);
-        const int tile = (int)(rest / K);
-        const int n = tile * kTcTileF + c;
-        const float x = n < N ? W[(size_t)k * N + n] : 0.0f;
-        if (kind == TC_TF32X3) {
-            unsigned u;
-            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));
-            const float h = __uint_as_float(u);
-            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x - h));
-            hi[i] = h;
-            lo[i] = __uint_as_float(u);
-        } else {
-            h16[i] = __float2half_rn(x);
-        }
-    }
-}
-
-size_t tc_tiled_elems(int K, int N) { return (size_t)((N + kTcTileF - 1) / kTcTileF) * kTcTileF * K; }
-
-void launch_tc_prep_tiled(int kind, const float *W, float *hi, float *lo, __half *h16, int K, int N, cudaStream_t st) {
-    const long long total = (long long)tc_tiled_elems(K, N);
-    const int blocks = (int)((total + 255) / 256 < 8192 ? (total + 255) / 256 : 8192);
-    tc_prep_tiled_kernel<<<blocks, 256, 0, st>>>(kind, W, hi, lo, h16, K, N, total);
 }
 
 int tc_weights_kmajor(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N) {
@@ -679,7 +624,6 @@ int tc_weights_kmajor(TcWeights *w, int kind, const void *hi, const void *lo, in
     w->K = K;
     w->N = N;
     w->kmajor = true;
-    w->tiled = false;
     w->wsplit = t && !lo;
     int rc = tc_encode(&w->hi, dt, hi, K, N, bk, kTcTileF, false);
     if (!rc && t && lo) rc = tc_encode(&w->lo, dt, lo, K, N, bk, kTcTileF, false);
@@ -766,8 +710,6 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
     a.part = partial;
     a.err = err;
     a.wsplit = w.wsplit ? 1 : 0;
-    a.wtiled = w.tiled ? 1 : 0;
-    a.K = w.K;
     (void)tile_ctr;
     a.e.bias = bias;
     a.e.resid = resid;

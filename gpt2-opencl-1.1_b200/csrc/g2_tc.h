@@ -37,15 +37,8 @@ struct TcWeights {
     int K, N;
     bool kmajor;   // false: [K][N] (Conv1D, feature-contiguous); true: [N][K] (rows of wte)
     bool wsplit;   // TC_TF32X3 with the fp32 weights in `hi`
-    bool tiled;    // feature-tile-major copies [N / 128][K][128] (tc_weights_tiled)
 };
 int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N);
-// Copies of W [K][N] in feature-tile-major order, [ceil(N / 128)][K][128] (a CTA's
-// 128 features over K rows are one contiguous block, so each ring stage reads
-// contiguous memory): tf32 hi / lo (TC_TF32X3) or fp16 (TC_F16) from fp32 W.
-size_t tc_tiled_elems(int K, int N);
-void launch_tc_prep_tiled(int kind, const float *W, float *hi, float *lo, __half *h16, int K, int N, cudaStream_t st);
-int tc_weights_tiled(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N);
 // The same for a [N][K] row-major weight (K-contiguous), e.g. the tied LM head wte.
 int tc_weights_kmajor(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N);
 
