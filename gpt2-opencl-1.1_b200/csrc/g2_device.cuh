@@ -72,8 +72,10 @@ struct Epi {
             if (isv) m -= E;
             const int h = m >> 6, d = m & 63;
             const int p = pos[r];
-            if (p < 0 || p >= kv.max_seq) return stored;   // positions are validated on the host; never write outside
-            const long long off = (long long)slot[r] * kv.slot_stride + (long long)layer * kv.layer_stride +
+            const int sl = slot[r];
+            // positions and slots are validated on the host; never write outside (reported when checked)
+            if (!G2_BOUNDS(p >= 0 && p < kv.max_seq && sl >= 0 && sl < kv.n_slots, 103)) return stored;
+            const long long off = (long long)sl * kv.slot_stride + (long long)layer * kv.layer_stride +
                                   ((long long)h * kv.max_seq + p) * kHeadDim + d;
             WT *base = reinterpret_cast<WT *>(isv ? kv.v : kv.k);
             base[off] = fromf<WT>(v);

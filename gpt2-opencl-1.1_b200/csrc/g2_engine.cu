@@ -120,6 +120,9 @@ struct g2_engine {
     std::map<int, PrefillGraph> prefill_graphs;
     bool prefill_graph_on = true;
     int batch_graph_n = 0, batch_graph_kernels = 0;
+    // Largest position a captured batch step may reach: it sizes the attention grid
+    // (128-key chunks per row), so the graph is re-captured when a generation needs more.
+    int batch_graph_pos = -1, batch_pos_hint = -1;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     float last_prefill_ms = 0, last_decode_ms = 0;
     int last_decode_steps = 0;
@@ -556,6 +559,7 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
     // KV caches [slot][layer][head][pos][64]
     e->kv.max_seq = S;
     e->kv.n_head = NH;
+    e->kv.n_slots = max_batch;
     e->kv.layer_stride = (long long)NH * S * kHeadDim;
     e->kv.slot_stride = e->kv.layer_stride * c.n_layer;
     const size_t kv_elems = (size_t)e->kv.slot_stride * max_batch;
@@ -1098,9 +1102,22 @@ static void dump_trace(g2_engine *e, int n_steps) {
     fclose(f);
 }
 
-// After a synchronisation: report an expired device-side wait of the decode kernel.
+namespace g2 {
+int check_flags() {
+    int v = check_flag_kernels();
+    const int t = check_flag_tc(), m = check_flag_mega();
+    if (!v) v = t;
+    if (!v) v = m;
+    return v;
+}
+}  // namespace g2
+
+// After a synchronisation: report an expired device-side wait of the decode kernel
+// (and, in the bounds-checked build, a failed bounds test of any kernel).
 static int check_mega_err(g2_engine *e) {
     int code = 0;
+    if (const int site = check_flags())
+        return set_err(G2_ERR_RANGE, "bounds check failed in a kernel (site %d, G2_CHECK build)", site);
     if (e->tc) {
         CK(cudaMemcpy(&code, e->tc_err, sizeof(int), cudaMemcpyDeviceToHost));
         if (code) {
@@ -1386,7 +1403,7 @@ extern "C" int g2_generate(g2_engine *e, int slot, const int *prompt, int n_prom
 template <typename WT>
 static int record_batch_step(g2_engine *e, int n) {
     const ModelConfig &c = e->c;
-    int rc = forward_rows<WT>(e, n, -1, true);
+    int rc = forward_rows<WT>(e, n, e->batch_pos_hint, true);
     if (rc) return rc;
     lm_head_rows<WT>(e, n);
     launch_argmax_rows(e->logits_rows, c.vocab_size, c.padded_vocab, n, 1, nullptr, nullptr, e->rows_tok,
@@ -1466,7 +1483,12 @@ extern "C" int g2_generate_batch(g2_engine *e, int n, const int *slots, const in
     CK(cudaMemcpyAsync(e->batch_step, &one, sizeof(int), cudaMemcpyHostToDevice, e->st));
     CK(cudaEventRecord(e->ev[1], e->st));
     if (n_new > 1) {
-        if (!e->batch_graph || e->batch_graph_n != n) {
+        // this generation's last decode position, rounded up to a whole attention chunk
+        int last = 0;
+        for (int i = 0; i < n; ++i) last = std::max(last, prompt_lens[i] + n_new - 2);
+        const int hint = std::min((last / kAttnChunk + 1) * kAttnChunk - 1, e->c.n_ctx - 1);
+        if (!e->batch_graph || e->batch_graph_n != n || e->batch_graph_pos < hint) {
+            e->batch_pos_hint = hint;
             if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
             e->batch_graph = nullptr;
             cudaGraph_t g;
@@ -1482,6 +1504,7 @@ extern "C" int g2_generate_batch(g2_engine *e, int n, const int *slots, const in
             e->batch_graph_kernels = (int)(e->launches - before);
             e->launches = before;
             e->batch_graph_n = n;
+            e->batch_graph_pos = hint;
         }
         for (int s = 1; s < n_new; ++s) CK(cudaGraphLaunch(e->batch_graph, e->st));
         e->launches += (long long)(n_new - 1) * e->batch_graph_kernels;

@@ -54,7 +54,34 @@ struct KVLayout {
     long long layer_stride;      // elements
     int max_seq;
     int n_head;
+    int n_slots = 1;             // sequence slots the cache holds
 };
+
+// Bounds-checked build (-DG2_CHECK, `make check`): device code tests the
+// data-dependent indexes it is about to use (token ids, positions, slots, key
+// counts) with G2_BOUNDS(ok, site); a failed test records `site` in this
+// translation unit's flag (first failure wins) and the access is skipped, in
+// place of a device assert.  The host reads and clears the flags with
+// check_flags() at its synchronising calls and reports G2_ERR_RANGE.  In the
+// normal build G2_BOUNDS(ok, site) is just `ok` (the same guards, unreported).
+#ifdef G2_CHECK
+#ifdef __CUDACC__
+static __device__ int g2_check_flag;
+__device__ __forceinline__ bool g2_bounds(bool ok, int site) {
+    if (!ok) atomicCAS(&g2_check_flag, 0, site);
+    return ok;
+}
+#define G2_BOUNDS(ok, site) ::g2::g2_bounds((ok), (site))
+#endif
+#else
+#define G2_BOUNDS(ok, site) (ok)
+#endif
+// The first failed bounds test of each kernel file since the last call (0: none),
+// cleared; always 0 in the normal build.
+int check_flags();
+int check_flag_kernels();
+int check_flag_mega();
+int check_flag_tc();
 
 // Row descriptors of a batched pass: row r embeds tok[r] at pos[r] of slot[r].
 struct Rows {

@@ -155,8 +155,13 @@ __global__ void embed_kernel(const WT *wte, const WT *wpe, Rows rows, float *h, 
     pdl_launch();
     const int r = blockIdx.x;
     // ids and positions are validated on the host; clamp so that a bad value
-    // can never address outside the tables
-    const int tok = min(max(rows.tok[r], 0), V - 1), pos = min(max(rows.pos[r], 0), n_pos - 1);
+    // can never address outside the tables (and report it in the checked build)
+    const int tok0 = rows.tok[r], pos0 = rows.pos[r];
+    if (threadIdx.x == 0) {
+        (void)G2_BOUNDS(tok0 >= 0 && tok0 < V, 101);
+        (void)G2_BOUNDS(pos0 >= 0 && pos0 < n_pos, 102);
+    }
+    const int tok = min(max(tok0, 0), V - 1), pos = min(max(pos0, 0), n_pos - 1);
     for (int i = threadIdx.x; i < E; i += blockDim.x)
         h[(size_t)r * E + i] = tof(wte[(size_t)tok * E + i]) + tof(wpe[(size_t)pos * E + i]);
 }
@@ -390,6 +395,7 @@ __global__ void __launch_bounds__(128, sizeof(KT) == 4 ? 3 : 4) attn_kernel(Attn
     const int h = blockIdx.x, sp = blockIdx.y, r = blockIdx.z, tid = threadIdx.x;
     const int NH = a.kv.n_head;
     const int T = a.rows.pos[r] + 1;
+    if (!G2_BOUNDS(T >= 1 && T <= a.kv.max_seq && a.rows.slot[r] >= 0 && a.rows.slot[r] < a.kv.n_slots, 104)) return;
     const int nsplit = (T + CH - 1) / CH;   // chunks; CTA sp takes chunks sp, sp + Y, ...
     const int Y = gridDim.y;
     if (sp >= nsplit) return;
@@ -591,6 +597,7 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillAttnArgs a) {
     __syncthreads();
     int pmax = -1;
     for (int i = 0; i < nr; ++i) pmax = max(pmax, spos[i]);
+    if (!G2_BOUNDS(pmax < a.kv.max_seq && a.rows.slot[r0] >= 0 && a.rows.slot[r0] < a.kv.n_slots, 105)) return;
     int mypos[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) mypos[i] = spos[ty * 4 + i];
@@ -1157,5 +1164,19 @@ void launch_transpose(const float *src, WT *dst, int rows, int cols, cudaStream_
     template void launch_transpose<WT>(const float *, WT *, int, int, cudaStream_t);
 G2_INST(float)
 G2_INST(__half)
+
+#ifdef G2_CHECK
+int check_flag_kernels() {
+    int v = 0;
+    cudaMemcpyFromSymbol(&v, g2_check_flag, sizeof(int));
+    if (v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g2_check_flag, &z, sizeof(int));
+    }
+    return v;
+}
+#else
+int check_flag_kernels() { return 0; }
+#endif
 
 }  // namespace g2

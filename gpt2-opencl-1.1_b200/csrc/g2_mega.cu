@@ -1000,6 +1000,11 @@ __global__ void __launch_bounds__(kThreads, 1) mega_decode_kernel(MegaParams P) 
     const int step_base = p.state->step, min_new = p.state->min_new;
     for (int step = 0; step < p.n_steps; ++step) {
         cx.tl = kTr && cx.tr && cx.cta == 0 && step == min(3, p.n_steps - 1);
+        // the host bounds the steps so that pos stays inside the cache; clamp regardless
+        if (!G2_BOUNDS(tok >= 0 && tok < p.V && pos >= 0 && pos < p.max_seq, 106)) {
+            tok = min(max(tok, 0), p.V - 1);
+            pos = min(max(pos, 0), p.max_seq - 1);
+        }
         // x = wte[tok] + wpe[pos] (embed, math.cl:333)
         for (int i = cx.ctid; i < E; i += kCons) {
             const float x = p.wte[(size_t)tok * E + i] + p.wpe[(size_t)pos * E + i];
@@ -1183,5 +1188,19 @@ const void *mega_kernel_ptr(bool traced) {
 }
 int mega_slot_bytes() { return kSlotBytes; }
 int mega_max_keys() { return kMaxKeys; }
+
+#ifdef G2_CHECK
+int check_flag_mega() {
+    int v = 0;
+    cudaMemcpyFromSymbol(&v, g2_check_flag, sizeof(int));
+    if (v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g2_check_flag, &z, sizeof(int));
+    }
+    return v;
+}
+#else
+int check_flag_mega() { return 0; }
+#endif
 
 }  // namespace g2

@@ -767,4 +767,18 @@ template int launch_tc_gemm<__half>(int, const TcWeights &, const TcRowsOperand 
                                     cudaStream_t, OperandOut, int, const __half *, const __half *, OperandOut, bool *,
                                     bool, int *);
 
+#ifdef G2_CHECK
+int check_flag_tc() {
+    int v = 0;
+    cudaMemcpyFromSymbol(&v, g2_check_flag, sizeof(int));
+    if (v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g2_check_flag, &z, sizeof(int));
+    }
+    return v;
+}
+#else
+int check_flag_tc() { return 0; }
+#endif
+
 }  // namespace g2

@@ -15,7 +15,9 @@ import os
 import numpy as np
 
 PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-LIB_PATH = os.path.join(PKG_DIR, "libgpt2b200.so")
+# G2_LIB selects another build of the same ABI, e.g. the bounds-checked
+# libgpt2b200_check.so (`make -C gpt2-opencl-1.1_b200 check`).
+LIB_PATH = os.environ.get("G2_LIB") or os.path.join(PKG_DIR, "libgpt2b200.so")
 
 G2_F32, G2_F16 = 0, 1
 EOS = 50256

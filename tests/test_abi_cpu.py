@@ -36,6 +36,16 @@ def test_library_exports_every_declared_function():
     assert not missing, f"not exported: {missing}"
 
 
+def test_checked_build_exports_every_declared_function():
+    """The bounds-checked build (make check, -DG2_CHECK) is the same ABI."""
+    path = os.path.join(ROOT, "gpt2-opencl-1.1_b200", "libgpt2b200_check.so")
+    if not os.path.exists(path):
+        pytest.skip("checked build not made (make -C gpt2-opencl-1.1_b200 check)")
+    lib = C.CDLL(path)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
 def test_workspace_queries_without_device():
     assert g2.matvec_workspace(2304, 768) > 0
     assert g2.matvec_workspace(0, 768) == 0
