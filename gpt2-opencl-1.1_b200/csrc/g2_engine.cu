@@ -161,6 +161,9 @@ struct g2_engine {
     float *tc_part = nullptr;                 // split-K partial sums
     float *tc_w = nullptr;                    // fp32 engine without wsplit: tf32 hi / lo copies of the projections
     float *tc_lm_w = nullptr;                 // fp32 engine without wsplit: tf32 hi / lo copies of wte
+    void *tc_img = nullptr;                   // stage images of the projections (TcWeights::img_hi / img_lo)
+    void *tc_idx = nullptr;                   // 16 KB: the coordinate tensor of tc_stage_perm
+    unsigned *tc_perm = nullptr;              // stage element positions (tc_stage_perm)
     size_t tc_part_floats = 0;
     int *tc_err = nullptr;
     // device sampler
@@ -198,7 +201,7 @@ static void free_engine(g2_engine *e) {
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
     for (auto &kv : e->prefill_graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_lm_w, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
+    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_lm_w, e->tc_img, e->tc_idx, e->tc_perm, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
                         e->t_best, e->t_att, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
                         e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
@@ -223,7 +226,12 @@ static int dalloc(g2_engine *e, T **p, size_t count) {
     if (r != cudaSuccess)
         return set_err(G2_ERR_OOM, "cudaMalloc(%zu bytes): %s", bytes, cudaGetErrorString(r));
     e->device_bytes += bytes;
+    // The zeroing runs on the legacy default stream, which the engine's
+    // non-blocking stream does not wait for: it must be complete before the
+    // caller hands the buffer to that stream, or it could land after the
+    // stream's first writes.
     r = cudaMemset(*p, 0, bytes);
+    if (r == cudaSuccess) r = cudaDeviceSynchronize();
     if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(r));
     return G2_OK;
 }
@@ -466,6 +474,12 @@ static int load_weights(g2_engine *e, const std::string &dir) {
         }
         if (r != cudaSuccess) return set_err(G2_ERR_CUDA, "upload '%s': %s", it.name.c_str(), cudaGetErrorString(r));
     }
+    // A cudaMemcpy from pageable host memory may return before its DMA has landed,
+    // and the engine's stream does not wait for the legacy default stream: every
+    // upload must be complete before the first kernel on that stream reads the
+    // weights (the tensor-core weight images are built right after this).
+    if ((r = cudaDeviceSynchronize()) != cudaSuccess)
+        return set_err(G2_ERR_CUDA, "weight upload: %s", cudaGetErrorString(r));
     // Algorithmic bytes streamed per decode step (weights + biases + LN + lm head).
     const size_t es = e->esize;
     e->stream_bytes = es * ((size_t)c.n_layer * ((size_t)4 * E * E + (size_t)2 * E * F) + (size_t)E * c.padded_vocab) +
@@ -686,30 +700,68 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
         if (e->tc) {
             e->tc_kind = dtype == G2_F32 ? TC_TF32X3 : TC_F16;
             const int Ks[4] = {E, E, E, F}, Ns[4] = {3 * E, E, F, E};
-            // fp16 weights are read in place.  fp32 weights: two tf32 copies (hi, lo) made
-            // here, or with G2_TC_WSPLIT=1 the fp32 weights themselves, split tile by tile
-            // inside the GEMM (half the bytes streamed, more shared-memory traffic).
+            // fp32 engines stream the projections as stage images (TcWeights::img_hi),
+            // one bulk copy per ring stage: tf32 hi / lo images (or, with
+            // G2_TC_WSPLIT=1, the fp32 image split in shared memory), in place of
+            // tf32 hi / lo copies read by tiled TMA boxes (G2_TC_IMG=0).  fp16 engines
+            // read their weights in place by tiled boxes (G2_TC_IMG=1 makes an fp16
+            // image; measured no faster, so it is not worth the second copy).
             const char *ws_env = getenv("G2_TC_WSPLIT");
             const bool wsplit = e->tc_kind == TC_TF32X3 && ws_env && ws_env[0] == '1';
-            size_t per_layer = 0;
-            for (int q = 0; q < 4; ++q) per_layer += align_up((size_t)Ks[q] * Ns[q], 64);
-            if (e->tc_kind == TC_TF32X3 && !wsplit) TRY(dalloc(e, &e->tc_w, 2 * per_layer * c.n_layer));
+            const char *img_env = getenv("G2_TC_IMG");
+            const bool img = img_env ? img_env[0] == '1' : e->tc_kind == TC_TF32X3;
+            const int ncopy = e->tc_kind == TC_TF32X3 && !wsplit ? 2 : 1;
+            const size_t elem = e->tc_kind == TC_TF32X3 ? 4 : 2;
+            size_t per_layer = 0, img_layer = 0;
+            for (int q = 0; q < 4; ++q) {
+                per_layer += align_up((size_t)Ks[q] * Ns[q], 64);
+                img_layer += tc_image_elems(e->tc_kind, Ks[q], Ns[q]) * elem;
+            }
+            if (img) {
+                TRY(dalloc(e, reinterpret_cast<unsigned char **>(&e->tc_img), ncopy * img_layer * c.n_layer));
+                TRY(dalloc(e, reinterpret_cast<unsigned char **>(&e->tc_idx), (size_t)16384));
+                TRY(dalloc(e, &e->tc_perm, (size_t)8192));
+                TRY(dalloc(e, &e->tc_err, 1));
+                if (tc_stage_perm(e->tc_kind, e->tc_idx, e->tc_perm, e->tc_err, e->st)) {
+                    free_engine(e);
+                    return set_err(G2_ERR_CUDA, "stage permutation of the tensor-core weights");
+                }
+            } else if (e->tc_kind == TC_TF32X3 && !wsplit) {
+                TRY(dalloc(e, &e->tc_w, 2 * per_layer * c.n_layer));
+            }
             e->tc_maps.resize((size_t)c.n_layer * 4);
-            size_t o = 0;
+            size_t o = 0, io = 0;
             for (int l = 0; l < c.n_layer; ++l) {
                 const LayerOff &lo = e->L[l];
                 const size_t wo[4] = {lo.qkv_w, lo.proj_w, lo.fc_w, lo.fc2_w};
                 for (int q = 0; q < 4; ++q) {
                     const size_t n = (size_t)Ks[q] * Ns[q];
+                    TcWeights &tw = e->tc_maps[(size_t)l * 4 + q];
                     int rc;
-                    if (e->tc_kind == TC_TF32X3 && !wsplit) {
+                    if (img) {
+                        // the maps stay valid descriptors of the weights; the GEMM reads the images
+                        const size_t ib = tc_image_elems(e->tc_kind, Ks[q], Ns[q]) * elem;
+                        unsigned char *ih = reinterpret_cast<unsigned char *>(e->tc_img) + io;
+                        unsigned char *il = ncopy == 2 ? ih + img_layer * c.n_layer : nullptr;
+                        if (e->tc_kind == TC_TF32X3) {
+                            rc = tc_weights(&tw, TC_TF32X3, e->w<float>(wo[q]), nullptr, Ks[q], Ns[q]);
+                            launch_tc_image(TC_TF32X3, e->w<float>(wo[q]), ih, il, e->tc_perm, Ks[q], Ns[q], e->st);
+                            tw.wsplit = wsplit;
+                        } else {
+                            rc = tc_weights(&tw, TC_F16, e->w<__half>(wo[q]), nullptr, Ks[q], Ns[q]);
+                            launch_tc_image(TC_F16, e->w<__half>(wo[q]), ih, nullptr, e->tc_perm, Ks[q], Ns[q], e->st);
+                        }
+                        tw.img_hi = ih;
+                        tw.img_lo = il;
+                        io += ib;
+                    } else if (e->tc_kind == TC_TF32X3 && !wsplit) {
                         float *hi = e->tc_w + o, *lo_ = e->tc_w + per_layer * c.n_layer + o;
                         launch_tc_prep(TC_TF32X3, e->w<float>(wo[q]), hi, lo_, nullptr, (long long)n, e->st);
-                        rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_TF32X3, hi, lo_, Ks[q], Ns[q]);
+                        rc = tc_weights(&tw, TC_TF32X3, hi, lo_, Ks[q], Ns[q]);
                     } else if (wsplit) {
-                        rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_TF32X3, e->w<float>(wo[q]), nullptr, Ks[q], Ns[q]);
+                        rc = tc_weights(&tw, TC_TF32X3, e->w<float>(wo[q]), nullptr, Ks[q], Ns[q]);
                     } else {
-                        rc = tc_weights(&e->tc_maps[(size_t)l * 4 + q], TC_F16, e->w<__half>(wo[q]), nullptr, Ks[q], Ns[q]);
+                        rc = tc_weights(&tw, TC_F16, e->w<__half>(wo[q]), nullptr, Ks[q], Ns[q]);
                     }
                     if (rc) {
                         free_engine(e);
@@ -752,15 +804,26 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
             for (int q = 0; q < 4; ++q)
                 e->tc_part_floats = std::max(e->tc_part_floats, tc_partial_floats(R, Ns[q], Ks[q], e->tc_kind, e->sms));
             TRY(dalloc(e, &e->tc_part, e->tc_part_floats));
-            TRY(dalloc(e, &e->tc_err, 1));
+            if (!e->tc_err) TRY(dalloc(e, &e->tc_err, 1));
             cudaError_t r = cudaStreamSynchronize(e->st);
             if (r != cudaSuccess) {
                 free_engine(e);
                 return set_err(G2_ERR_CUDA, "tensor-core weight split: %s", cudaGetErrorString(r));
             }
+            int perm_err = 0;   // an expired wait in tc_stage_perm
+            if (cudaMemcpy(&perm_err, e->tc_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess || perm_err) {
+                free_engine(e);
+                return set_err(perm_err ? perm_err : G2_ERR_CUDA, "tensor-core weight images: the stage permutation failed");
+            }
         }
     }
 #undef TRY
+    // the remaining uploads of set-up (row tables, packed units) are complete
+    // before any call runs work on the engine's stream
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+        free_engine(e);
+        return set_err(G2_ERR_CUDA, "g2_open: engine set-up failed");
+    }
     *out = e;
     return G2_OK;
 }
@@ -883,14 +946,14 @@ static int forward_rows(g2_engine *e, int nrows, int max_pos, bool decode_rows =
         }
         QkvPartials qp;
         if (e->tc && decode_rows) {   // c_attn without its reduce: the attention sums the partials
-            int splits = 1;
+            SplitInfo si;
             e->launches += launch_tc_gemm<WT>(e->tc_kind, e->tc_maps[(size_t)l * 4], e->tc_x_e, nrows, e->tc_part,
                                               e->tc_part_floats, e->tc_ctr, e->tc_err, e->w<WT>(o.qkv_b), nullptr,
                                               e->qkv, EPI_BIAS | EPI_KV, &e->kv, l, rows, e->sms, st, OperandOut(), 0,
-                                              nullptr, nullptr, OperandOut(), nullptr, true, &splits);
-            if (splits > 1) {
+                                              nullptr, nullptr, OperandOut(), nullptr, true, &si);
+            if (si.split()) {
                 qp.part = e->tc_part;
-                qp.splits = splits;
+                qp.si = si;
                 qp.bias = e->w<WT>(o.qkv_b);
             }
         } else {
@@ -1121,14 +1184,14 @@ static int check_mega_err(g2_engine *e) {
     if (e->tc) {
         CK(cudaMemcpy(&code, e->tc_err, sizeof(int), cudaMemcpyDeviceToHost));
         if (code) {
-            CK(cudaMemset(e->tc_err, 0, sizeof(int)));
+            CK(cudaMemsetAsync(e->tc_err, 0, sizeof(int), e->st));   // ordered before the stream's next kernels
             return set_err(G2_ERR_TIMEOUT, "tensor-core GEMM: a bounded device-side wait expired");
         }
     }
     if (!e->mega) return G2_OK;
     CK(cudaMemcpy(&code, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code) {
-        CK(cudaMemset(e->d_err, 0, sizeof(int)));
+        CK(cudaMemsetAsync(e->d_err, 0, sizeof(int), e->st));
         if (code == kErrClamp)
             return set_err(G2_ERR_RANGE, "decode kernel: an accumulator contribution exceeded +-2^21 and was clamped");
         return set_err(G2_ERR_TIMEOUT, "decode kernel: a bounded device-side wait expired (site %d)", code);

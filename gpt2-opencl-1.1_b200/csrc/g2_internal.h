@@ -143,14 +143,40 @@ void launch_gemm_rows(const float *A, const WT *W, const WT *bias, const float *
 // 0..pos[r] of its slot. partial/counters: scratch (see attn_workspace_*).
 size_t attn_partial_floats(int nrows, int n_head, int max_seq);
 size_t attn_counter_count(int nrows, int n_head);
+
+// How many split-K partials a tensor-core GEMM left for an output column, and
+// where.  Partial j of column n is at part[j][row][n] either way.
+//  * Uniform splits (G == 0): every 128-feature tile has `splits` partials.
+//  * Balanced split (G > 0): the tiles' K blocks, tile-major (U = tiles * KB
+//    units), are cut into G contiguous equal shares, one per CTA, so a CTA
+//    may finish one tile and start the next.  CTA c takes units
+//    [floor(c U / G), floor((c + 1) U / G)); its piece of tile t is partial
+//    c - cta_of(t KB) of that tile, so the pieces of a tile are summed in
+//    K order.
+struct SplitInfo {
+    int splits = 1;
+    int G = 0;
+    int KB = 0;
+    long long U = 0;
+    // the CTA whose share holds unit u
+    __host__ __device__ int cta_of(long long u) const { return (int)(((u + 1) * G - 1) / U); }
+    // partials of output column n (tiles of 128 features)
+    __host__ __device__ int at(int n) const {
+        if (!G) return splits;
+        const long long u0 = (long long)(n >> 7) * KB;
+        return cta_of(u0 + KB - 1) - cta_of(u0) + 1;
+    }
+    __host__ __device__ bool split() const { return G > 0 || splits > 1; }
+};
+
 // The c_attn output of a batched decode step still as split-K partial tiles
-// ([splits][rows][3E], row stride qkv_stride) plus the c_attn bias: the
+// ([partials][rows][3E], row stride qkv_stride, counted by si) plus the c_attn bias: the
 // attention sums them itself (and appends the new K and V to the cache), so
 // the GEMM needs no reduce launch.  Only for rows of distinct sequences: a
 // row's attention then reads no K/V row that another row of the pass appends.
 struct QkvPartials {
     const float *part = nullptr;
-    int splits = 0;
+    SplitInfo si;
     const void *bias = nullptr;   // [3E] of the engine's weight type
 };
 

@@ -369,8 +369,8 @@ struct AttnArgs {
     unsigned *counters;  // [rows][heads]
     int max_splits;
     OperandOut op;       // the output also as the next GEMM's operand (row stride out_stride)
-    const float *qpart;  // c_attn split-K partials [qsplits][rows][qkv_stride], or nullptr (qkv holds the sums)
-    int qsplits;
+    const float *qpart;  // c_attn split-K partials [partials][rows][qkv_stride], or nullptr (qkv holds the sums)
+    SplitInfo qsi;       // partials per column
     long long qtotal;    // rows * qkv_stride
     const KT *qbias;     // c_attn bias [3E]
 };
@@ -414,8 +414,18 @@ __global__ void __launch_bounds__(128, sizeof(KT) == 4 ? 3 : 4) attn_kernel(Attn
         for (int c = tid; c < (kv_here ? 3 : 1) * kHeadDim; c += blockDim.x) {
             const int part = c / kHeadDim, d = c % kHeadDim;   // 0 q, 1 k, 2 v
             const size_t col = (size_t)part * E + h * kHeadDim + d;
-            float acc = a.qpart[(size_t)r * a.qkv_stride + col];
-            for (int sp2 = 1; sp2 < a.qsplits; ++sp2) acc += a.qpart[(size_t)sp2 * a.qtotal + (size_t)r * a.qkv_stride + col];
+            // the partials' loads are issued eight at a time; the sum stays in split order
+            const float *pc = a.qpart + (size_t)r * a.qkv_stride + col;
+            const int ns = a.qsi.at((int)col);
+            float acc = 0.0f;
+            for (int s0 = 0; s0 < ns; s0 += 8) {
+                float pv[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) pv[k] = s0 + k < ns ? pc[(size_t)(s0 + k) * a.qtotal] : 0.0f;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (s0 + k < ns) acc = s0 + k == 0 ? pv[0] : acc + pv[k];
+            }
             const float v = acc + tof(a.qbias[col]);
             if (part == 0) {
                 q[d] = v * 0.125f;
@@ -1022,7 +1032,7 @@ void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int 
     AttnArgs<KT> a;
     a.op = op;
     a.qpart = qp.part;
-    a.qsplits = qp.splits;
+    a.qsi = qp.si;
     a.qtotal = (long long)nrows * qkv_stride;
     a.qbias = reinterpret_cast<const KT *>(qp.bias);
     a.qkv = qkv;

@@ -30,8 +30,11 @@
 // stage (half the HBM bytes, more shared-memory traffic).  Every wait
 // is bounded; on expiry the kernel records G2_ERR_TIMEOUT in *err, drains its
 // own copies, frees its tensor memory and returns.
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
+#include <vector>
 
 #include "g2_device.cuh"
 #include "g2_tc.h"
@@ -78,6 +81,14 @@ __device__ __forceinline__ bool mbar_wait(u64 *b, unsigned parity) {
         if (mbar_try(b, parity)) return true;
         if (gtime() > limit) return false;
     }
+}
+// One contiguous bulk copy global -> shared (16-byte aligned, size a multiple of 16), L2 policy `pol`.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned bytes, u64 *bar, u64 pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, u64 *bar) {
     asm volatile(
@@ -155,11 +166,13 @@ __device__ __forceinline__ void tmem_ld16(unsigned taddr, float (&v)[16]) {
 template <typename WT>
 struct TcArgs {
     int N, R;
-    int kb_total, kb_per;   // K blocks in total and per split
+    int kb_total, kb_per;   // K blocks in total and per split (uniform splits)
     int splits;
-    float *part;            // [splits][R][N] when splits > 1
+    SplitInfo si;           // si.G > 0: balanced split over si.G CTAs (one row tile), else si.splits == splits
+    float *part;            // [partials][R][N] when the GEMM is split
     int *err;
     int wsplit;             // 3xTF32 only: the weight map is the fp32 weights, split in shared memory
+    const unsigned char *img_hi, *img_lo;   // stage images of the weights (TcWeights), or nullptr
     Epi<WT> e;              // bias / GELU / residual / K,V append, out
     OperandOut op;          // the output also as the next GEMM's operand (row stride N)
 };
@@ -213,9 +226,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     u64 *conv = done + 1;   // [STAGES]: the stage's weight tile is split (kSplitW)
     unsigned *tslot = reinterpret_cast<unsigned *>(conv + STAGES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int f0 = blockIdx.x * kTcTileF, r0 = blockIdx.y * BN;
-    const int kb0 = blockIdx.z * a.kb_per;
-    const int nkb = min(a.kb_per, a.kb_total - kb0);   // >= 1 (the planner guarantees it)
+    // This CTA's work: one segment (tile, first K block, K blocks, partial index), or,
+    // under the balanced split, the end of one tile and the start of the next (the
+    // planner keeps a share under one tile's K blocks, so never more than two).
+    int sf0, sf1, sk0, sk1, sn0, sn1 = 0, sj0, sj1 = 0;   // segments 0 and 1 (scalars, no local-memory arrays)
+    const int r0 = a.si.G ? 0 : blockIdx.y * BN;
+    if (a.si.G) {
+        const long long U = a.si.U, KB = a.si.KB;
+        const long long u0 = (long long)blockIdx.x * U / a.si.G, u1 = (long long)(blockIdx.x + 1) * U / a.si.G;
+        const int t0 = (int)(u0 / KB);
+        const long long e0 = min(u1, (long long)(t0 + 1) * KB);
+        sf0 = t0 * kTcTileF;
+        sk0 = (int)(u0 - t0 * KB);
+        sn0 = (int)(e0 - u0);
+        sj0 = (int)blockIdx.x - a.si.cta_of((long long)t0 * KB);
+        sf1 = sf0 + kTcTileF;
+        sk1 = 0;
+        sn1 = (int)(u1 - e0);   // the next tile's first K blocks, if any (partial 0 of that tile)
+    } else {
+        sf0 = blockIdx.x * kTcTileF;
+        sk0 = blockIdx.z * a.kb_per;
+        sn0 = min(a.kb_per, a.kb_total - sk0);   // >= 1 (the planner guarantees it)
+        sj0 = blockIdx.z;
+        sf1 = sf0;
+        sk1 = 0;
+    }
+    const int nkb = sn0 + sn1;
+    const unsigned tcols = a.si.G ? 2u * BN : (unsigned)BN;   // one BN-column accumulator per segment
 
     if (threadIdx.x == 0) {
         // the TMA descriptors (kernel parameters) are fetched while the barriers are set up
@@ -235,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
-                     "r"((unsigned)BN));
+                     "r"(tcols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -249,14 +286,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         // tiles are requested before waiting for the previous kernel, the rows
         // (its output) after.
         const int pre = nkb < STAGES ? nkb : STAGES;
+        u64 pol;   // weights are read once per pass: L2 evict-first
+        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
         for (int i = 0; i < pre; ++i) {
             unsigned char *st = base + (size_t)i * C::STAGE;
-            const int k = (kb0 + i) * S::BK;
+            const int sg = i < sn0 ? 0 : 1, f0 = sg ? sf1 : sf0;
+            const int k = ((sg ? sk1 : sk0) + i - (sg ? sn0 : 0)) * S::BK;
             mbar_expect_tx(&full[i], kTx);
 #pragma unroll 2
             for (int p = 0; p < WPASS; ++p) {
                 if (AK) {
                     tma_load_2d(st + p * S::A_BYTES, p ? &mw_lo : &mw_hi, k, f0, &full[i]);
+                } else if (a.img_hi) {   // the stage image: one bulk copy
+                    bulk_load(st + p * S::A_BYTES,
+                              (p ? a.img_lo : a.img_hi) + ((size_t)(f0 / kTcTileF) * a.kb_total + k / S::BK) * S::A_BYTES,
+                              S::A_BYTES, &full[i], pol);
                 } else {
 #pragma unroll
                     for (int b = 0; b < S::NBOX; ++b)
@@ -269,7 +313,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         pdl_launch();
         for (int i = 0; i < pre; ++i) {
             unsigned char *st = base + (size_t)i * C::STAGE;
-            const int k = (kb0 + i) * S::BK;
+            const int sg = i < sn0 ? 0 : 1;
+            const int k = ((sg ? sk1 : sk0) + i - (sg ? sn0 : 0)) * S::BK;
 #pragma unroll
             for (int p = 0; p < S::NPASS; ++p)
                 tma_load_2d(st + S::NPASS * S::A_BYTES + p * C::B_BYTES, p ? &mx_lo : &mx_hi, k, r0, &full[i]);
@@ -282,12 +327,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             unsigned char *st = base + (size_t)s * C::STAGE;
-            const int k = (kb0 + i) * S::BK;
+            const int sg = i < sn0 ? 0 : 1, f0 = sg ? sf1 : sf0;
+            const int k = ((sg ? sk1 : sk0) + i - (sg ? sn0 : 0)) * S::BK;
             mbar_expect_tx(&full[s], kTx);
 #pragma unroll 2
             for (int p = 0; p < WPASS; ++p) {
                 if (AK) {   // 128 rows x 128 bytes of K in one box
                     tma_load_2d(st + p * S::A_BYTES, p ? &mw_lo : &mw_hi, k, f0, &full[s]);
+                } else if (a.img_hi) {
+                    bulk_load(st + p * S::A_BYTES,
+                              (p ? a.img_lo : a.img_hi) + ((size_t)(f0 / kTcTileF) * a.kb_total + k / S::BK) * S::A_BYTES,
+                              S::A_BYTES, &full[s], pol);
                 } else {
 #pragma unroll
                     for (int b = 0; b < S::NBOX; ++b)
@@ -318,19 +368,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const unsigned a_hi = smem_u32(base + (size_t)s * C::STAGE);
             const unsigned b_hi = a_hi + S::NPASS * S::A_BYTES;
+            const int sg = i < sn0 ? 0 : 1, ki = i - (sg ? sn0 : 0);   // segment, K block within it
+            const unsigned td = tmem + (unsigned)(sg * BN);
 #pragma unroll
             for (int j = 0; j < S::NSTEP; ++j) {
                 const unsigned ao = AK ? j * S::KSTEP * S::ELEM : j * S::KSTEP * 128, bo = j * S::KSTEP * S::ELEM;
                 const u64 ad = AK ? sw128_desc(a_hi + ao, 16, 1024) : sw128_desc(a_hi + ao, S::BK * 128, S::A_SBO, S::A_LAYOUT);
                 const u64 bd = sw128_desc(b_hi + bo, 16, 1024);
-                const unsigned acc = (i | j) != 0;
-                mma<KIND>(tmem, ad, bd, idesc, acc);
+                const unsigned acc = (ki | j) != 0;
+                mma<KIND>(td, ad, bd, idesc, acc);
                 if (KIND == TC_TF32X3) {
                     const u64 ad_lo = AK ? sw128_desc(a_hi + S::A_BYTES + ao, 16, 1024)
                                          : sw128_desc(a_hi + S::A_BYTES + ao, S::BK * 128, S::A_SBO, S::A_LAYOUT);
                     const u64 bd_lo = sw128_desc(b_hi + C::B_BYTES + bo, 16, 1024);
-                    mma<KIND>(tmem, ad, bd_lo, idesc, 1u);
-                    mma<KIND>(tmem, ad_lo, bd, idesc, 1u);
+                    mma<KIND>(td, ad, bd_lo, idesc, 1u);
+                    mma<KIND>(td, ad_lo, bd, idesc, 1u);
                 }
             }
             mma_commit(&empty[s]);
@@ -371,38 +423,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok && lane == 0) atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     // Warp w reads tensor-memory lanes 32 (w % 4) .. (its lane quarter: features f0 + 32 (w % 4) + lane)
-    // and columns (w / 4) BN / 2 .. of them (rows r0 + ...): two warps per quarter.
+    // and columns (w / 4) BN / 2 .. of them (rows r0 + ...): two warps per quarter.  One
+    // accumulator per segment; a split GEMM writes the segment's partial of its tile.
     const int q = warp & 3, ch = warp >> 2;
-    const int f = f0 + q * 32 + lane;
+    const bool direct = !a.si.G && a.splits == 1;
     if (ok) {
-        float *dst = a.part + (size_t)blockIdx.z * a.R * a.N;
         constexpr int HALF = BN / 2;
         constexpr int CW = HALF < 32 ? HALF : 32;   // columns per tensor-memory load
 #pragma unroll 1
-        for (int c0 = ch * HALF; c0 < (ch + 1) * HALF; c0 += CW) {
-            float v[32];
-            if (CW == 32) {
-                tmem_ld32(tmem + ((unsigned)(q * 32) << 16) + (unsigned)c0, v);
-            } else {
-                float v16[16];
-                tmem_ld16(tmem + ((unsigned)(q * 32) << 16) + (unsigned)c0, v16);
+        for (int sg = 0; sg < 2; ++sg) {
+            if ((sg ? sn1 : sn0) == 0) continue;
+            const int f = (sg ? sf1 : sf0) + q * 32 + lane;
+            float *dst = a.part + (size_t)(sg ? sj1 : sj0) * a.R * a.N;
+#pragma unroll 1
+            for (int c0 = ch * HALF; c0 < (ch + 1) * HALF; c0 += CW) {
+                float v[32];
+                const unsigned ta = tmem + ((unsigned)(q * 32) << 16) + (unsigned)(sg * BN + c0);
+                if (CW == 32) {
+                    tmem_ld32(ta, v);
+                } else {
+                    float v16[16];
+                    tmem_ld16(ta, v16);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = v16[j];
-            }
-            if (f < a.N) {
+                    for (int j = 0; j < 16; ++j) v[j] = v16[j];
+                }
+                if (f < a.N) {
 #pragma unroll
-                for (int j = 0; j < CW; ++j) {
-                    const int r = r0 + c0 + j;
-                    if (r >= a.R) continue;
-                    if (a.splits == 1) put_operand(a.op, (size_t)r * a.N + f, a.e.apply(r, f, v[j]));
-                    else dst[(size_t)r * a.N + f] = v[j];
+                    for (int j = 0; j < CW; ++j) {
+                        const int r = r0 + c0 + j;
+                        if (r >= a.R) continue;
+                        if (direct) put_operand(a.op, (size_t)r * a.N + f, a.e.apply(r, f, v[j]));
+                        else dst[(size_t)r * a.N + f] = v[j];
+                    }
                 }
             }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((unsigned)BN));
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols));
 }
 
 // Sum of the split-K partials part[s][i .. i+3] in split order.  The loads of up
@@ -435,14 +494,14 @@ __device__ __forceinline__ float4 split_sum(const float *part, int splits, long 
 // Ordered sum of the splits + epilogue (+ the next GEMM's operand), 4 outputs
 // per thread (N % 4 == 0); used when a GEMM ran with split-K.
 template <typename WT>
-__global__ void tc_reduce_kernel(const float *part, int splits, int R, int N, Epi<WT> e, OperandOut op) {
+__global__ void tc_reduce_kernel(const float *part, SplitInfo si, int R, int N, Epi<WT> e, OperandOut op) {
     pdl_wait();
     pdl_launch();
     const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
     const long long total = (long long)R * N;
     if (i >= total) return;
-    const float4 acc = split_sum(part, splits, total, i);
     const int r = (int)(i / N), n = (int)(i % N);
+    const float4 acc = split_sum(part, si.at(n), total, i);
     put_operand(op, (size_t)i, e.apply(r, n, acc.x));
     put_operand(op, (size_t)i + 1, e.apply(r, n + 1, acc.y));
     put_operand(op, (size_t)i + 2, e.apply(r, n + 2, acc.z));
@@ -456,7 +515,7 @@ __global__ void tc_reduce_kernel(const float *part, int splits, int R, int N, Ep
 // row, times gamma plus beta, as the next GEMM's operand.  N % 4 == 0,
 // N <= 2048.
 template <typename WT>
-__global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, int splits, int R, int N, Epi<WT> e,
+__global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, SplitInfo si, int R, int N, Epi<WT> e,
                                                            const WT *g, const WT *b, OperandOut op) {
     pdl_wait();
     pdl_launch();
@@ -470,7 +529,7 @@ __global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, in
         const int n = (t + k * 256) * 4;
         if (n < N) {
             const long long i = (long long)r * N + n;
-            const float4 acc = split_sum(part, splits, total, i);
+            const float4 acc = split_sum(part, si.at(n), total, i);
             v[4 * k] = e.apply(r, n, acc.x);
             v[4 * k + 1] = e.apply(r, n + 1, acc.y);
             v[4 * k + 2] = e.apply(r, n + 2, acc.z);
@@ -534,6 +593,79 @@ __global__ void tc_prep_kernel(int kind, const float4 *x, float4 *hi, float4 *lo
     }
 }
 
+// ---- stage images -------------------------------------------------------------
+// Element positions of one stage's weight tile as the tiled TMA loads of the
+// GEMM place them: the NBOX boxes of BOX_F features x BK rows of a tensor
+// whose element (row, feature) holds row * 128 + feature are loaded exactly as
+// the producer loads a weight stage (same box shapes, swizzle and shared-memory
+// alignment), then copied out, so table[p] names the element at position p.
+template <int KIND>
+__global__ void tc_perm_kernel(const __grid_constant__ CUtensorMap m, unsigned *table, int *err) {
+    using S = TcShape<KIND>;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char *base =
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    u64 *bar = reinterpret_cast<u64 *>(base + S::A_BYTES);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_expect_tx(bar, S::A_BYTES);
+        for (int b = 0; b < S::NBOX; ++b) tma_load_2d(base + b * (S::BK * 128), &m, b * S::BOX_F, 0, bar);
+    }
+    __syncthreads();
+    const bool ok = mbar_wait(bar, 0);
+    if (!ok) {
+        if (threadIdx.x == 0) atomicCAS(err, 0, G2_ERR_TIMEOUT);
+        return;
+    }
+    for (int i = threadIdx.x; i < S::A_BYTES / S::ELEM; i += blockDim.x)
+        table[i] = S::ELEM == 4 ? reinterpret_cast<const unsigned *>(base)[i]
+                                : (unsigned)reinterpret_cast<const unsigned short *>(base)[i];
+}
+
+__global__ void tc_iota_kernel(unsigned *idx32, unsigned short *idx16, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        if (idx32) idx32[i] = (unsigned)i;
+        else idx16[i] = (unsigned short)i;
+    }
+}
+
+// img[(t KB + kb) PER + p] = W[kb BK + row][t 128 + feature], (row, feature) = table[p]
+// (zero past N; a table entry outside the stage also gives zero).  TC_TF32X3:
+// tf32 hi / lo images split as tc_prep_kernel does, or the fp32 image when
+// img_lo is null.  TC_F16: the fp16 image.
+__global__ void tc_image_kernel(int kind, const void *W, void *img_hi, void *img_lo, const unsigned *table, int K,
+                                int N, long long total) {
+    const int BK = kind == TC_TF32X3 ? 32 : 64;
+    const int PER = kind == TC_TF32X3 ? 4096 : 8192;   // elements per 16 KB stage
+    const int KB = K / BK;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long st = i / PER;
+        const unsigned e = table[(int)(i - st * PER)];
+        const int row = (int)(e >> 7), col = (int)(e & 127u);
+        const int t = (int)(st / KB), kb = (int)(st - (long long)t * KB);
+        const int k = kb * BK + row, n = t * kTcTileF + col;
+        const bool in = row < BK && n < N;
+        if (kind == TC_TF32X3) {
+            const float x = in ? reinterpret_cast<const float *>(W)[(size_t)k * N + n] : 0.0f;
+            if (img_lo) {
+                unsigned u;
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));
+                const float h = __uint_as_float(u);
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x - h));
+                reinterpret_cast<float *>(img_hi)[i] = h;
+                reinterpret_cast<float *>(img_lo)[i] = __uint_as_float(u);
+            } else {
+                reinterpret_cast<float *>(img_hi)[i] = x;
+            }
+        } else {
+            reinterpret_cast<__half *>(img_hi)[i] =
+                in ? reinterpret_cast<const __half *>(W)[(size_t)k * N + n] : __float2half_rn(0.0f);
+        }
+    }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -568,6 +700,38 @@ TcPlan plan(int R, int N, int kb_total, int sms) {
     return p;
 }
 
+// Balanced split (SplitInfo) for R rows of an N-output projection over
+// kb_total K blocks: when the rows fit one tile height and the 128-feature
+// tiles are fewer than the SMs, the tiles' K blocks are shared out equally
+// over min(sms, U / 2) CTAs (at least two K blocks each), so that every SM
+// streams weights; each share then spans at most two tiles.  Uniform splits
+// of each tile leave SMs idle whenever tiles x splits misses the SM count
+// (76 to 104 of 148 CTAs on the 32-row GEMMs of GPT-2 XL).  Measured on
+// B200: the balanced GEMMs' main loops are up to twice as short, but the
+// extra partials (up to 13 per column) cost their consumers (the attention's
+// c_attn sum, the LayerNorm-fused reduces) about as much: c5 +0.6%, c4 -6%.
+// So it is off unless G2_TC_BALANCED sets the largest row count that uses it.
+SplitInfo balanced_plan(int R, int N, int kb_total, int bn, int sms) {
+    static const int max_rows = getenv("G2_TC_BALANCED") ? atoi(getenv("G2_TC_BALANCED")) : 0;
+    SplitInfo si;
+    const int tiles = (N + kTcTileF - 1) / kTcTileF;
+    const long long U = (long long)tiles * kb_total;
+    if (R > max_rows || R > bn || N % 4 || tiles >= sms || kb_total < 2) return si;
+    const int G = (int)(U / 2 < sms ? U / 2 : sms);
+    if (G <= tiles) return si;
+    si.G = G;
+    si.KB = kb_total;
+    si.U = U;
+    return si;
+}
+// The most partials any output column of the plan has.
+int max_partials(const SplitInfo &si, int N) {
+    int m = si.splits;
+    if (si.G)
+        for (int n = 0; n < N; n += kTcTileF) m = std::max(m, si.at(n));
+    return m;
+}
+
 template <int KIND, int BN, typename WT, bool AK>
 void launch_kernel(const TcWeights &w, const TcRowsOperand &x, int bn_idx, const TcArgs<WT> &a, cudaStream_t st) {
     using C = TcCfg<KIND, BN>;
@@ -580,7 +744,7 @@ void launch_kernel(const TcWeights &w, const TcRowsOperand &x, int bn_idx, const
     } else if (dev >= 64) {
         cudaFuncSetAttribute(tc_gemm_kernel<KIND, BN, WT, AK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     }
-    dim3 grid((a.N + kTcTileF - 1) / kTcTileF, (a.R + BN - 1) / BN, a.splits);
+    const dim3 grid = a.si.G ? dim3((unsigned)a.si.G) : dim3((a.N + kTcTileF - 1) / kTcTileF, (a.R + BN - 1) / BN, a.splits);
     launch_pdl(tc_gemm_kernel<KIND, BN, WT, AK>, grid, dim3(kThreads), C::SMEM, st, w.hi, KIND == TC_TF32X3 ? w.lo : w.hi,
                x.hi[bn_idx], KIND == TC_TF32X3 ? x.lo[bn_idx] : x.hi[bn_idx], a);
 }
@@ -615,6 +779,61 @@ int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, in
     if (!rc && t && lo) rc = tc_encode(&w->lo, dt, lo, N, K, bf, bk, t);
     else w->lo = w->hi;
     return rc;
+}
+
+int tc_stage_perm(int kind, void *idx, unsigned *table, int *err, cudaStream_t st) {
+    // The table depends only on the weight kind: it is recorded once per process
+    // and kind, checked on the host to be a permutation of the stage's elements,
+    // and uploaded for every later engine.
+    static std::mutex mu;
+    static std::vector<unsigned> cached[2];
+    const bool t = kind == TC_TF32X3;
+    const int BK = t ? 32 : 64, n = BK * kTcTileF;   // one stage: BK rows x 128 features
+    std::lock_guard<std::mutex> lk(mu);
+    std::vector<unsigned> &c = cached[t ? 1 : 0];
+    if (c.empty()) {
+        tc_iota_kernel<<<(n + 255) / 256, 256, 0, st>>>(t ? reinterpret_cast<unsigned *>(idx) : nullptr,
+                                                        t ? nullptr : reinterpret_cast<unsigned short *>(idx), n);
+        CUtensorMap m;
+        const int rc = tc_encode(&m, t ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, idx, kTcTileF,
+                                 BK, t ? 32 : 64, BK, t);
+        if (rc) return rc;
+        const size_t smem = 16384 + 1024 + 64;
+        if (t) {
+            cudaFuncSetAttribute(tc_perm_kernel<TC_TF32X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            tc_perm_kernel<TC_TF32X3><<<1, 256, smem, st>>>(m, table, err);
+        } else {
+            cudaFuncSetAttribute(tc_perm_kernel<TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            tc_perm_kernel<TC_F16><<<1, 256, smem, st>>>(m, table, err);
+        }
+        std::vector<unsigned> h(n);
+        int e = 0;
+        if (cudaMemcpyAsync(h.data(), table, sizeof(unsigned) * n, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(&e, err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess || e)
+            return G2_ERR_CUDA;
+        std::vector<char> seen(n, 0);
+        for (unsigned v : h) {
+            if (v >= (unsigned)n || seen[v]) return G2_ERR_CUDA;   // not a permutation
+            seen[v] = 1;
+        }
+        c = h;
+        return G2_OK;
+    }
+    return cudaMemcpyAsync(table, c.data(), sizeof(unsigned) * n, cudaMemcpyHostToDevice, st) == cudaSuccess ? G2_OK
+                                                                                                          : G2_ERR_CUDA;
+}
+
+size_t tc_image_elems(int kind, int K, int N) {
+    (void)kind;
+    return (size_t)((N + kTcTileF - 1) / kTcTileF) * kTcTileF * K;
+}
+
+void launch_tc_image(int kind, const void *W, void *img_hi, void *img_lo, const unsigned *table, int K, int N,
+                     cudaStream_t st) {
+    const long long total = (long long)tc_image_elems(kind, K, N);
+    const int blocks = (int)((total + 255) / 256 < 8192 ? (total + 255) / 256 : 8192);
+    tc_image_kernel<<<blocks, 256, 0, st>>>(kind, W, img_hi, img_lo, table, K, N, total);
 }
 
 int tc_weights_kmajor(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N) {
@@ -660,7 +879,8 @@ size_t tc_partial_floats(int R_max, int N, int K, int kind, int sms) {
     size_t m = 0;
     for (int R = 1; R <= R_max; ++R) {
         const TcPlan p = plan(R, N, kb_total, sms);
-        const size_t f = (size_t)p.splits * R * N;
+        const SplitInfo si = balanced_plan(R, N, kb_total, p.bn, sms);
+        const size_t f = (size_t)(si.G ? max_partials(si, N) : p.splits) * R * N;
         m = f > m ? f : m;
     }
     return m;
@@ -671,7 +891,7 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
                    unsigned *tile_ctr, int *err, const WT *bias, const float *resid, float *out, int epi,
                    const KVLayout *kv, int layer, Rows rows, int sms, cudaStream_t st, OperandOut op, int out_stride,
                    const WT *ln_g, const WT *ln_b, OperandOut ln_op, bool *ln_done, bool defer_reduce,
-                   int *splits_out) {
+                   SplitInfo *si_out) {
     const int bk = kind == TC_TF32X3 ? 32 : 64;
     const int kb_total = w.K / bk;
     TcPlan p = plan(R, w.N, kb_total, sms);
@@ -707,9 +927,16 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
     a.kb_total = kb_total;
     a.kb_per = p.kb_per;
     a.splits = p.splits;
+    a.si.splits = p.splits;
+    if (!w.kmajor) {   // the balanced split, where it applies and its partials fit the scratch
+        const SplitInfo si = balanced_plan(R, w.N, kb_total, p.bn, sms);
+        if (si.G && (size_t)max_partials(si, w.N) * R * w.N <= partial_floats) a.si = si;
+    }
     a.part = partial;
     a.err = err;
     a.wsplit = w.wsplit ? 1 : 0;
+    a.img_hi = w.kmajor ? nullptr : reinterpret_cast<const unsigned char *>(w.img_hi);
+    a.img_lo = w.kmajor ? nullptr : reinterpret_cast<const unsigned char *>(w.img_lo);
     (void)tile_ctr;
     a.e.bias = bias;
     a.e.resid = resid;
@@ -743,17 +970,17 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
         else launch_kernel<TC_F16, 128, WT, false>(w, x, bi, a, st);
     }
     if (ln_done) *ln_done = false;
-    if (splits_out) *splits_out = p.splits;
-    if (p.splits == 1) return 1;   // the GEMM applied the epilogue itself
+    if (si_out) *si_out = a.si;
+    if (!a.si.split()) return 1;   // the GEMM applied the epilogue itself
     if (defer_reduce) return 1;    // the consumer sums the partials
     if (ln_g && w.N <= 2048 && (w.N % 4) == 0) {   // sum the splits, epilogue and the next LayerNorm in one kernel
-        launch_pdl(tc_reduce_ln_kernel<WT>, dim3((unsigned)R), dim3(256), 0, st, (const float *)partial, p.splits, R, w.N,
+        launch_pdl(tc_reduce_ln_kernel<WT>, dim3((unsigned)R), dim3(256), 0, st, (const float *)partial, a.si, R, w.N,
                    a.e, ln_g, ln_b, ln_op);
         if (ln_done) *ln_done = true;
         return 2;
     }
     const long long n4 = (long long)R * w.N / 4;
-    launch_pdl(tc_reduce_kernel<WT>, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, st, (const float *)partial, p.splits,
+    launch_pdl(tc_reduce_kernel<WT>, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, st, (const float *)partial, a.si,
                R, w.N, a.e, op);
     return 2;
 }
@@ -761,11 +988,11 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
 template int launch_tc_gemm<float>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, unsigned *,
                                    int *, const float *, const float *, float *, int, const KVLayout *, int, Rows, int,
                                    cudaStream_t, OperandOut, int, const float *, const float *, OperandOut, bool *, bool,
-                                   int *);
+                                   SplitInfo *);
 template int launch_tc_gemm<__half>(int, const TcWeights &, const TcRowsOperand &, int, float *, size_t, unsigned *,
                                     int *, const __half *, const float *, float *, int, const KVLayout *, int, Rows, int,
                                     cudaStream_t, OperandOut, int, const __half *, const __half *, OperandOut, bool *,
-                                    bool, int *);
+                                    bool, SplitInfo *);
 
 #ifdef G2_CHECK
 int check_flag_tc() {

@@ -32,13 +32,34 @@ int tc_encode(CUtensorMap *map, CUtensorMapDataType dt, const void *base, unsign
 // Weight operand of one projection W [K][N]: tensor maps of its tf32 hi and lo
 // copies (TC_TF32X3), or with lo == nullptr of the fp32 weights themselves,
 // split in the kernel (wsplit), or of the fp16 weights (TC_F16, lo unused).
+// img_hi / img_lo (optional, [K][N] weights only): the weights as stage
+// images, the exact shared-memory bytes of one ring stage's weight tile for
+// tile t and K block kb at ((t * K / BK) + kb) * 16 KB, so that one bulk copy
+// fills a stage (four to eight tiled TMA boxes otherwise; a ring CTA then
+// streams about twice the bytes per second).  With wsplit, img_hi is the fp32
+// image, split in shared memory; otherwise the tf32 hi / lo images (or the
+// fp16 image).
 struct TcWeights {
     CUtensorMap hi, lo;
     int K, N;
     bool kmajor;   // false: [K][N] (Conv1D, feature-contiguous); true: [N][K] (rows of wte)
-    bool wsplit;   // TC_TF32X3 with the fp32 weights in `hi`
+    bool wsplit;   // TC_TF32X3 with the fp32 weights in `hi` (or the fp32 image)
+    const void *img_hi = nullptr, *img_lo = nullptr;
 };
 int tc_weights(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N);
+
+// Stage images.  tc_stage_perm records, on the device, where a tiled TMA load
+// of one stage's weight boxes puts each element: table[p] = row * 128 +
+// feature of the element at element position p of the stage (4096 fp32 or
+// 8192 fp16 positions), found by loading a tensor whose elements hold their
+// own coordinates (idx: 16 KB of device scratch, 16-byte aligned).
+// tc_image_elems is the size of one projection's image in elements;
+// launch_tc_image gathers W [K][N] into it (features past N zero), as tf32
+// hi / lo (TC_TF32X3 with img_lo), fp32 (img_lo == nullptr) or fp16.
+int tc_stage_perm(int kind, void *idx, unsigned *table, int *err, cudaStream_t st);
+size_t tc_image_elems(int kind, int K, int N);
+void launch_tc_image(int kind, const void *W, void *img_hi, void *img_lo, const unsigned *table, int K, int N,
+                     cudaStream_t st);
 // The same for a [N][K] row-major weight (K-contiguous), e.g. the tied LM head wte.
 int tc_weights_kmajor(TcWeights *w, int kind, const void *hi, const void *lo, int K, int N);
 
@@ -72,14 +93,14 @@ constexpr int kTcMaxTiles = 4096;
 // writes it as ln_op, the next GEMM's operand; *ln_done then says whether it
 // did (a single-split GEMM does not: its caller runs the LayerNorm).  With
 // defer_reduce a split-K GEMM leaves its partial tiles in `partial` for the
-// consumer to sum; *splits_out receives the split count (1: the GEMM applied
-// the epilogue itself).  `err` receives an
-// error code if a wait inside the kernel expires.  Returns the launch count.
+// consumer to sum; *si_out receives where the partials are (si_out->split()
+// false: the GEMM applied the epilogue itself).  `err` receives an error code
+// if a wait inside the kernel expires.  Returns the launch count.
 template <typename WT>
 int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, float *partial, size_t partial_floats,
                    unsigned *tile_ctr, int *err, const WT *bias, const float *resid, float *out, int epi,
                    const KVLayout *kv, int layer, Rows rows, int sms, cudaStream_t st, OperandOut op = OperandOut(),
                    int out_stride = 0, const WT *ln_g = nullptr, const WT *ln_b = nullptr, OperandOut ln_op = OperandOut(),
-                   bool *ln_done = nullptr, bool defer_reduce = false, int *splits_out = nullptr);
+                   bool *ln_done = nullptr, bool defer_reduce = false, SplitInfo *si_out = nullptr);
 
 }  // namespace g2

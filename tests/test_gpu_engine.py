@@ -298,3 +298,26 @@ def test_generation_across_launch_chunks(g2, tiny_affine_model):
     with g2.Engine(tiny_affine_model) as eng:
         got = eng.generate(prompt, 300)
     assert list(got) == list(want)
+
+
+def test_engines_in_sequence_agree(g2, tiny_affine_model, small_model):
+    """Engines opened one after another in one process compute the same thing.
+    Regression test: buffers are zeroed at open on the legacy default stream,
+    which the engine's non-blocking stream does not wait for; the zeroing must
+    be complete before that stream writes the buffers (it once landed after
+    the tensor-core weight images' position table was written, so that every
+    engine after the first in a process computed garbage)."""
+    prompt = synth.prompt_ids(3, 64)
+    with g2.Engine(tiny_affine_model) as eng:
+        eng.prefill(prompt[:16])
+    out = []
+    for _ in range(2):
+        with g2.Engine(small_model) as eng:
+            eng.prefill(prompt)
+            out.append(eng.logits())
+    ref = oracle.RefModel(small_model)
+    ref.prefill(prompt)
+    want = ref.logits()
+    ref.close()
+    assert rel(out[0], want) <= FP32_TOL
+    assert np.array_equal(out[0], out[1])

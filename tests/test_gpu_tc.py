@@ -10,6 +10,10 @@ Tolerances, max|gpu - ref| <= RTOL * max|ref|:
 Shapes cover partial feature tiles (N % 128 != 0), partial row tiles, a single
 row, split-K and the GPT-2 small / medium / XL projection shapes.
 """
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
@@ -57,7 +61,7 @@ def rel_err(got, want):
 
 
 SHAPES = [(64, 2304, 768), (64, 768, 3072), (5, 384, 128), (1, 256, 64), (33, 200, 64), (130, 4800, 1600),
-          (512, 3072, 768), (256, 1024, 4096)]
+          (512, 3072, 768), (256, 1024, 4096), (32, 4800, 1600), (32, 1024, 4096)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -99,3 +103,14 @@ def test_matmul_tc_rejects_bad_shapes(g2):
         g2.matmul_tc(A, B, C_, 4, 64, 96, workspace=ws, workspace_bytes=4 << 20)
     with pytest.raises(g2.G2Error):   # workspace too small
         g2.matmul_tc(A, B, C_, 4, 64, 64, workspace=ws, workspace_bytes=64)
+
+
+def test_matmul_tc_balanced_split(g2):
+    """The balanced split (G2_TC_BALANCED: the K blocks of all tiles shared out
+    equally over the SMs, a CTA's share spanning up to two tiles) is off by
+    default; the same cases are run again in a process where it applies to
+    every GEMM of up to 32 rows."""
+    env = dict(os.environ, G2_TC_BALANCED="32")
+    r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-x", "-p", "no:cacheprovider", "-k",
+                        "test_matmul_tc and not balanced"], env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
