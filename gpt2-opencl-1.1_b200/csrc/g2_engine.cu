@@ -954,6 +954,7 @@ static int forward_rows(g2_engine *e, int nrows, int max_pos, bool decode_rows =
             if (si.split()) {
                 qp.part = e->tc_part;
                 qp.si = si;
+                qp.err = e->tc_err;
                 qp.bias = e->w<WT>(o.qkv_b);
             }
         } else {

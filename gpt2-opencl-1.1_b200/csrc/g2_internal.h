@@ -178,6 +178,7 @@ struct QkvPartials {
     const float *part = nullptr;
     SplitInfo si;
     const void *bias = nullptr;   // [3E] of the engine's weight type
+    int *err = nullptr;           // where an expired wait of the streamed attention is recorded
 };
 
 template <typename KT>

@@ -26,6 +26,7 @@
 #include <climits>
 
 #include "g2_device.cuh"
+#include "gpt2b200.h"
 
 namespace g2 {
 
@@ -373,6 +374,7 @@ struct AttnArgs {
     SplitInfo qsi;       // partials per column
     long long qtotal;    // rows * qkv_stride
     const KT *qbias;     // c_attn bias [3E]
+    int *err;            // attn_stream_kernel: G2_ERR_TIMEOUT if a wait expired
 };
 
 template <typename KT>
@@ -554,6 +556,349 @@ __global__ void __launch_bounds__(128, sizeof(KT) == 4 ? 3 : 4) attn_kernel(Attn
         put_operand(a.op, o, O / L);
     }
     if (tid == 0) *ctr = 0u;
+}
+
+// ------------------------------------------------------------------------------
+// Single-query attention of a batched decode step, streamed (attn_scores_1q,
+// attn_softmax_1q, attn_out_1q, math.cl:388-476, for one token of each of R
+// sequences), used when the attention sums c_attn's split-K partials itself.
+//
+// The work items are (row, head, 128-key chunk), row-major then head-major.
+// CTA c of G takes items [c I / G, (c + 1) I / G), so every SM streams about the
+// same number of K and V bytes.  A CTA stages its items' K and V chunks in a
+// two-stage shared-memory ring with one bulk copy each (the rows are
+// contiguous), computes each chunk from shared memory and merges consecutive
+// chunks of one (row, head) with the online softmax.  A (row, head) whose
+// chunks span several CTAs is finished by the last of them to arrive (partials
+// in slice order, as attn_kernel does).  The first stages are requested before
+// the wait for the previous kernel: the cached K and V rows before the step's
+// position were written by earlier steps, and the row at the position comes from
+// the summed c_attn partials, not from the cache.  Every wait is bounded; on
+// expiry the CTA records G2_ERR_TIMEOUT in a.err, waits (bounded) for its own
+// copies in flight and returns.
+// ------------------------------------------------------------------------------
+namespace {
+constexpr int kAsThreads = 256;
+constexpr int kAsStages = 2;
+constexpr int kAsMaxRows = 256;        // rows (sequences) one launch may take
+typedef unsigned long long u64a;
+__device__ __forceinline__ unsigned as_smem(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ u64a as_time() {
+    u64a t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool as_try(u64a *b, unsigned par) {
+    unsigned ok;
+    asm volatile("{ .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok)
+                 : "r"(as_smem(b)), "r"(par)
+                 : "memory");
+    return ok != 0;
+}
+// Wait for phase `par` of b for at most 1 s.
+__device__ __forceinline__ bool as_wait(u64a *b, unsigned par) {
+    if (as_try(b, par)) return true;
+    const u64a lim = as_time() + 1000000000ull;
+    for (;;) {
+        if (as_try(b, par)) return true;
+        if (as_time() > lim) return false;
+    }
+}
+__device__ __forceinline__ void as_bulk(void *dst, const void *src, unsigned bytes, u64a *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     as_smem(dst)),
+                 "l"(src), "r"(bytes), "r"(as_smem(bar))
+                 : "memory");
+}
+}  // namespace
+
+// Keys per item: 128 for fp16 caches, 64 for fp32 (a two-stage ring of 32 KB
+// stages either way, so that three CTAs share an SM).
+template <typename KT>
+__host__ __device__ constexpr int as_chunk() {
+    return sizeof(KT) == 2 ? 128 : 64;
+}
+size_t attn_stream_smem(int elem) { return (size_t)kAsStages * 2 * (elem == 2 ? 128 : 64) * kHeadDim * elem; }
+
+template <typename KT>
+__global__ void __launch_bounds__(kAsThreads, 3) attn_stream_kernel(AttnArgs<KT> a, int nrows) {
+    constexpr int CH = as_chunk<KT>();               // keys per item
+    constexpr int NW = kAsThreads / 32;              // warps
+    constexpr int KPW = CH / NW;                     // keys per warp: 16 (fp16) or 8 (fp32)
+    constexpr int TPK = 32 / KPW;                    // threads per key in the score pass: 2 or 4
+    constexpr int EPC = 16 / sizeof(KT);             // elements per 16-byte chunk of a key row
+    constexpr int CB = CH * kHeadDim * sizeof(KT);   // bytes of a full K (or V) chunk
+    static_assert(kHeadDim * sizeof(KT) == TPK * 64, "each thread of a key reads four 16-byte chunks");
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char *ring = smem_raw;                  // [stage][K chunk, V chunk]
+    __shared__ u64a full[kAsStages];
+    __shared__ float q[kHeadDim];
+    __shared__ float wo[NW][kHeadDim], wm[NW], wl[NW];   // per-warp partial (o, max, sum)
+    __shared__ float knew[2][kHeadDim];
+    __shared__ int nch[kAsMaxRows], off[kAsMaxRows + 1], rpos[kAsMaxRows], rslot[kAsMaxRows];
+    __shared__ int s_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, NH = a.kv.n_head;
+    if (tid == 0) {
+        for (int s = 0; s < kAsStages; ++s)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(as_smem(&full[s])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // items per row (chunks of its keys, per head), their prefix sums, positions and slots
+    for (int r = tid; r < nrows; r += kAsThreads) {
+        const int T = a.rows.pos[r] + 1, sl = a.rows.slot[r];
+        const bool ok = G2_BOUNDS(T >= 1 && T <= a.kv.max_seq && sl >= 0 && sl < a.kv.n_slots, 107);
+        nch[r] = ok ? (T + CH - 1) / CH : 0;
+        rpos[r] = T - 1;
+        rslot[r] = sl;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        off[0] = 0;
+        for (int r = 0; r < nrows; ++r) off[r + 1] = off[r] + NH * nch[r];
+    }
+    __syncthreads();
+    // the items are shared over G = min(grid, I) CTAs, so that every CTA of the
+    // partition holds at least one (the part counts of the merge rely on it)
+    const long long I = off[nrows];
+    const int G = (int)(I < (long long)gridDim.x ? I : (long long)gridDim.x), c = blockIdx.x;
+    const int i0 = c < G ? (int)((long long)c * I / G) : 0, i1 = c < G ? (int)((long long)(c + 1) * I / G) : 0;
+    // A cursor over (row, head, chunk): placed by one scan, then advanced in O(1).
+    struct Cur {
+        int r, h, ch;
+    };
+    auto place = [&](int i) {
+        Cur u;
+        u.r = 0;
+        while (off[u.r + 1] <= i) ++u.r;
+        const int j = i - off[u.r];
+        u.h = j / nch[u.r];
+        u.ch = j - u.h * nch[u.r];
+        return u;
+    };
+    auto next = [&](Cur &u) {
+        if (++u.ch == nch[u.r]) {
+            u.ch = 0;
+            if (++u.h == NH) {
+                u.h = 0;
+                do ++u.r;
+                while (u.r < nrows && nch[u.r] == 0);
+            }
+        }
+    };
+    auto kv_base = [&](int r, int h) -> long long {
+        return (long long)rslot[r] * a.kv.slot_stride + (long long)a.layer * a.kv.layer_stride +
+               (long long)h * a.kv.max_seq * kHeadDim;
+    };
+    // thread 0: request item (cursor u, index i)'s K and V rows into stage (i - i0) % kAsStages
+    auto issue = [&](const Cur &u, int i) {
+        const int T = rpos[u.r] + 1, j0 = u.ch * CH, nj = min(CH, T - j0);
+        const unsigned bytes = (unsigned)(nj * kHeadDim * sizeof(KT));
+        const int s = (i - i0) % kAsStages;
+        u64a *bar = &full[s];
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(as_smem(bar)), "r"(2 * bytes)
+                     : "memory");
+        const long long b = kv_base(u.r, u.h) + (long long)j0 * kHeadDim;
+        as_bulk(ring + (size_t)s * 2 * CB, reinterpret_cast<const KT *>(a.kv.k) + b, bytes, bar);
+        as_bulk(ring + (size_t)s * 2 * CB + CB, reinterpret_cast<const KT *>(a.kv.v) + b, bytes, bar);
+    };
+    Cur iu{0, 0, 0};   // thread 0's issue cursor
+    if (tid == 0 && i0 < i1) {
+        iu = place(i0);
+        for (int i = i0; i < i1 && i < i0 + kAsStages; ++i) {
+            issue(iu, i);
+            next(iu);
+        }
+    }
+    pdl_wait();
+    pdl_launch();
+    const int E = a.qkv_stride / 3;
+    // score pass: lane (kl, part) of warp w takes key w KPW + kl, 16-byte chunks 4 part .. 4 part + 3
+    // of its row, read in an order rotated by the key (bank-conflict free); q in that order in registers
+    const int kl = lane / TPK, part = lane % TPK;
+    int rot[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) rot[t] = part * 4 + ((t + kl + (TPK == 4 && part >= 2 ? 2 : 0)) & 3);
+    float qr[4][EPC];
+    float Mr = -FLT_MAX, Lr = 0.0f, acc = 0.0f;      // running softmax of the current (row, head), threads < 64
+    Cur u{0, 0, 0};
+    if (i0 < i1) u = place(i0);
+    for (int i = i0; i < i1; ++i, next(u)) {
+        const int r = u.r, h = u.h, ch = u.ch;
+        const int T = rpos[r] + 1, pos = T - 1, j0 = ch * CH, nj = min(CH, T - j0);
+        const int s = (i - i0) % kAsStages;
+        const bool fresh = i == i0 || ch == 0;       // a new (row, head) run of this CTA
+        if (fresh) {
+            Mr = -FLT_MAX;
+            Lr = 0.0f;
+            acc = 0.0f;
+        }
+        {   // q at a run's start, and at the chunk with pos also k and v (appended), from c_attn's partials
+            const bool kv_here = ch == nch[r] - 1;
+            for (int cc = tid; cc < 3 * kHeadDim; cc += kAsThreads) {
+                const int pt = cc / kHeadDim, d = cc % kHeadDim;
+                if (pt == 0 ? !fresh : !kv_here) continue;
+                const size_t col = (size_t)pt * E + h * kHeadDim + d;
+                const float *pc = a.qpart + (size_t)r * a.qkv_stride + col;
+                const int ns = a.qsi.at((int)col);
+                float sum = 0.0f;
+                for (int s0 = 0; s0 < ns; s0 += 8) {   // loads issued eight at a time, summed in split order
+                    float pv[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) pv[k] = s0 + k < ns ? pc[(size_t)(s0 + k) * a.qtotal] : 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (s0 + k < ns) sum = s0 + k == 0 ? pv[0] : sum + pv[k];
+                }
+                const float v = sum + tof(a.qbias[col]);
+                if (pt == 0) {
+                    q[d] = v * 0.125f;   // 1/sqrt(64)
+                } else {   // K / V append (split_kv, math.cl:367-383), kept at the cache's precision
+                    const KT stv = fromf<KT>(v);
+                    KT *dst = reinterpret_cast<KT *>(pt == 1 ? a.kv.k : a.kv.v) + kv_base(r, h) + (size_t)pos * kHeadDim + d;
+                    *dst = stv;
+                    knew[pt - 1][d] = tof(stv);
+                }
+            }
+        }
+        // this item's K and V in shared memory (bounded wait; a failure is carried by the barrier)
+        const int fail = as_wait(&full[s], (unsigned)(((i - i0) / kAsStages) & 1)) ? 0 : 1;
+        if (__syncthreads_or(fail)) {
+            if (tid == 0) {
+                atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
+                // copies this CTA issued and nobody consumed: wait for them (bounded) before exiting
+                for (int k = i + 1; k < i1 && k < i + kAsStages; ++k)
+                    as_wait(&full[(k - i0) % kAsStages], (unsigned)(((k - i0) / kAsStages) & 1));
+            }
+            return;
+        }
+        if (fresh) {
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+#pragma unroll
+                for (int e = 0; e < EPC; ++e) qr[t][e] = q[rot[t] * EPC + e];
+        }
+        const KT *Ks = reinterpret_cast<const KT *>(ring + (size_t)s * 2 * CB);
+        const KT *Vs = reinterpret_cast<const KT *>(ring + (size_t)s * 2 * CB + CB);
+        const int jpos = pos - j0;   // the key at pos (this step's), if in this chunk: from knew
+        const int j = warp * KPW + kl;
+        float sc = 0.0f;
+        if (j < nj) {
+            if (j == jpos) {
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+#pragma unroll
+                    for (int e = 0; e < EPC; ++e) sc = fmaf(knew[0][rot[t] * EPC + e], qr[t][e], sc);
+            } else {
+                const uint4 *kr = reinterpret_cast<const uint4 *>(Ks + (size_t)j * kHeadDim);
+                uint4 w[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) w[t] = kr[rot[t]];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) sc += dot_vec(w[t], qr[t], KT());
+            }
+        }
+#pragma unroll
+        for (int o = 1; o < TPK; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+        // the warp's softmax over its keys, then P.V: lane l takes dims 2 l, 2 l + 1
+        const float m = warp_max(j < nj ? sc : -FLT_MAX);
+        const float pj = j < nj ? expf(sc - m) : 0.0f;
+        const float l = warp_sum(part == 0 ? pj : 0.0f);
+        // every slot of the warp is read (rows past nj hold stale data: their weight
+        // and value are selected to 0, so nothing of them reaches the sums), so that
+        // the loop has no exit and its loads and shuffles are issued ahead
+        const int kmax = nj - warp * KPW;   // valid keys of this warp (may be <= 0)
+        float o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+        for (int k = 0; k < KPW; ++k) {
+            const int jj = warp * KPW + k;
+            const bool in = k < kmax;
+            const float ps = __shfl_sync(0xffffffffu, pj, k * TPK);
+            const float pk = in ? ps : 0.0f;
+            float2 f;
+            if (sizeof(KT) == 2)
+                f = __half22float2(reinterpret_cast<const __half2 *>(Vs + (size_t)jj * kHeadDim)[lane]);
+            else
+                f = reinterpret_cast<const float2 *>(Vs + (size_t)jj * kHeadDim)[lane];
+            if (jj == jpos) f = make_float2(knew[1][2 * lane], knew[1][2 * lane + 1]);
+            o0 = fmaf(pk, in ? f.x : 0.0f, o0);
+            o1 = fmaf(pk, in ? f.y : 0.0f, o1);
+        }
+        wo[warp][2 * lane] = o0;
+        wo[warp][2 * lane + 1] = o1;
+        if (lane == 0) {
+            wm[warp] = m;
+            wl[warp] = l;
+        }
+        __syncthreads();
+        // the stage is free again: request the item kAsStages ahead into it
+        if (tid == 0 && i + kAsStages < i1) {
+            issue(iu, i + kAsStages);
+            next(iu);
+        }
+        if (tid < kHeadDim) {   // the warps' partials merged in warp order, then into the run
+            float M = -FLT_MAX;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w]);
+            float lc = 0.0f, oc = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const float f = expf(wm[w] - M);   // 0 for a warp without keys
+                lc = fmaf(wl[w], f, lc);
+                oc = fmaf(wo[w][tid], f, oc);
+            }
+            const float Mn = fmaxf(Mr, M);
+            const float so = expf(Mr - Mn), sn = expf(M - Mn);   // so = 0 on a run's first chunk
+            acc = acc * so + oc * sn;
+            Lr = Lr * so + lc * sn;
+            Mr = Mn;
+        }
+        // the end of this (row, head) in this CTA: finish it, or hand in a partial
+        if (ch == nch[r] - 1 || i == i1 - 1) {
+            const long long u0 = off[r] + (long long)h * nch[r];     // the (row, head)'s first item
+            const int c0 = (int)(((u0 + 1) * G - 1) / I);            // CTAs holding its first and last items
+            const int c1 = (int)(((u0 + nch[r]) * G - 1) / I);
+            const int nparts = c1 - c0 + 1, seg = c - c0;
+            const size_t o = (size_t)r * a.out_stride + h * kHeadDim + tid;
+            if (nparts == 1) {
+                if (tid < kHeadDim) {
+                    a.out[o] = acc / Lr;
+                    put_operand(a.op, o, acc / Lr);
+                }
+            } else {
+                float *P = a.partial + (((size_t)r * NH + h) * a.max_splits + seg) * (kHeadDim + 2);
+                if (tid < kHeadDim) P[2 + tid] = acc;
+                if (tid == 0) {
+                    P[0] = Mr;
+                    P[1] = Lr;
+                }
+                __threadfence();
+                __syncthreads();
+                unsigned *ctr = a.counters + (size_t)r * NH + h;
+                if (tid == 0) s_last = (atomicAdd(ctr, 1u) == (unsigned)(nparts - 1));
+                __syncthreads();
+                if (s_last) {
+                    __threadfence();
+                    if (tid < kHeadDim) {
+                        const float *P0 = a.partial + ((size_t)r * NH + h) * a.max_splits * (kHeadDim + 2);
+                        float M = -FLT_MAX;
+                        for (int k = 0; k < nparts; ++k) M = fmaxf(M, __ldcg(P0 + (size_t)k * (kHeadDim + 2)));
+                        float L = 0.0f, O = 0.0f;
+                        for (int k = 0; k < nparts; ++k) {
+                            const float *Pk = P0 + (size_t)k * (kHeadDim + 2);
+                            const float w = expf(__ldcg(Pk) - M);
+                            L = fmaf(__ldcg(Pk + 1), w, L);
+                            O = fmaf(__ldcg(Pk + 2 + tid), w, O);
+                        }
+                        a.out[o] = O / L;
+                        put_operand(a.op, o, O / L);
+                    }
+                    if (tid == 0) *ctr = 0u;
+                }
+            }
+        }
+        __syncthreads();   // q, knew and the warp partials are reused by the next item
+    }
 }
 
 // ------------------------------------------------------------------------------
@@ -1020,7 +1365,7 @@ void launch_gemm_rows(const float *A, const WT *W, const WT *bias, const float *
 }
 
 size_t attn_partial_floats(int nrows, int n_head, int max_seq) {
-    const int ms = (max_seq + kAttnChunk - 1) / kAttnChunk;
+    const int ms = (max_seq + 63) / 64;   // the streamed kernel's 64-key chunks of fp32 caches
     return (size_t)nrows * n_head * ms * (kHeadDim + 2);
 }
 size_t attn_counter_count(int nrows, int n_head) { return (size_t)nrows * n_head; }
@@ -1045,6 +1390,29 @@ void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int 
     a.partial = partial;
     a.counters = counters;
     a.max_splits = (kv.max_seq + kAttnChunk - 1) / kAttnChunk;
+    a.err = qp.err;
+    if (qp.part && qp.err && nrows <= kAsMaxRows) {
+        // decode rows with c_attn's partials: the streamed kernel, as many CTAs as fit at once
+        static unsigned long long attr_set = 0;   // devices on which its shared-memory limit was raised
+        static int per_sm[64];
+        int dev = 0, sms = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const size_t smem = attn_stream_smem((int)sizeof(KT));
+        if (dev >= 64 || !(__atomic_load_n(&attr_set, __ATOMIC_ACQUIRE) >> dev & 1ull)) {
+            cudaFuncSetAttribute(attn_stream_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            int n = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_stream_kernel<KT>, kAsThreads, smem);
+            if (dev < 64) {
+                per_sm[dev] = n > 0 ? n : 1;
+                __atomic_fetch_or(&attr_set, 1ull << dev, __ATOMIC_RELEASE);
+            }
+        }
+        const int G = sms * (dev < 64 ? per_sm[dev] : 1);
+        a.max_splits = (kv.max_seq + as_chunk<KT>() - 1) / as_chunk<KT>();   // partial slots per (row, head)
+        launch_pdl(attn_stream_kernel<KT>, dim3((unsigned)G), dim3(kAsThreads), smem, st, a, nrows);
+        return;
+    }
     const int splits = max_pos_hint < 0 ? a.max_splits : (max_pos_hint + kAttnChunk) / kAttnChunk;
     dim3 grid(kv.n_head, splits, nrows);
     launch_pdl(attn_kernel<KT>, grid, dim3(128), 0, st, a);
