@@ -411,14 +411,25 @@ def measure(name, cfg, args, steps, warmup, ws, rank, local, dist, torch, g2, sy
                 tok, _ = eng.argmax(forbid_eos=True)
             loop_t += time.perf_counter() - t1
             loop_tokens += cfg["steps"]
+    # --lm-shard (c5 only): the same generation with the LM head split over the ranks by
+    # vocabulary rows (gpt2b200.lmshard), wall-clock with prefill, beside g2_generate_batch's
+    shard_t = 0.0
+    if getattr(args, "lm_shard", False) and name == "c5" and B > 1:
+        from gpt2b200 import lmshard
+        dev = torch.device("cuda", local if ws > 1 else 0)
+        lmshard.generate_batch_sharded(eng, prompts, n_new, dev)   # warm-up
+        for _ in range(reps):
+            t1 = time.perf_counter()
+            lmshard.generate_batch_sharded(eng, prompts, n_new, dev)
+            shard_t += time.perf_counter() - t1
     cfgd = eng.cfg
     elem = 2 if cfg["dtype"] == "f16" else 4
     per_seq_kv = kv_bytes(shape, elem, cfg["prompt"], cfg["steps"], 1)
     bytes_per_step = cfgd.weight_bytes + per_seq_kv * B / cfg["steps"] + B * (2 * shape.n_embd * elem + 4 * shape.padded_vocab)
     persistent = bool(cfgd.persistent) and B == 1
     eng.close()
-    dec_max, pre_max, wall_max, e2e_max, loop_max = replicas.max_over_ranks([dec_ms, pre_ms, wall, e2e_t, loop_t],
-                                                                           device="cuda")
+    dec_max, pre_max, wall_max, e2e_max, loop_max, shard_max = replicas.max_over_ranks(
+        [dec_ms, pre_ms, wall, e2e_t, loop_t, shard_t], device="cuda")
     n_total = cfg["batch"] * (ws if scaling == "weak" else 1)    # sequences over all ranks
     total_tokens = dec_steps * n_total
     value = total_tokens / (dec_max / 1000.0)
@@ -453,6 +464,11 @@ def measure(name, cfg, args, steps, warmup, ws, rank, local, dist, torch, g2, sy
                             "path": "g2_prefill + per-token g2_decode/g2_argmax (the reference's host loop)"}
                            if loop_max > 0 else None)},
         gpu_launches=int(launches) * ws, wall_s=round(wall_max, 4))
+    if shard_max > 0:
+        m["lm_shard"] = {"e2e": round(cfg["steps"] * n_total / shard_max * reps, 3), "unit": "tok/s",
+                         "unsplit_e2e": m["e2e"]["value"],
+                         "path": f"LM head split by vocabulary rows over {ws} GPU(s) (gpt2b200.lmshard: NCCL "
+                                 "all-gather of rows and of per-row bests), wall-clock, prefill included"}
     if clk:
         m["clocks"] = clk
     return m
@@ -520,6 +536,8 @@ def main():
     ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["c2"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--lm-shard", action="store_true",
+                    help="also time c5 with the LM head split over the GPUs by vocabulary rows")
     ap.add_argument("--no-batched", dest="batched", action="store_false",
                     help="skip the batched sub-object (c4 and c5 on the same GPUs)")
     ap.add_argument("--decode-steps", type=int, default=0,

@@ -172,6 +172,11 @@ struct g2_engine {
     int *h_ctx = nullptr;           // pinned staging of the context ids
     std::vector<TcWeights> tc_maps;           // [L][4]: qkv, proj, fc, fc2
     TcWeights tc_lm{};                        // the tied LM head: wte [V][E] as a K-major operand
+    // LM head over one range of vocabulary rows (g2_lm_head_rows): its operand map and logits
+    TcWeights tc_lm_shard{};
+    int shard_v0 = -1, shard_v1 = -1;
+    float *shard_logits = nullptr;            // [rows][stride] of the last g2_lm_head_rows
+    size_t shard_cap = 0;                     // floats shard_logits holds
     TcRowsOperand tc_x_e{}, tc_x_f{};         // input rows with K = E (tc_x*) and K = F (tc_x2*)
 
     template <typename WT>
@@ -201,7 +206,7 @@ static void free_engine(g2_engine *e) {
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
     for (auto &kv : e->prefill_graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    void *dev_ptrs[] = {e->sample_work, e->sample_ctx, e->tc_w, e->tc_lm_w, e->tc_img, e->tc_idx, e->tc_perm, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
+    void *dev_ptrs[] = {e->shard_logits, e->sample_work, e->sample_ctx, e->tc_w, e->tc_lm_w, e->tc_img, e->tc_idx, e->tc_perm, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
                         e->t_best, e->t_att, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
                         e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
@@ -1330,6 +1335,111 @@ extern "C" int g2_decode_batch(g2_engine *e, int n, const int *slots, const int 
     for (int i = 0; i < n; ++i) e->filled[slots[i]] = pos[i] + 1;
     e->result_slot = -1;
     return G2_OK;
+}
+
+// ------------------------------------------------------------------------------
+// LM head split by vocabulary rows (the optional column-sharded XL head): the
+// layers of a batched step without their LM head, and the LM head over one
+// range of wte rows for any set of normalised rows.  Several GPUs each take a
+// range and exchange the per-row best (gpt2b200.lmshard).
+// ------------------------------------------------------------------------------
+extern "C" int g2_decode_batch_rows(g2_engine *e, int n, const int *slots, const int *tokens, const int *pos,
+                                    float *rows) {
+    NvtxRange nvtx_range("g2_decode_batch_rows");
+    if (!e || !slots || !tokens || !pos || !rows) return set_err(G2_ERR_ARG, "g2_decode_batch_rows: null argument");
+    if (((uintptr_t)rows) & 15) return set_err(G2_ERR_ARG, "g2_decode_batch_rows: rows not 16-byte aligned");
+    if (n < 1 || n > e->max_batch) return set_err(G2_ERR_RANGE, "batch %d out of range [1,%d]", n, e->max_batch);
+    int rc, maxp = 0;
+    std::vector<int> seen(e->max_batch, 0);
+    for (int i = 0; i < n; ++i) {
+        if ((rc = check_slot(e, slots[i]))) return rc;
+        if (seen[slots[i]]++) return set_err(G2_ERR_ARG, "slot %d repeated in batch", slots[i]);
+        if (pos[i] < 0 || pos[i] >= e->c.n_ctx) return set_err(G2_ERR_RANGE, "position %d out of range", pos[i]);
+        if (pos[i] > e->filled[slots[i]]) return set_err(G2_ERR_STATE, "slot %d: position %d beyond %d filled", slots[i], pos[i], e->filled[slots[i]]);
+        maxp = std::max(maxp, pos[i]);
+    }
+    if ((rc = check_ids(e, tokens, n))) return rc;
+    CK(cudaSetDevice(e->device));
+    if ((rc = stage_rows(e, n, tokens, pos, slots))) return rc;
+    const ModelConfig &c = e->c;
+    // the residual stream after the last layer, then ln_f (math.cl:283-311) into the caller's rows
+    if (e->dtype == G2_F32) {
+        if ((rc = forward_rows<float>(e, n, maxp, true))) return rc;
+        launch_layernorm<float>(e->h, rows, e->w<float>(e->lnf_g), e->w<float>(e->lnf_b), c.n_embd, n, e->st);
+    } else {
+        if ((rc = forward_rows<__half>(e, n, maxp, true))) return rc;
+        launch_layernorm<__half>(e->h, rows, e->w<__half>(e->lnf_g), e->w<__half>(e->lnf_b), c.n_embd, n, e->st);
+    }
+    e->launches += 1;
+    CKL();
+    for (int i = 0; i < n; ++i) e->filled[slots[i]] = pos[i] + 1;
+    e->result_slot = -1;
+    CK(cudaStreamSynchronize(e->st));   // the caller's collectives run on another stream
+    return check_mega_err(e);
+}
+
+extern "C" int g2_lm_head_rows(g2_engine *e, int nrows, const float *rows, int v0, int v1, float *best_value,
+                               int *best_index) {
+    NvtxRange nvtx_range("g2_lm_head_rows");
+    if (!e || !rows || !best_value || !best_index) return set_err(G2_ERR_ARG, "g2_lm_head_rows: null argument");
+    const ModelConfig &c = e->c;
+    const int E = c.n_embd;
+    if (nrows < 1 || nrows > e->R) return set_err(G2_ERR_RANGE, "g2_lm_head_rows: %d rows (at most %d)", nrows, e->R);
+    if (v0 < 0 || v1 <= v0 || v1 > c.vocab_size || v0 % 4)
+        return set_err(G2_ERR_RANGE, "g2_lm_head_rows: rows [%d, %d) of %d (v0 a multiple of 4)", v0, v1, c.vocab_size);
+    if (((uintptr_t)rows) & 15) return set_err(G2_ERR_ARG, "g2_lm_head_rows: rows not 16-byte aligned");
+    CK(cudaSetDevice(e->device));
+    const int W = v1 - v0, Ws = (W + 3) / 4 * 4;   // logits row stride: whole float4s for the argmax
+    if ((size_t)nrows * Ws > e->shard_cap) {
+        if (e->shard_logits) cudaFree(e->shard_logits);
+        e->shard_logits = nullptr;
+        e->shard_cap = 0;
+        int rc = dalloc(e, &e->shard_logits, (size_t)nrows * Ws);
+        if (rc) return rc;
+        e->shard_cap = (size_t)nrows * Ws;
+    }
+    if (e->tc) {
+        if (v0 != e->shard_v0 || v1 != e->shard_v1) {   // the operand map of rows [v0, v1) of the head
+            int rc;
+            const size_t n = (size_t)c.vocab_size * E;
+            if (e->tc_kind == TC_TF32X3 && e->tc_lm_w)
+                rc = tc_weights_kmajor(&e->tc_lm_shard, TC_TF32X3, e->tc_lm_w + (size_t)v0 * E,
+                                       e->tc_lm_w + align_up(n, 64) + (size_t)v0 * E, E, W);
+            else if (e->tc_kind == TC_TF32X3)
+                rc = tc_weights_kmajor(&e->tc_lm_shard, TC_TF32X3, e->w<float>(e->lm) + (size_t)v0 * E, nullptr, E, W);
+            else
+                rc = tc_weights_kmajor(&e->tc_lm_shard, TC_F16, e->w<__half>(e->lm) + (size_t)v0 * E, nullptr, E, W);
+            if (rc) return set_err(rc, "g2_lm_head_rows: tensor map of vocabulary rows [%d, %d)", v0, v1);
+            e->shard_v0 = v0;
+            e->shard_v1 = v1;
+        }
+        // the rows as the GEMM operand (tf32 hi / lo, or fp16), then logits = rows . wte[v0..v1)
+        launch_tc_prep(e->tc_kind, rows, e->tc_xhi, e->tc_xlo, reinterpret_cast<__half *>(e->tc_xhi),
+                       (long long)nrows * E, e->st);
+        Rows rr{e->rows_tok, e->rows_pos, e->rows_slot};
+        e->launches += 1 + (e->dtype == G2_F32
+                                ? launch_tc_gemm<float>(e->tc_kind, e->tc_lm_shard, e->tc_x_e, nrows, e->tc_part,
+                                                        e->tc_part_floats, e->tc_ctr, e->tc_err, nullptr, nullptr,
+                                                        e->shard_logits, 0, nullptr, 0, rr, e->sms, e->st, OperandOut(), Ws)
+                                : launch_tc_gemm<__half>(e->tc_kind, e->tc_lm_shard, e->tc_x_e, nrows, e->tc_part,
+                                                         e->tc_part_floats, e->tc_ctr, e->tc_err, nullptr, nullptr,
+                                                         e->shard_logits, 0, nullptr, 0, rr, e->sms, e->st, OperandOut(),
+                                                         Ws));
+    } else if (e->dtype == G2_F32) {
+        launch_lm_head_rows<float>(rows, e->w<float>(e->lm) + (size_t)v0 * E, e->shard_logits, E, W, Ws, nrows, e->st);
+        e->launches += 1;
+    } else {
+        launch_lm_head_rows<__half>(rows, e->w<__half>(e->lm) + (size_t)v0 * E, e->shard_logits, E, W, Ws, nrows, e->st);
+        e->launches += 1;
+    }
+    // per row the first maximum of the range (main.c:1898-1904), as an index into the whole vocabulary
+    launch_argmax_rows(e->shard_logits, W, Ws, nrows, 0, best_index, best_value, nullptr, nullptr, nullptr, 0, nullptr,
+                       e->st);
+    launch_add_ints(best_index, nrows, v0, e->st);
+    e->launches += 2;
+    CKL();
+    CK(cudaStreamSynchronize(e->st));
+    return check_mega_err(e);
 }
 
 extern "C" int g2_logits(g2_engine *e, int slot, float *host, int n) {

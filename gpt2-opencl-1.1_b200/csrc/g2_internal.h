@@ -215,6 +215,8 @@ void launch_argmax_rows(const float *logits, int V, int Vp, int nrows, int forbi
                         cudaStream_t st);
 
 void launch_copy_row(const float *src, float *dst, int n, cudaStream_t st);
+// p[0..n) += add
+void launch_add_ints(int *p, int n, int add, cudaStream_t st);
 
 // dst[c][r] = src[r][c] for a [rows][cols] fp32 matrix, converted to WT: the
 // load-time transpose of an nn.Linear [out][in] weight into the Conv1D

@@ -1495,6 +1495,13 @@ void launch_argmax_rows(const float *logits, int V, int Vp, int nrows, int forbi
 void launch_copy_row(const float *src, float *dst, int n, cudaStream_t st) {
     launch_pdl(copy_kernel, dim3((n + 255) / 256), dim3(256), 0, st, src, dst, n);
 }
+__global__ void add_ints_kernel(int *p, int n, int add) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] += add;
+}
+void launch_add_ints(int *p, int n, int add, cudaStream_t st) {
+    add_ints_kernel<<<(n + 255) / 256, 256, 0, st>>>(p, n, add);
+}
 void launch_step_advance(int *step_ptr, cudaStream_t st) { launch_pdl(step_advance_kernel, dim3(1), dim3(1), 0, st, step_ptr); }
 
 // 32 x 32 tiles through shared memory (one padding column against bank

@@ -50,6 +50,8 @@ def _load():
     L.g2_prefill.argtypes = [vp, C.c_int, ip, C.c_int]
     L.g2_decode.argtypes = [vp, C.c_int, C.c_int, C.c_int]
     L.g2_decode_batch.argtypes = [vp, C.c_int, ip, ip, ip]
+    L.g2_decode_batch_rows.argtypes = [vp, C.c_int, ip, ip, ip, vp]
+    L.g2_lm_head_rows.argtypes = [vp, C.c_int, vp, C.c_int, C.c_int, vp, vp]
     L.g2_logits.argtypes = [vp, C.c_int, fp, C.c_int]
     L.g2_argmax.argtypes = [vp, C.c_int, C.c_int, ip, fp]
     L.g2_sample.argtypes = [fp, C.c_int, ip, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, ip]
@@ -187,6 +189,19 @@ class Engine:
         out = np.zeros((len(prompts), n_new), np.int32)
         check(lib.g2_generate_batch(self.h, len(s), sp, fp_, lp, n_new, out.ctypes.data_as(C.POINTER(C.c_int))))
         return out
+
+    def decode_batch_rows(self, slots, tokens, pos, rows):
+        """One decode step of several sequences without the LM head; the final
+        LayerNorm of each row into `rows` (a device tensor [n, n_embd], fp32)."""
+        s, sp = _i32(slots)
+        t, tp = _i32(tokens)
+        q, qp = _i32(pos)
+        check(lib.g2_decode_batch_rows(self.h, len(s), sp, tp, qp, _ptr(rows)))
+
+    def lm_head_rows(self, rows, nrows: int, v0: int, v1: int, best_value, best_index):
+        """LM head over vocabulary rows [v0, v1) for `nrows` normalised rows (device
+        tensors): each row's first maximum there and its vocabulary index."""
+        check(lib.g2_lm_head_rows(self.h, nrows, _ptr(rows), v0, v1, _ptr(best_value), _ptr(best_index)))
 
     def synchronize(self):
         check(lib.g2_synchronize(self.h))

@@ -82,6 +82,21 @@ int g2_decode(g2_engine *e, int slot, int token, int pos);
 /* decode for n slots at once (one token each, each at its own position). */
 int g2_decode_batch(g2_engine *e, int n, const int *slots, const int *tokens, const int *pos);
 
+/* The LM head split over several GPUs by vocabulary rows (the optional
+ * column-sharded GPT-2 XL head: each GPU takes a range of wte's rows for the
+ * rows of every GPU and the best per row is exchanged).
+ * g2_decode_batch_rows: decode() (main.c:1792-1830) for n sequences without
+ * the LM head matvec (main.c:1831); writes the final LayerNorm of each row,
+ * [n][n_embd] fp32, to `rows` (device memory, 16-byte aligned).  No logits are
+ * written.  Returns once the rows are complete.
+ * g2_lm_head_rows: the LM head matvec (main.c:1831) over wte rows [v0, v1)
+ * (v0 a multiple of 4) for nrows (<= max(n_ctx, max_batch)) normalised rows in
+ * device memory; best_value[r] / best_index[r] (device memory) receive the
+ * row's first maximum in that range (main.c:1898-1904) and its index in the
+ * whole vocabulary.  Returns once they are complete. */
+int g2_decode_batch_rows(g2_engine *e, int n, const int *slots, const int *tokens, const int *pos, float *rows);
+int g2_lm_head_rows(g2_engine *e, int nrows, const float *rows, int v0, int v1, float *best_value, int *best_index);
+
 /* Copy the first n (<= padded_vocab) logits of `slot` to host memory. */
 int g2_logits(g2_engine *e, int slot, float *host, int n);
 /* Device argmax over logits[0..vocab_size) of `slot`, first index on ties
