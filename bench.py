@@ -514,6 +514,8 @@ def run_ours(args, cfg):
                 "wall_s": main["wall_s"]}
         if "clocks" in main:
             line["clocks"] = main["clocks"]
+        if "lm_shard" in main:
+            line["lm_shard"] = main["lm_shard"]
         if batched:
             line["batched"] = {n: dict(b) for n, b in batched.items()}
             line["gpu_launches"] += sum(b["gpu_launches"] for b in batched.values())
