@@ -707,13 +707,17 @@ TcPlan plan(int R, int N, int kb_total, int sms) {
 // streams weights; each share then spans at most two tiles.  Uniform splits
 // of each tile leave SMs idle whenever tiles x splits misses the SM count
 // (76 to 104 of 148 CTAs on the 32-row GEMMs of GPT-2 XL).  Measured on
-// B200: the balanced GEMMs' main loops are up to twice as short, but the
-// extra partials (up to 13 per column) cost their consumers (the attention's
-// c_attn sum, the LayerNorm-fused reduces) about as much: c5 +0.6%, c4 -6%.
-// So it is off unless G2_TC_BALANCED sets the largest row count that uses it.
-SplitInfo balanced_plan(int R, int N, int kb_total, int bn, int sms) {
-    static const int max_rows = getenv("G2_TC_BALANCED") ? atoi(getenv("G2_TC_BALANCED")) : 0;
+// B200: the balanced GEMMs' main loops are up to twice as short; their extra
+// partials (up to 13 per column) cost the LayerNorm-fused reduces about as
+// much, so a GEMM whose reduce takes a LayerNorm keeps uniform splits.  For the
+// others (c_attn, c_fc) it pays on the 3xTF32 GEMMs (c5 +3.7%) and not on the
+// fp16 ones (c4 -7%): by default it applies to 3xTF32 GEMMs of up to 32 rows;
+// G2_TC_BALANCED sets the largest row count for both precisions (0 = never).
+SplitInfo balanced_plan(int R, int N, int kb_total, int bn, int sms, int kind, bool ln) {
+    static const int env_rows = getenv("G2_TC_BALANCED") ? atoi(getenv("G2_TC_BALANCED")) : -1;
+    const int max_rows = env_rows >= 0 ? env_rows : (kind == TC_TF32X3 ? 32 : 0);
     SplitInfo si;
+    if (ln) return si;
     const int tiles = (N + kTcTileF - 1) / kTcTileF;
     const long long U = (long long)tiles * kb_total;
     if (R > max_rows || R > bn || N % 4 || tiles >= sms || kb_total < 2) return si;
@@ -879,8 +883,9 @@ size_t tc_partial_floats(int R_max, int N, int K, int kind, int sms) {
     size_t m = 0;
     for (int R = 1; R <= R_max; ++R) {
         const TcPlan p = plan(R, N, kb_total, sms);
-        const SplitInfo si = balanced_plan(R, N, kb_total, p.bn, sms);
-        const size_t f = (size_t)(si.G ? max_partials(si, N) : p.splits) * R * N;
+        const SplitInfo si = balanced_plan(R, N, kb_total, p.bn, sms, kind, false);
+        // room for either plan (a GEMM followed by a LayerNorm reduce keeps uniform splits)
+        const size_t f = (size_t)std::max(si.G ? max_partials(si, N) : 0, p.splits) * R * N;
         m = f > m ? f : m;
     }
     return m;
@@ -929,7 +934,7 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
     a.splits = p.splits;
     a.si.splits = p.splits;
     if (!w.kmajor) {   // the balanced split, where it applies and its partials fit the scratch
-        const SplitInfo si = balanced_plan(R, w.N, kb_total, p.bn, sms);
+        const SplitInfo si = balanced_plan(R, w.N, kb_total, p.bn, sms, kind, ln_g != nullptr);
         if (si.G && (size_t)max_partials(si, w.N) * R * w.N <= partial_floats) a.si = si;
     }
     a.part = partial;

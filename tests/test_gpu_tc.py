@@ -106,10 +106,10 @@ def test_matmul_tc_rejects_bad_shapes(g2):
 
 
 def test_matmul_tc_balanced_split(g2):
-    """The balanced split (G2_TC_BALANCED: the K blocks of all tiles shared out
-    equally over the SMs, a CTA's share spanning up to two tiles) is off by
-    default; the same cases are run again in a process where it applies to
-    every GEMM of up to 32 rows."""
+    """The balanced split (the K blocks of all tiles shared out equally over the
+    SMs, a CTA's share spanning up to two tiles) applies by default to 3xTF32
+    GEMMs of up to 32 rows only; the same cases are run again in a process
+    where G2_TC_BALANCED extends it to every GEMM of up to 32 rows, fp16 too."""
     env = dict(os.environ, G2_TC_BALANCED="32")
     r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-x", "-p", "no:cacheprovider", "-k",
                         "test_matmul_tc and not balanced"], env=env, capture_output=True, text=True, timeout=900)
