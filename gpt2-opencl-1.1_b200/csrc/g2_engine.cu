@@ -88,6 +88,10 @@ struct g2_engine {
     // KV caches
     void *kbuf = nullptr, *vbuf = nullptr;
     KVLayout kv{};
+    // fp16 caches as 2-D tensors ([rows][64], one row per (slot, layer, head,
+    // position)) for the batched attention's swizzled TMA loads
+    CUtensorMap kv_kmap{}, kv_vmap{};
+    bool kv_maps = false;
     // workspaces
     int R = 0;   // rows capacity
     float *h = nullptr, *xln = nullptr, *qkv = nullptr, *attn = nullptr, *ffn = nullptr;
@@ -593,6 +597,23 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
         e->device_bytes += 2 * bytes;
         e->kv.k = e->kbuf;
         e->kv.v = e->vbuf;
+        // zeroed once: positions a sequence has not written hold zeros, never stale bit
+        // patterns of other data (the batched attention reads whole 128-key tiles)
+        r1 = cudaMemset(e->kbuf, 0, bytes);
+        if (r1 == cudaSuccess) r1 = cudaMemset(e->vbuf, 0, bytes);
+        if (r1 == cudaSuccess) r1 = cudaDeviceSynchronize();
+        if (r1 != cudaSuccess) {
+            free_engine(e);
+            return set_err(G2_ERR_CUDA, "KV cache zeroing: %s", cudaGetErrorString(r1));
+        }
+        if (dtype == G2_F16) {
+            const unsigned long long rows = kv_elems / kHeadDim;
+            if (tc_encode(&e->kv_kmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, e->kbuf, kHeadDim, rows, kHeadDim, 64,
+                          false) == G2_OK &&
+                tc_encode(&e->kv_vmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, e->vbuf, kHeadDim, rows, kHeadDim, 64,
+                          false) == G2_OK)
+                e->kv_maps = true;
+        }
     }
     e->R = S > max_batch ? S : max_batch;
     const int R = e->R;
@@ -960,6 +981,10 @@ static int forward_rows(g2_engine *e, int nrows, int max_pos, bool decode_rows =
                 qp.part = e->tc_part;
                 qp.si = si;
                 qp.err = e->tc_err;
+                if (e->kv_maps) {
+                    qp.kmap = &e->kv_kmap;
+                    qp.vmap = &e->kv_vmap;
+                }
                 qp.bias = e->w<WT>(o.qkv_b);
             }
         } else {

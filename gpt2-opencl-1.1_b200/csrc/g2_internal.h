@@ -179,6 +179,9 @@ struct QkvPartials {
     SplitInfo si;
     const void *bias = nullptr;   // [3E] of the engine's weight type
     int *err = nullptr;           // where an expired wait of the streamed attention is recorded
+    // fp16 caches: CUtensorMaps of K and V as [rows][64] (box 64 x 64, 128-byte
+    // swizzle) for the tensor-core path of the streamed attention, or nullptr
+    const void *kmap = nullptr, *vmap = nullptr;
 };
 
 template <typename KT>

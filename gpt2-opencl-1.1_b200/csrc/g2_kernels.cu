@@ -21,6 +21,8 @@
 // Arithmetic is fp32 with fp32 accumulation (fp16 weights are widened on
 // load).  Summation orders differ from the reference (parallel reductions);
 // parity is checked against the oracle within the stated tolerances.
+#include <cuda.h>
+
 #include <cfloat>
 #include <cstdlib>
 #include <climits>
@@ -605,6 +607,40 @@ __device__ __forceinline__ bool as_wait(u64a *b, unsigned par) {
         if (as_time() > lim) return false;
     }
 }
+// 2-D tiled TMA load of box (x, y) of map into shared memory (signals bar)
+__device__ __forceinline__ void as_tma2d(void *dst, const CUtensorMap *map, int x, int y, u64a *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            as_smem(dst)),
+        "l"(reinterpret_cast<u64a>(map)), "r"(x), "r"(y), "r"(as_smem(bar))
+        : "memory");
+}
+// Tensor-core pieces of the fp16 path: m16n8k16 (fp16 operands, fp32 accumulation),
+// ldmatrix of 8 x 8 fp16 tiles, and the byte offset of 16-byte chunk c of row r in
+// a tile of 128-byte rows stored with the 128-byte swizzle (what the TMA load writes).
+__device__ __forceinline__ void mma16816(float (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(unsigned (&r)[4], unsigned addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(unsigned (&r)[4], unsigned addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ unsigned swz128(int r, int c) { return (unsigned)(r * 128 + ((c ^ (r & 7)) << 4)); }
+__device__ __forceinline__ unsigned pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const unsigned *>(&h);
+}
 __device__ __forceinline__ void as_bulk(void *dst, const void *src, unsigned bytes, u64a *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      as_smem(dst)),
@@ -619,10 +655,19 @@ template <typename KT>
 __host__ __device__ constexpr int as_chunk() {
     return sizeof(KT) == 2 ? 128 : 64;
 }
-size_t attn_stream_smem(int elem) { return (size_t)kAsStages * 2 * (elem == 2 ? 128 : 64) * kHeadDim * elem; }
+// Dynamic shared memory: the ring (1 KB more for the alignment of the swizzled tiles).
+size_t attn_stream_smem(int elem) { return (size_t)kAsStages * 2 * (elem == 2 ? 128 : 64) * kHeadDim * elem + 1024; }
 
-template <typename KT>
-__global__ void __launch_bounds__(kAsThreads, 3) attn_stream_kernel(AttnArgs<KT> a, int nrows) {
+// MMA (fp16 caches with their tensor maps mk, mv): each K and V chunk arrives by one
+// tiled TMA load in the 128-byte swizzle, and each warp computes its 16 keys' scores
+// (K tile x q) and P.V (P x V tile, V read transposed by ldmatrix) with m16n8k16
+// tensor-core operations, fp16 operands (q and the probabilities rounded to fp16, as
+// the fp16 engine's GEMM operands are) and fp32 accumulation.  The cache row at the
+// step's position is patched into the staged tiles from the summed c_attn partials.
+template <typename KT, bool MMA>
+__global__ void __launch_bounds__(kAsThreads, 3)
+    attn_stream_kernel(AttnArgs<KT> a, int nrows, const __grid_constant__ CUtensorMap mk,
+                       const __grid_constant__ CUtensorMap mv) {
     constexpr int CH = as_chunk<KT>();               // keys per item
     constexpr int NW = kAsThreads / 32;              // warps
     constexpr int KPW = CH / NW;                     // keys per warp: 16 (fp16) or 8 (fp32)
@@ -630,8 +675,10 @@ __global__ void __launch_bounds__(kAsThreads, 3) attn_stream_kernel(AttnArgs<KT>
     constexpr int EPC = 16 / sizeof(KT);             // elements per 16-byte chunk of a key row
     constexpr int CB = CH * kHeadDim * sizeof(KT);   // bytes of a full K (or V) chunk
     static_assert(kHeadDim * sizeof(KT) == TPK * 64, "each thread of a key reads four 16-byte chunks");
+    static_assert(!MMA || sizeof(KT) == 2, "the tensor-core path takes fp16 caches");
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    unsigned char *ring = smem_raw;                  // [stage][K chunk, V chunk]
+    unsigned char *ring =                            // [stage][K chunk, V chunk], 1024-byte aligned
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     __shared__ u64a full[kAsStages];
     __shared__ float q[kHeadDim];
     __shared__ float wo[NW][kHeadDim], wm[NW], wl[NW];   // per-warp partial (o, max, sum)
@@ -693,15 +740,33 @@ __global__ void __launch_bounds__(kAsThreads, 3) attn_stream_kernel(AttnArgs<KT>
     // thread 0: request item (cursor u, index i)'s K and V rows into stage (i - i0) % kAsStages
     auto issue = [&](const Cur &u, int i) {
         const int T = rpos[u.r] + 1, j0 = u.ch * CH, nj = min(CH, T - j0);
-        const unsigned bytes = (unsigned)(nj * kHeadDim * sizeof(KT));
         const int s = (i - i0) % kAsStages;
         u64a *bar = &full[s];
+        if (MMA) {   // 64-row boxes covering the chunk's keys (rows past them: weighted 0)
+            const int nbox = (nj + 63) / 64;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(as_smem(bar)),
+                         "r"((unsigned)(nbox * CB))
+                         : "memory");
+            const int row = (int)((kv_base(u.r, u.h) + (long long)j0 * kHeadDim) / kHeadDim);
+            for (int b = 0; b < nbox; ++b) {
+                as_tma2d(ring + (size_t)s * 2 * CB + b * (CB / 2), &mk, 0, row + 64 * b, bar);
+                as_tma2d(ring + (size_t)s * 2 * CB + CB + b * (CB / 2), &mv, 0, row + 64 * b, bar);
+            }
+            return;
+        }
+        const unsigned bytes = (unsigned)(nj * kHeadDim * sizeof(KT));
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(as_smem(bar)), "r"(2 * bytes)
                      : "memory");
         const long long b = kv_base(u.r, u.h) + (long long)j0 * kHeadDim;
         as_bulk(ring + (size_t)s * 2 * CB, reinterpret_cast<const KT *>(a.kv.k) + b, bytes, bar);
         as_bulk(ring + (size_t)s * 2 * CB + CB, reinterpret_cast<const KT *>(a.kv.v) + b, bytes, bar);
     };
+    if (MMA) {   // the ring starts as zeros: rows a short chunk leaves unloaded are read with weight 0
+        uint4 *z = reinterpret_cast<uint4 *>(ring);
+        for (int k = tid; k < kAsStages * 2 * CB / 16; k += kAsThreads) z[k] = make_uint4(0u, 0u, 0u, 0u);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // before the TMA writes
+        __syncthreads();
+    }
     Cur iu{0, 0, 0};   // thread 0's issue cursor
     if (tid == 0 && i0 < i1) {
         iu = place(i0);
@@ -720,6 +785,7 @@ __global__ void __launch_bounds__(kAsThreads, 3) attn_stream_kernel(AttnArgs<KT>
 #pragma unroll
     for (int t = 0; t < 4; ++t) rot[t] = part * 4 + ((t + kl + (TPK == 4 && part >= 2 ? 2 : 0)) & 3);
     float qr[4][EPC];
+    unsigned qb[4][2];   // MMA: q as the B operand of the score products
     float Mr = -FLT_MAX, Lr = 0.0f, acc = 0.0f;      // running softmax of the current (row, head), threads < 64
     Cur u{0, 0, 0};
     if (i0 < i1) u = place(i0);
@@ -772,6 +838,67 @@ __global__ void __launch_bounds__(kAsThreads, 3) attn_stream_kernel(AttnArgs<KT>
             }
             return;
         }
+        if constexpr (MMA) {
+            const unsigned kb = as_smem(ring + (size_t)s * 2 * CB), vb = kb + CB;
+            const int jpos = pos - j0;   // the key at pos (this step's), if in this chunk
+            if (jpos >= 0 && jpos < nj) {   // its K and V rows into the staged tiles, from the summed partials
+                if (tid < 2 * kHeadDim) {
+                    const int d = tid & (kHeadDim - 1), w = tid >> 6;
+                    __half *dst = reinterpret_cast<__half *>(ring + (size_t)s * 2 * CB + (w ? CB : 0) +
+                                                             swz128(jpos, d >> 3) + (d & 7) * 2);
+                    *dst = __float2half_rn(knew[w][d]);
+                }
+                // these generic writes come before the TMA that next fills this stage
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncthreads();
+            }
+            const int g = lane >> 2, t = lane & 3, q8 = lane >> 3;
+            if (fresh) {   // q as the B operand: column 0 only (lanes of group 0), fp16
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    qb[k][0] = g == 0 ? pack_h2(q[16 * k + 2 * t], q[16 * k + 2 * t + 1]) : 0u;
+                    qb[k][1] = g == 0 ? pack_h2(q[16 * k + 8 + 2 * t], q[16 * k + 9 + 2 * t]) : 0u;
+                }
+            }
+            const int r0 = warp * 16;                              // this warp's 16 keys of the chunk
+            const int lrow = r0 + (q8 & 1) * 8 + (lane & 7);       // the row this lane addresses for ldmatrix
+            float sd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {   // dims 16 k .. 16 k + 15
+                unsigned af[4];
+                ldsm_x4(af, kb + swz128(lrow, 2 * k + (q8 >> 1)));
+                mma16816(sd, af, qb[k][0], qb[k][1]);
+            }
+            // column 0 (lanes t == 0): sd[0] = score of key r0 + g, sd[2] = of key r0 + g + 8
+            const bool va = t == 0 && r0 + g < nj, vb8 = t == 0 && r0 + g + 8 < nj;
+            const float m = warp_max(fmaxf(va ? sd[0] : -FLT_MAX, vb8 ? sd[2] : -FLT_MAX));
+            const float p0 = va ? expf(sd[0] - m) : 0.0f, p1 = vb8 ? expf(sd[2] - m) : 0.0f;
+            const float l = warp_sum(p0 + p1);
+            // P as the A operand: row 0 holds keys r0 .. r0 + 15 (lanes of group 0), fp16
+            const float pa = __shfl_sync(0xffffffffu, p0, 8 * t), pb = __shfl_sync(0xffffffffu, p0, 8 * t + 4);
+            const float pc = __shfl_sync(0xffffffffu, p1, 8 * t), pd = __shfl_sync(0xffffffffu, p1, 8 * t + 4);
+            const unsigned pf[4] = {g == 0 ? pack_h2(pa, pb) : 0u, 0u, g == 0 ? pack_h2(pc, pd) : 0u, 0u};
+            float o[8][4];
+#pragma unroll
+            for (int nb = 0; nb < 8; ++nb) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {   // dims 16 u .. 16 u + 15: two n-blocks of 8
+                unsigned bf[4];
+                ldsm_x4_t(bf, vb + swz128(lrow, 2 * u + (q8 >> 1)));
+                mma16816(o[2 * u], pf, bf[0], bf[1]);
+                mma16816(o[2 * u + 1], pf, bf[2], bf[3]);
+            }
+            if (g == 0)   // row 0 of each n-block: dims 8 nb + 2 t, + 1
+#pragma unroll
+                for (int nb = 0; nb < 8; ++nb) {
+                    wo[warp][8 * nb + 2 * t] = o[nb][0];
+                    wo[warp][8 * nb + 2 * t + 1] = o[nb][1];
+                }
+            if (lane == 0) {
+                wm[warp] = m;
+                wl[warp] = l;
+            }
+        } else {
         if (fresh) {
 #pragma unroll
             for (int t = 0; t < 4; ++t)
@@ -830,6 +957,7 @@ __global__ void __launch_bounds__(kAsThreads, 3) attn_stream_kernel(AttnArgs<KT>
             wm[warp] = m;
             wl[warp] = l;
         }
+        }   // the CUDA-core path
         __syncthreads();
         // the stage is free again: request the item kAsStages ahead into it
         if (tid == 0 && i + kAsStages < i1) {
@@ -872,13 +1000,17 @@ __global__ void __launch_bounds__(kAsThreads, 3) attn_stream_kernel(AttnArgs<KT>
                     P[0] = Mr;
                     P[1] = Lr;
                 }
-                __threadfence();
+                // the CTA barrier orders every thread's partial before thread 0's release;
+                // the last arrival's acquire (then the barrier) orders the reads after all
                 __syncthreads();
                 unsigned *ctr = a.counters + (size_t)r * NH + h;
-                if (tid == 0) s_last = (atomicAdd(ctr, 1u) == (unsigned)(nparts - 1));
+                if (tid == 0) {
+                    unsigned prev;
+                    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
+                    s_last = prev == (unsigned)(nparts - 1);
+                }
                 __syncthreads();
                 if (s_last) {
-                    __threadfence();
                     if (tid < kHeadDim) {
                         const float *P0 = a.partial + ((size_t)r * NH + h) * a.max_splits * (kHeadDim + 2);
                         float M = -FLT_MAX;
@@ -1370,6 +1502,30 @@ size_t attn_partial_floats(int nrows, int n_head, int max_seq) {
 }
 size_t attn_counter_count(int nrows, int n_head) { return (size_t)nrows * n_head; }
 
+// One streamed-attention launch: G = SMs x resident CTAs (per device and instantiation,
+// with the shared-memory limit raised once per device).
+template <typename KT, bool MMA>
+static void launch_attn_stream(const AttnArgs<KT> &a, int nrows, const CUtensorMap &mk, const CUtensorMap &mv,
+                               cudaStream_t st) {
+    static unsigned long long attr_set = 0;
+    static int per_sm[64];
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const size_t smem = attn_stream_smem((int)sizeof(KT));
+    if (dev >= 64 || !(__atomic_load_n(&attr_set, __ATOMIC_ACQUIRE) >> dev & 1ull)) {
+        cudaFuncSetAttribute(attn_stream_kernel<KT, MMA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        int n = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_stream_kernel<KT, MMA>, kAsThreads, smem);
+        if (dev < 64) {
+            per_sm[dev] = n > 0 ? n : 1;
+            __atomic_fetch_or(&attr_set, 1ull << dev, __ATOMIC_RELEASE);
+        }
+    }
+    const int G = sms * (dev < 64 ? per_sm[dev] : 1);
+    launch_pdl(attn_stream_kernel<KT, MMA>, dim3((unsigned)G), dim3(kAsThreads), smem, st, a, nrows, mk, mv);
+}
+
 template <typename KT>
 void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
                       float *out, int out_stride, float *partial, unsigned *counters, int max_pos_hint,
@@ -1393,24 +1549,13 @@ void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int 
     a.err = qp.err;
     if (qp.part && qp.err && nrows <= kAsMaxRows) {
         // decode rows with c_attn's partials: the streamed kernel, as many CTAs as fit at once
-        static unsigned long long attr_set = 0;   // devices on which its shared-memory limit was raised
-        static int per_sm[64];
-        int dev = 0, sms = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        const size_t smem = attn_stream_smem((int)sizeof(KT));
-        if (dev >= 64 || !(__atomic_load_n(&attr_set, __ATOMIC_ACQUIRE) >> dev & 1ull)) {
-            cudaFuncSetAttribute(attn_stream_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            int n = 0;
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_stream_kernel<KT>, kAsThreads, smem);
-            if (dev < 64) {
-                per_sm[dev] = n > 0 ? n : 1;
-                __atomic_fetch_or(&attr_set, 1ull << dev, __ATOMIC_RELEASE);
-            }
-        }
-        const int G = sms * (dev < 64 ? per_sm[dev] : 1);
+        // (fp16 caches with their tensor maps: the tensor-core instantiation)
         a.max_splits = (kv.max_seq + as_chunk<KT>() - 1) / as_chunk<KT>();   // partial slots per (row, head)
-        launch_pdl(attn_stream_kernel<KT>, dim3((unsigned)G), dim3(kAsThreads), smem, st, a, nrows);
+        if (sizeof(KT) == 2 && qp.kmap && qp.vmap)
+            launch_attn_stream<KT, sizeof(KT) == 2>(a, nrows, *static_cast<const CUtensorMap *>(qp.kmap),
+                                                     *static_cast<const CUtensorMap *>(qp.vmap), st);
+        else
+            launch_attn_stream<KT, false>(a, nrows, CUtensorMap{}, CUtensorMap{}, st);
         return;
     }
     const int splits = max_pos_hint < 0 ? a.max_splits : (max_pos_hint + kAttnChunk) / kAttnChunk;
