@@ -105,7 +105,7 @@ struct g2_engine {
     int *h_rows = nullptr;          // [3][R]
     StepState *h_state = nullptr;   // ring
     int h_state_i = 0;
-    int *h_small = nullptr;         // results
+    int *h_small = nullptr;         // results; its last two ints receive the error words (sync_and_check)
     cudaEvent_t staged = nullptr;
     GemvPlan plan_qkv{}, plan_proj{}, plan_fc{}, plan_fc2{};
     std::vector<int> filled;        // positions present in each slot's cache
@@ -173,6 +173,7 @@ struct g2_engine {
     // device sampler
     float *sample_work = nullptr;   // [padded_vocab]
     int *sample_ctx = nullptr;      // [n_ctx] context ids
+    int *topk_out = nullptr;        // g2_topk: [G2_MAX_TOPK] values (as float) then [G2_MAX_TOPK] ids
     int *h_ctx = nullptr;           // pinned staging of the context ids
     std::vector<TcWeights> tc_maps;           // [L][4]: qkv, proj, fc, fc2
     TcWeights tc_lm{};                        // the tied LM head: wte [V][E] as a K-major operand
@@ -210,7 +211,7 @@ static void free_engine(g2_engine *e) {
     if (e->batch_graph) cudaGraphExecDestroy(e->batch_graph);
     for (auto &kv : e->prefill_graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    void *dev_ptrs[] = {e->shard_logits, e->sample_work, e->sample_ctx, e->tc_w, e->tc_lm_w, e->tc_img, e->tc_idx, e->tc_perm, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
+    void *dev_ptrs[] = {e->shard_logits, e->sample_work, e->sample_ctx, e->topk_out, e->tc_w, e->tc_lm_w, e->tc_img, e->tc_idx, e->tc_perm, e->tc_xhi, e->tc_xlo, e->tc_x2hi, e->tc_x2lo, e->tc_ctr, e->tc_part, e->tc_err, e->d_trace, e->packed, e->d_layer_off, e->d_layers, e->t_qkv, e->mega_acc,
                         e->t_best, e->t_att, e->d_err, e->wbuf, e->kbuf, e->vbuf, e->h, e->xln, e->qkv, e->attn, e->ffn, e->logits,
                         e->logits_rows, e->gemv_partial, e->attn_partial, e->lm_partial, e->gemv_ctr,
                         e->attn_ctr, e->lm_ctr, e->rows_tok, e->rows_pos, e->rows_slot, e->result,
@@ -658,6 +659,7 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
     TRY(dalloc(e, &e->state, 1));
     TRY(dalloc(e, &e->sample_work, (size_t)Vp));
     TRY(dalloc(e, &e->sample_ctx, (size_t)S));
+    TRY(dalloc(e, &e->topk_out, (size_t)2 * G2_MAX_TOPK));
     {
         cudaError_t r = cudaMallocHost(&e->h_rows, sizeof(int) * 3 * (size_t)R);
         if (r == cudaSuccess) r = cudaMallocHost(&e->h_state, sizeof(StepState) * 64);
@@ -1206,22 +1208,25 @@ int check_flags() {
 }
 }  // namespace g2
 
-// After a synchronisation: report an expired device-side wait of the decode kernel
-// (and, in the bounds-checked build, a failed bounds test of any kernel).
-static int check_mega_err(g2_engine *e) {
-    int code = 0;
+// Synchronise the engine's stream and report what its kernels recorded: an
+// expired bounded wait of a tensor-core GEMM or of the decode kernel, a clamped
+// accumulator contribution, and (bounds-checked build) a failed bounds test of
+// any kernel.  The two error words are copied to pinned memory behind the
+// caller's own copies on the stream, so one synchronisation serves both (a
+// token of the host loop pays one host round trip, not three).
+static int sync_and_check(g2_engine *e) {
+    int *h = e->h_small + 4 * (size_t)e->max_batch;   // the two spare ints
+    h[0] = h[1] = 0;
+    if (e->tc) CK(cudaMemcpyAsync(&h[0], e->tc_err, sizeof(int), cudaMemcpyDeviceToHost, e->st));
+    if (e->mega) CK(cudaMemcpyAsync(&h[1], e->d_err, sizeof(int), cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
     if (const int site = check_flags())
         return set_err(G2_ERR_RANGE, "bounds check failed in a kernel (site %d, G2_CHECK build)", site);
-    if (e->tc) {
-        CK(cudaMemcpy(&code, e->tc_err, sizeof(int), cudaMemcpyDeviceToHost));
-        if (code) {
-            CK(cudaMemsetAsync(e->tc_err, 0, sizeof(int), e->st));   // ordered before the stream's next kernels
-            return set_err(G2_ERR_TIMEOUT, "tensor-core GEMM: a bounded device-side wait expired");
-        }
+    if (h[0]) {
+        CK(cudaMemsetAsync(e->tc_err, 0, sizeof(int), e->st));   // ordered before the stream's next kernels
+        return set_err(G2_ERR_TIMEOUT, "tensor-core GEMM: a bounded device-side wait expired");
     }
-    if (!e->mega) return G2_OK;
-    CK(cudaMemcpy(&code, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (code) {
+    if (const int code = h[1]) {
         CK(cudaMemsetAsync(e->d_err, 0, sizeof(int), e->st));
         if (code == kErrClamp)
             return set_err(G2_ERR_RANGE, "decode kernel: an accumulator contribution exceeded +-2^21 and was clamped");
@@ -1399,8 +1404,7 @@ extern "C" int g2_decode_batch_rows(g2_engine *e, int n, const int *slots, const
     CKL();
     for (int i = 0; i < n; ++i) e->filled[slots[i]] = pos[i] + 1;
     e->result_slot = -1;
-    CK(cudaStreamSynchronize(e->st));   // the caller's collectives run on another stream
-    return check_mega_err(e);
+    return sync_and_check(e);   // the caller's collectives run on another stream
 }
 
 extern "C" int g2_lm_head_rows(g2_engine *e, int nrows, const float *rows, int v0, int v1, float *best_value,
@@ -1463,8 +1467,7 @@ extern "C" int g2_lm_head_rows(g2_engine *e, int nrows, const float *rows, int v
     launch_add_ints(best_index, nrows, v0, e->st);
     e->launches += 2;
     CKL();
-    CK(cudaStreamSynchronize(e->st));
-    return check_mega_err(e);
+    return sync_and_check(e);
 }
 
 extern "C" int g2_logits(g2_engine *e, int slot, float *host, int n) {
@@ -1474,8 +1477,7 @@ extern "C" int g2_logits(g2_engine *e, int slot, float *host, int n) {
     if (n < 0 || n > e->c.padded_vocab) return set_err(G2_ERR_RANGE, "g2_logits: n %d > padded_vocab", n);
     CK(cudaSetDevice(e->device));
     CK(cudaMemcpyAsync(host, e->logits + (size_t)slot * e->c.padded_vocab, sizeof(float) * n, cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
-    return check_mega_err(e);
+    return sync_and_check(e);
 }
 
 extern "C" int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, float *value) {
@@ -1488,8 +1490,7 @@ extern "C" int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, flo
         // the LM-head kernel's argmax (no EOS exclusion); it also answers the
         // EOS-excluding query whenever its token is not EOS
         CK(cudaMemcpyAsync(e->h_small, e->result, 2 * sizeof(int), cudaMemcpyDeviceToHost, e->st));
-        CK(cudaStreamSynchronize(e->st));
-        if ((rc = check_mega_err(e))) return rc;
+        if ((rc = sync_and_check(e))) return rc;
         if (!forbid_eos || e->h_small[0] != kEos) {
             *token = e->h_small[0];
             if (value) memcpy(value, &e->h_small[1], 4);
@@ -1502,8 +1503,7 @@ extern "C" int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, flo
     e->launches += 1;
     CKL();
     CK(cudaMemcpyAsync(e->h_small, e->argmax_out, 2 * sizeof(int), cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
-    if ((rc = check_mega_err(e))) return rc;
+    if ((rc = sync_and_check(e))) return rc;
     *token = e->h_small[0];
     if (value) memcpy(value, &e->h_small[1], 4);
     return G2_OK;
@@ -1529,17 +1529,34 @@ extern "C" int g2_sample_device(g2_engine *e, int slot, const int *context_ids, 
     e->launches += 1;
     CKL();
     CK(cudaMemcpyAsync(e->h_small, e->argmax_out, sizeof(int), cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
-    if ((rc = check_mega_err(e))) return rc;
+    if ((rc = sync_and_check(e))) return rc;
     *out_token = e->h_small[0];
     return G2_OK;
+}
+
+extern "C" int g2_topk(g2_engine *e, int slot, int k, float *values, int *ids) {
+    NvtxRange nvtx_range("g2_topk");
+    if (!e || !values || !ids) return set_err(G2_ERR_ARG, "g2_topk: null argument");
+    int rc;
+    if ((rc = check_slot(e, slot))) return rc;
+    if (k < 1 || k > G2_MAX_TOPK || k > e->c.vocab_size)
+        return set_err(G2_ERR_RANGE, "g2_topk: k %d out of range [1,%d]", k, std::min(G2_MAX_TOPK, e->c.vocab_size));
+    if (e->filled[slot] == 0) return set_err(G2_ERR_STATE, "g2_topk: slot %d has no logits yet", slot);
+    CK(cudaSetDevice(e->device));
+    float *dv = reinterpret_cast<float *>(e->topk_out);
+    int *di = e->topk_out + G2_MAX_TOPK;
+    launch_topk(e->logits + (size_t)slot * e->c.padded_vocab, e->c.vocab_size, k, dv, di, e->st);
+    e->launches += 1;
+    CKL();
+    CK(cudaMemcpyAsync(values, dv, sizeof(float) * k, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaMemcpyAsync(ids, di, sizeof(int) * k, cudaMemcpyDeviceToHost, e->st));
+    return sync_and_check(e);
 }
 
 extern "C" int g2_synchronize(g2_engine *e) {
     if (!e) return set_err(G2_ERR_ARG, "null engine");
     CK(cudaSetDevice(e->device));
-    CK(cudaStreamSynchronize(e->st));
-    return check_mega_err(e);
+    return sync_and_check(e);
 }
 
 extern "C" int g2_last_timing(g2_engine *e, float *prefill_ms, float *decode_ms, int *decode_steps) {
@@ -1584,8 +1601,7 @@ extern "C" int g2_generate(g2_engine *e, int slot, const int *prompt, int n_prom
     CK(cudaEventRecord(e->ev[2], e->st));
     CK(cudaMemcpyAsync(out_tokens, e->out_tokens + (size_t)slot * e->c.n_ctx, sizeof(int) * n_new,
                        cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
-    if ((rc = check_mega_err(e))) return rc;
+    if ((rc = sync_and_check(e))) return rc;
     if (e->mega && n_new > 1) dump_trace(e, n_new - 1);
     CK(cudaEventElapsedTime(&e->last_prefill_ms, e->ev[0], e->ev[1]));
     CK(cudaEventElapsedTime(&e->last_decode_ms, e->ev[1], e->ev[2]));
@@ -1709,7 +1725,7 @@ extern "C" int g2_generate_batch(g2_engine *e, int n, const int *slots, const in
         e->launches += (long long)(n_new - 1) * e->batch_graph_kernels;
     }
     CK(cudaEventRecord(e->ev[2], e->st));
-    CK(cudaStreamSynchronize(e->st));
+    if ((rc = sync_and_check(e))) return rc;   // an expired GEMM wait of any step is reported here
     for (int i = 0; i < n; ++i) {
         CK(cudaMemcpy(out_tokens + (size_t)i * n_new + 1, e->out_tokens + (size_t)i * c.n_ctx + 1,
                       sizeof(int) * (n_new - 1), cudaMemcpyDeviceToHost));
@@ -1839,6 +1855,15 @@ extern "C" int g2k_layernorm(const float *x, float *out, const float *gamma, con
     if (!x || !out || !gamma || !beta) return set_err(G2_ERR_ARG, "g2k_layernorm: null argument");
     if (n_embd <= 0 || rows <= 0) return set_err(G2_ERR_ARG, "g2k_layernorm: bad size");
     launch_layernorm<float>(x, out, gamma, beta, n_embd, rows, (cudaStream_t)stream);
+    CKL();
+    return G2_OK;
+}
+
+extern "C" int g2k_topk(const float *logits, int n, int k, float *values, int *ids, void *stream) {
+    if (!logits || !values || !ids) return set_err(G2_ERR_ARG, "g2k_topk: null argument");
+    if (n < 1 || k < 1 || k > G2_MAX_TOPK || k > n)
+        return set_err(G2_ERR_RANGE, "g2k_topk: need 1 <= k <= min(%d, n), n >= 1 (k %d, n %d)", G2_MAX_TOPK, k, n);
+    launch_topk(logits, n, k, values, ids, (cudaStream_t)stream);
     CKL();
     return G2_OK;
 }

@@ -108,6 +108,9 @@ void launch_set_ints(int *p, int a, int b, int c, int d, cudaStream_t st);
 // sample_next_token on the device (g2_sample_dev.cu): token -> out[0].
 void launch_sample(const float *logits, float *work, int V, const int *ctx, int n_ctx, int forbid_eos,
                    float temperature, int top_k, float rep_penalty, double u, int *out, cudaStream_t st);
+// The k (<= G2_MAX_TOPK) largest of logits[0..V) on the device (g2_sample_dev.cu):
+// vals / idx [k], the larger value first, equal values by the smaller index.
+void launch_topk(const float *logits, int V, int k, float *vals, int *idx, cudaStream_t st);
 
 template <typename WT>
 void launch_embed(const WT *wte, const WT *wpe, Rows rows, float *h, int E, int V, int n_pos, int nrows,

@@ -203,7 +203,133 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
     if (t == 0) a.out[0] = ired[0] == INT_MAX ? V - 1 : ired[0];
 }
 
+// The k (<= G2_MAX_TOPK) largest of logits[0..V), in the order of the reference's
+// first-maximum scan (main.c:1898-1904): the larger value first, equal values by
+// the smaller index.  One CTA:
+//   1. the k-th largest key by the radix select of sample_kernel (kth_largest,
+//      main.c:1839-1868): T, and `need`, how many keys equal to T belong to the
+//      top k (every key above T does: there are k - need of them);
+//   2. each thread owns a contiguous block of indices; block counts of keys above
+//      T and equal to T are scanned in index order, so each selected logit gets
+//      its output slot and the keys equal to T are taken in increasing index;
+//   3. a bitonic sort of the k (key, index) pairs in shared memory.
+// -0.0 is keyed as +0.0 (they compare equal as floats); logits are finite.
+constexpr int kTopkThreads = 1024;
+__device__ __forceinline__ unsigned logit_key(float f) { return float_key(f == 0.0f ? 0.0f : f); }
+
+__global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float *logits, int V, int k, float *vals, int *idx) {
+    __shared__ unsigned hist[256];
+    __shared__ unsigned sel[2];                       // prefix, remaining rank
+    __shared__ int wtot[2][32];
+    __shared__ unsigned long long cand[G2_MAX_TOPK];  // (key << 32) | (0xffffffff - index)
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    if (t == 0) {
+        sel[0] = 0;
+        sel[1] = (unsigned)k;
+    }
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int b = t; b < 256; b += kTopkThreads) hist[b] = 0;
+        __syncthreads();
+        const unsigned prefix = sel[0];
+        const unsigned hmask = pass == 0 ? 0u : (0xffffffffu << (shift + 8));
+        for (int i = t; i < V; i += kTopkThreads) {
+            const unsigned key = logit_key(logits[i]);
+            if ((key & hmask) == (prefix & hmask)) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (t == 0) {
+            unsigned need = sel[1];
+            int b = 255;
+            for (; b > 0; --b) {
+                if (hist[b] >= need) break;
+                need -= hist[b];
+            }
+            sel[0] = prefix | ((unsigned)b << shift);
+            sel[1] = need;
+        }
+        __syncthreads();
+    }
+    const unsigned T = sel[0];
+    const int need = (int)sel[1];
+    const int per = (V + kTopkThreads - 1) / kTopkThreads, lo = min(V, t * per), hi = min(V, lo + per);
+    int ngt = 0, neq = 0;
+    for (int i = lo; i < hi; ++i) {
+        const unsigned key = logit_key(logits[i]);
+        ngt += key > T;
+        neq += key == T;
+    }
+    // exclusive prefix sums of both counts over the threads, in index order
+    int sg = ngt, se = neq;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, sg, o), b = __shfl_up_sync(0xffffffffu, se, o);
+        if (lane >= o) {
+            sg += a;
+            se += b;
+        }
+    }
+    if (lane == 31) {
+        wtot[0][warp] = sg;
+        wtot[1][warp] = se;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int a = wtot[0][lane], b = wtot[1][lane];
+        for (int o = 1; o < 32; o <<= 1) {
+            const int x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b, o);
+            if (lane >= o) {
+                a += x;
+                b += y;
+            }
+        }
+        wtot[0][lane] = a - wtot[0][lane];   // exclusive, per warp
+        wtot[1][lane] = b - wtot[1][lane];
+    }
+    __syncthreads();
+    int pg = wtot[0][warp] + sg - ngt, pe = wtot[1][warp] + se - neq;   // this thread's first slots
+    const int base_eq = k - need;
+    for (int i = lo; i < hi && (pg < base_eq || pe < need); ++i) {
+        const unsigned key = logit_key(logits[i]);
+        const unsigned long long c = ((unsigned long long)key << 32) | (0xffffffffu - (unsigned)i);
+        if (key > T) {
+            cand[pg++] = c;
+        } else if (key == T) {
+            if (pe < need) cand[base_eq + pe] = c;
+            ++pe;
+        }
+    }
+    int P = 1;
+    while (P < k) P <<= 1;
+    for (int i = k + t; i < P; i += kTopkThreads) cand[i] = 0ull;   // below every real entry
+    __syncthreads();
+    // bitonic sort, decreasing
+    for (int size = 2; size <= P; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = t; i < P; i += kTopkThreads) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const unsigned long long x = cand[i], y = cand[j];
+                    if ((i & size) == 0 ? x < y : x > y) {
+                        cand[i] = y;
+                        cand[j] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int r = t; r < k; r += kTopkThreads) {
+        const int id = (int)(0xffffffffu - (unsigned)(cand[r] & 0xffffffffu));
+        idx[r] = id;
+        vals[r] = logits[id];
+    }
+}
+
 }  // namespace
+
+void launch_topk(const float *logits, int V, int k, float *vals, int *idx, cudaStream_t st) {
+    topk_kernel<<<1, kTopkThreads, 0, st>>>(logits, V, k, vals, idx);
+}
 
 void launch_sample(const float *logits, float *work, int V, const int *ctx, int n_ctx, int forbid_eos,
                    float temperature, int top_k, float rep_penalty, double u, int *out, cudaStream_t st) {

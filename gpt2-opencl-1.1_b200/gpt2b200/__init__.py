@@ -54,6 +54,7 @@ def _load():
     L.g2_lm_head_rows.argtypes = [vp, C.c_int, vp, C.c_int, C.c_int, vp, vp]
     L.g2_logits.argtypes = [vp, C.c_int, fp, C.c_int]
     L.g2_argmax.argtypes = [vp, C.c_int, C.c_int, ip, fp]
+    L.g2_topk.argtypes = [vp, C.c_int, C.c_int, fp, ip]
     L.g2_sample.argtypes = [fp, C.c_int, ip, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, ip]
     L.g2_sample_device.argtypes = [vp, C.c_int, ip, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, C.c_double, ip]
     L.g2_tokenizer_load.argtypes = [C.c_char_p, C.POINTER(vp)]
@@ -80,6 +81,7 @@ def _load():
     L.g2k_attention_workspace.argtypes = [C.c_int, C.c_int]
     L.g2k_attention_workspace.restype = C.c_size_t
     L.g2k_attention.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, C.c_size_t, vp]
+    L.g2k_topk.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp]
     return L
 
 
@@ -164,6 +166,14 @@ class Engine:
         t, v = C.c_int(), C.c_float()
         check(lib.g2_argmax(self.h, slot, int(forbid_eos), C.byref(t), C.byref(v)))
         return t.value, v.value
+
+    def topk(self, k: int, slot: int = 0):
+        """The k largest logits of `slot` (device): (values [k] decreasing,
+        token ids [k]), equal values by increasing id."""
+        vals, ids = np.zeros(k, np.float32), np.zeros(k, np.int32)
+        check(lib.g2_topk(self.h, slot, k, vals.ctypes.data_as(C.POINTER(C.c_float)),
+                          ids.ctypes.data_as(C.POINTER(C.c_int))))
+        return vals, ids
 
     def sample_device(self, context, forbid_eos: bool = False, temperature: float = 0.0, top_k: int = 0,
                       rep_penalty: float = 1.0, u: float = 0.0, slot: int = 0) -> int:
@@ -305,6 +315,11 @@ def matmul_tc(A, B, C_, M, N, K, bias=None, residual=None, gelu=False, precision
 
 def layernorm(x, out, gamma, beta, n_embd, rows, stream=0):
     check(lib.g2k_layernorm(_ptr(x), _ptr(out), _ptr(gamma), _ptr(beta), n_embd, rows, C.c_void_p(stream)))
+
+
+def topk(logits, n, k, values, ids, stream=0):
+    """g2k_topk on device tensors: the k largest of logits[0..n) into values / ids."""
+    check(lib.g2k_topk(_ptr(logits), n, k, _ptr(values), _ptr(ids), C.c_void_p(stream)))
 
 
 def attention_workspace(n_head: int, max_seq: int) -> int:

@@ -103,6 +103,14 @@ int g2_logits(g2_engine *e, int slot, float *host, int n);
  * (main.c:1898-1904); forbid_eos excludes G2_EOS (main.c:1882). */
 int g2_argmax(g2_engine *e, int slot, int forbid_eos, int *token, float *value);
 
+/* The k largest logits of `slot` over logits[0..vocab_size), found on the
+ * device (1 <= k <= min(G2_MAX_TOPK, vocab_size)): values[0..k) in decreasing
+ * order with their token ids, equal values by increasing id (the order of the
+ * first-maximum scan, main.c:1898-1904), so values[k-1] is kth_largest(logits,
+ * k) (main.c:1839-1868) and ids[0] is the greedy token.  values and ids are host
+ * arrays of k entries; 2 k values come back instead of the vocab_size logits. */
+int g2_topk(g2_engine *e, int slot, int k, float *values, int *ids);
+
 /* sample_next_token (main.c:1872-1939) on host logits[0..vocab_size): EOS mask,
  * repetition penalty over the unique context ids, then greedy (temperature
  * <= 0, first max) or temperature + top-k (<= G2_MAX_TOPK) + C rand() draw. */
@@ -219,6 +227,12 @@ size_t g2k_attention_workspace(int n_head, int max_seq);
  * Workspace rules as g2k_matvec. */
 int g2k_attention(const float *q, const float *K, const float *V, float *out, int n_head,
                   int max_seq, int T_kv, void *workspace, size_t workspace_bytes, void *stream);
+
+/* The kernel of g2_topk on device pointers: the k (1 <= k <= min(G2_MAX_TOPK, n))
+ * largest of logits[0..n), values[0..k) decreasing with their indices ids[0..k),
+ * equal values by increasing index (-0.0 and +0.0 are equal; logits finite).
+ * Asynchronous on `stream`. */
+int g2k_topk(const float *logits, int n, int k, float *values, int *ids, void *stream);
 
 #ifdef __cplusplus
 }
