@@ -1034,6 +1034,367 @@ __global__ void __launch_bounds__(kAsThreads, 3)
 }
 
 // ------------------------------------------------------------------------------
+// Single-query attention of a batched decode step over fp16 caches, one warp per
+// run of keys (attn_scores_1q, attn_softmax_1q, attn_out_1q, math.cl:388-476, for
+// one token of each of R sequences).
+//
+// The work items are (row, head, 64-key chunk), row-major then head-major, and
+// warp w of W takes items [w I / W, (w + 1) I / W).  W is the number of (row,
+// head) runs times the whole number of warps each can have (at least one; fewer
+// warps than runs: the warps' shares hold several runs), so when the rows have
+// equal positions every warp streams exactly one run, or an equal share of one.
+// Each warp:
+//   * requests its chunks' K and V tiles (64 rows x 128 B, 128-byte swizzle) by
+//     TMA into its own three-stage ring, the first stages before the wait for
+//     the previous kernel (the cached rows before each step's position were
+//     written by earlier steps);
+//   * sums q from c_attn's split-K partials at a run's start, and at a run's last
+//     chunk the new K and V rows, which it appends to the cache (split_kv,
+//     math.cl:367-383) and patches into the staged tiles;
+//   * computes the chunk's scores (K tile x q) and P.V (P x V tile, V read
+//     transposed by ldmatrix) with m16n8k16 tensor-core operations, fp16 operands
+//     (q and the probabilities rounded to fp16, as the fp16 engine's GEMM operands
+//     are) and fp32 accumulation, and keeps the run's online softmax -- running
+//     maximum, sum and the 64 outputs, the latter in the MMA accumulators --
+//     in registers;
+//   * at the end of its share of a run writes the output (and the next GEMM's
+//     operand), or hands in a partial that the last warp of the run to arrive
+//     merges in slice order.
+// After the set-up no CTA-wide barrier is taken: a warp never waits for another.
+// Every wait is bounded; on expiry the warp records G2_ERR_TIMEOUT in a.err, waits
+// (bounded) for its own copies in flight and returns.
+// ------------------------------------------------------------------------------
+namespace {
+constexpr int kAwWarps = 4;                        // warps per CTA
+constexpr int kAwStages = 3;                       // ring stages per warp
+constexpr int kAwChunk = 64;                       // keys per item (one 64-row TMA box of K and of V)
+constexpr int kAwTile = kAwChunk * kHeadDim * 2;   // bytes of one staged K (or V) tile: 8 KB
+constexpr int kAwCols = 3 * kHeadDim / 32;         // q, k, v columns of a head per lane: 6
+}  // namespace
+size_t attn_warp_smem() { return (size_t)kAwWarps * kAwStages * 2 * kAwTile + 1024; }
+
+__global__ void __launch_bounds__(kAwWarps * 32, 1)
+    attn_warp_kernel(AttnArgs<__half> a, int nrows, int wmax, const __grid_constant__ CUtensorMap mk,
+                     const __grid_constant__ CUtensorMap mv) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char *ring =   // [warp][stage][K tile, V tile], 1024-byte aligned
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ u64a full[kAwWarps][kAwStages];
+    __shared__ float qs[kAwWarps][kHeadDim];
+    __shared__ float knew[kAwWarps][2][kHeadDim];
+    __shared__ int nch[kAsMaxRows], off[kAsMaxRows + 1], rpos[kAsMaxRows], rslot[kAsMaxRows];
+    __shared__ int s_runs;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, NH = a.kv.n_head;
+    if (tid == 0) {
+        for (int w = 0; w < kAwWarps; ++w)
+            for (int s = 0; s < kAwStages; ++s)
+                asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(as_smem(&full[w][s])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // chunks per row (of its keys, per head), their prefix sums, positions and slots
+    for (int r = tid; r < nrows; r += kAwWarps * 32) {
+        const int T = a.rows.pos[r] + 1, sl = a.rows.slot[r];
+        const bool ok = G2_BOUNDS(T >= 1 && T <= a.kv.max_seq && sl >= 0 && sl < a.kv.n_slots, 108);
+        nch[r] = ok ? (T + kAwChunk - 1) / kAwChunk : 0;
+        rpos[r] = T - 1;
+        rslot[r] = sl;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int runs = 0;
+        off[0] = 0;
+        for (int r = 0; r < nrows; ++r) {
+            off[r + 1] = off[r] + NH * nch[r];
+            runs += nch[r] ? NH : 0;
+        }
+        s_runs = runs;
+    }
+    __syncthreads();
+    // W <= I, so that every warp of the partition holds at least one item (the part
+    // counts of the merge rely on it)
+    const long long I = off[nrows];
+    const int runs = s_runs;
+    long long Wl = runs == 0 ? 0 : (runs <= wmax ? (long long)runs * (wmax / runs) : (long long)wmax);
+    if (Wl > I) Wl = I;
+    const int W = (int)Wl, w = blockIdx.x * kAwWarps + warp;
+    const int i0 = w < W ? (int)((long long)w * I / W) : 0, i1 = w < W ? (int)((long long)(w + 1) * I / W) : 0;
+    unsigned char *wring = ring + (size_t)warp * kAwStages * 2 * kAwTile;
+    u64a *wfull = full[warp];
+    struct Cur {
+        int r, h, ch;
+    };
+    auto place = [&](int i) {
+        Cur u;
+        u.r = 0;
+        while (off[u.r + 1] <= i) ++u.r;
+        const int j = i - off[u.r];
+        u.h = j / nch[u.r];
+        u.ch = j - u.h * nch[u.r];
+        return u;
+    };
+    auto next = [&](Cur &u) {
+        if (++u.ch == nch[u.r]) {
+            u.ch = 0;
+            if (++u.h == NH) {
+                u.h = 0;
+                do ++u.r;
+                while (u.r < nrows && nch[u.r] == 0);
+            }
+        }
+    };
+    auto kv_base = [&](int r, int h) -> long long {
+        return (long long)rslot[r] * a.kv.slot_stride + (long long)a.layer * a.kv.layer_stride +
+               (long long)h * a.kv.max_seq * kHeadDim;
+    };
+    // lane 0: request item (cursor u, index i)'s K and V tiles into stage (i - i0) % kAwStages
+    auto issue = [&](const Cur &u, int i) {
+        const int s = (i - i0) % kAwStages;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(as_smem(&wfull[s])),
+                     "r"((unsigned)(2 * kAwTile))
+                     : "memory");
+        const int row = (int)(kv_base(u.r, u.h) / kHeadDim) + u.ch * kAwChunk;
+        as_tma2d(wring + (size_t)s * 2 * kAwTile, &mk, 0, row, &wfull[s]);
+        as_tma2d(wring + (size_t)s * 2 * kAwTile + kAwTile, &mv, 0, row, &wfull[s]);
+    };
+    Cur iu{0, 0, 0};   // lane 0's issue cursor
+    if (lane == 0 && i0 < i1) {
+        iu = place(i0);
+        for (int i = i0; i < i1 && i < i0 + kAwStages; ++i) {
+            issue(iu, i);
+            next(iu);
+        }
+    }
+    pdl_wait();
+    pdl_launch();
+    if (i0 >= i1) return;   // a warp without items
+    const int E = a.qkv_stride / 3;
+    const int g = lane >> 2, t = lane & 3, q8 = lane >> 3;
+    const int lrow = (q8 & 1) * 8 + (lane & 7);   // tile row (within 16) this lane addresses: K (A of the scores)
+    const int krow = (q8 >> 1) * 8 + (lane & 7);  // and V (A of V^T P, read transposed)
+    // P.V accumulators: column 0 (lanes t == 0) of m-tile dm holds dims 16 dm + g (o[dm][0]) and
+    // 16 dm + g + 8 (o[dm][2])
+    float o[4][4];
+    float Mr = -FLT_MAX, Lr = 0.0f;               // the run's running maximum and sum
+    unsigned qb[4][2];                            // q (column 0 of the scores' B operand): dims 16 k + 2 t, + 8
+    Cur u = place(i0);
+    for (int i = i0; i < i1; ++i, next(u)) {
+        const int r = u.r, h = u.h, ch = u.ch;
+        const int T = rpos[r] + 1, pos = T - 1, j0 = ch * kAwChunk, nj = min(kAwChunk, T - j0);
+        const int s = (i - i0) % kAwStages;
+        const bool fresh = i == i0 || ch == 0;   // a new (row, head) run of this warp
+        if (fresh) {
+            Mr = -FLT_MAX;
+            Lr = 0.0f;
+#pragma unroll
+            for (int dm = 0; dm < 4; ++dm) o[dm][0] = o[dm][1] = o[dm][2] = o[dm][3] = 0.0f;
+            // q, and the new k and v when this warp's share holds the run's last chunk (the one
+            // with the step's position), from c_attn's partials: lane takes columns lane + 32 j
+            // of the head's 192; all their partial loads are issued before any is summed, and
+            // each column is summed in split order
+            const bool kv_mine = off[r] + (long long)h * nch[r] + nch[r] - 1 < i1;
+            const float *pcv[kAwCols];
+            int nsv[kAwCols], nsmax = 0;
+            float acc[kAwCols];
+#pragma unroll
+            for (int j = 0; j < kAwCols; ++j) {
+                const int cc = lane + 32 * j, pt = cc >> 6, d = cc & (kHeadDim - 1);
+                const size_t col = (size_t)pt * E + h * kHeadDim + d;
+                const bool need = pt == 0 || kv_mine;
+                pcv[j] = a.qpart + (size_t)r * a.qkv_stride + col;
+                nsv[j] = need ? a.qsi.at((int)col) : 0;
+                nsmax = max(nsmax, nsv[j]);
+                acc[j] = 0.0f;
+            }
+            constexpr int QB = 8;   // partials per column per round
+            for (int s0 = 0; s0 < nsmax; s0 += QB) {
+                float pv[kAwCols][QB];
+#pragma unroll
+                for (int j = 0; j < kAwCols; ++j)
+#pragma unroll
+                    for (int k = 0; k < QB; ++k) pv[j][k] = s0 + k < nsv[j] ? pcv[j][(size_t)(s0 + k) * a.qtotal] : 0.0f;
+#pragma unroll
+                for (int j = 0; j < kAwCols; ++j)
+#pragma unroll
+                    for (int k = 0; k < QB; ++k)
+                        if (s0 + k < nsv[j]) acc[j] = s0 + k == 0 ? pv[j][k] : acc[j] + pv[j][k];
+            }
+#pragma unroll
+            for (int j = 0; j < kAwCols; ++j) {
+                if (!nsv[j]) continue;
+                const int cc = lane + 32 * j, pt = cc >> 6, d = cc & (kHeadDim - 1);
+                const float v = acc[j] + tof(a.qbias[(size_t)pt * E + h * kHeadDim + d]);
+                if (pt == 0) {
+                    qs[warp][d] = v * 0.125f;   // 1/sqrt(64)
+                } else {   // K / V append at the cache's precision
+                    const __half stv = __float2half_rn(v);
+                    __half *dst = reinterpret_cast<__half *>(pt == 1 ? a.kv.k : a.kv.v) + kv_base(r, h) +
+                                  (size_t)pos * kHeadDim + d;
+                    *dst = stv;
+                    knew[warp][pt - 1][d] = __half2float(stv);
+                }
+            }
+            __syncwarp();
+            // q as column 0 of the scores' B operand (lanes of group 0), fp16
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                qb[k][0] = g == 0 ? pack_h2(qs[warp][16 * k + 2 * t], qs[warp][16 * k + 2 * t + 1]) : 0u;
+                qb[k][1] = g == 0 ? pack_h2(qs[warp][16 * k + 8 + 2 * t], qs[warp][16 * k + 9 + 2 * t]) : 0u;
+            }
+        }
+        // this item's K and V tiles (bounded wait)
+        const bool ok = as_wait(&wfull[s], (unsigned)(((i - i0) / kAwStages) & 1));
+        if (__any_sync(0xffffffffu, !ok)) {
+            if (lane == 0) {
+                atomicCAS(a.err, 0, G2_ERR_TIMEOUT);
+                // copies this warp issued and nobody consumed: wait for them (bounded) before exiting
+                for (int k = i + 1; k < i1 && k < i + kAwStages; ++k)
+                    as_wait(&wfull[(k - i0) % kAwStages], (unsigned)(((k - i0) / kAwStages) & 1));
+            }
+            return;
+        }
+        const unsigned kb = as_smem(wring + (size_t)s * 2 * kAwTile), vb = kb + kAwTile;
+        const int jpos = pos - j0;   // the key at pos (this step's), if in this chunk
+        if (jpos >= 0 && jpos < nj) {   // its K and V rows into the staged tiles, from the summed partials
+#pragma unroll
+            for (int e = lane; e < 2 * kHeadDim; e += 32) {
+                const int d = e & (kHeadDim - 1), w2 = e >> 6;
+                __half *dst = reinterpret_cast<__half *>(wring + (size_t)s * 2 * kAwTile + (w2 ? kAwTile : 0) +
+                                                         swz128(jpos, d >> 3) + (d & 7) * 2);
+                *dst = __float2half_rn(knew[warp][w2][d]);
+            }
+            // these generic writes come before the TMA that next fills this stage
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+        }
+        // scores with the keys on the MMA's m and q as column 0 of B: keys 16 mt + g (sd[mt][0])
+        // and 16 mt + g + 8 (sd[mt][2]) in lanes t == 0
+        float sd[4][4];
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+            sd[mt][0] = sd[mt][1] = sd[mt][2] = sd[mt][3] = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {   // dims 16 k .. 16 k + 15
+                unsigned af[4];
+                ldsm_x4(af, kb + swz128(16 * mt + lrow, 2 * k + (q8 >> 1)));
+                mma16816(sd[mt], af, qb[k][0], qb[k][1]);
+            }
+        }
+        // online softmax over the run, among the lanes t == 0 (the others take no part)
+        float mloc = -FLT_MAX;
+        if (t == 0) {
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                if (nj == kAwChunk || 16 * mt + g < nj) mloc = fmaxf(mloc, sd[mt][0]);
+                if (nj == kAwChunk || 16 * mt + g + 8 < nj) mloc = fmaxf(mloc, sd[mt][2]);
+            }
+        }
+        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 4));
+        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 8));
+        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 16));
+        const float mn = fmaxf(Mr, mloc);
+        const float sc = __expf(Mr - mn);   // 0 at a run's first chunk
+        float p0[4], p1[4], ls = 0.0f;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+            p0[mt] = t == 0 && (nj == kAwChunk || 16 * mt + g < nj) ? __expf(sd[mt][0] - mn) : 0.0f;
+            p1[mt] = t == 0 && (nj == kAwChunk || 16 * mt + g + 8 < nj) ? __expf(sd[mt][2] - mn) : 0.0f;
+            ls += p0[mt] + p1[mt];
+        }
+        ls += __shfl_xor_sync(0xffffffffu, ls, 4);
+        ls += __shfl_xor_sync(0xffffffffu, ls, 8);
+        ls += __shfl_xor_sync(0xffffffffu, ls, 16);
+        Lr = Lr * sc + ls;
+        Mr = mn;
+#pragma unroll
+        for (int dm = 0; dm < 4; ++dm) {   // columns 1-7 of the accumulators stay 0
+            o[dm][0] *= sc;
+            o[dm][2] *= sc;
+        }
+        // P.V as V^T P: the dims on the MMA's m (V read transposed by ldmatrix as the A operand),
+        // P as column 0 of B (lanes of group 0 hold keys 2 t, + 1 and 2 t + 8, + 9 of each step)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {   // keys 16 kk .. 16 kk + 15
+            const float pa = __shfl_sync(0xffffffffu, p0[kk], 8 * t), pb = __shfl_sync(0xffffffffu, p0[kk], 8 * t + 4);
+            const float pc = __shfl_sync(0xffffffffu, p1[kk], 8 * t), pd = __shfl_sync(0xffffffffu, p1[kk], 8 * t + 4);
+            const unsigned b0 = g == 0 ? pack_h2(pa, pb) : 0u, b1 = g == 0 ? pack_h2(pc, pd) : 0u;
+#pragma unroll
+            for (int dm = 0; dm < 4; ++dm) {   // dims 16 dm .. 16 dm + 15
+                unsigned af[4];
+                ldsm_x4_t(af, vb + swz128(16 * kk + krow, 2 * dm + (q8 & 1)));
+                mma16816(o[dm], af, b0, b1);
+            }
+        }
+        // the stage is read: request the item kAwStages ahead into it
+        __syncwarp();
+        if (lane == 0 && i + kAwStages < i1) {
+            issue(iu, i + kAwStages);
+            next(iu);
+        }
+        // the end of this (row, head) in this warp: finish it, or hand in a partial
+        if (ch == nch[r] - 1 || i == i1 - 1) {
+            const long long u0 = off[r] + (long long)h * nch[r];   // the run's first item
+            const int c0 = (int)(((u0 + 1) * W - 1) / I);          // warps holding its first and last items
+            const int c1 = (int)(((u0 + nch[r]) * W - 1) / I);
+            const int nparts = c1 - c0 + 1, seg = w - c0;
+            const size_t ob = (size_t)r * a.out_stride + h * kHeadDim;
+            if (nparts == 1) {
+                if (t == 0) {
+                    const float inv = 1.0f / Lr;
+#pragma unroll
+                    for (int dm = 0; dm < 4; ++dm)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const size_t oi = ob + 16 * dm + g + 8 * e;
+                            const float v = o[dm][2 * e] * inv;
+                            a.out[oi] = v;
+                            put_operand(a.op, oi, v);
+                        }
+                }
+            } else {
+                float *P = a.partial + (((size_t)r * NH + h) * a.max_splits + seg) * (kHeadDim + 2);
+                if (t == 0)
+#pragma unroll
+                    for (int dm = 0; dm < 4; ++dm) {
+                        P[2 + 16 * dm + g] = o[dm][0];
+                        P[2 + 16 * dm + g + 8] = o[dm][2];
+                    }
+                if (lane == 0) {
+                    P[0] = Mr;
+                    P[1] = Lr;
+                }
+                __threadfence();   // this warp's partial before its arrival
+                __syncwarp();
+                unsigned *ctr = a.counters + (size_t)r * NH + h;
+                unsigned prev = 0;
+                if (lane == 0) prev = atomicAdd(ctr, 1u);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev == (unsigned)(nparts - 1)) {   // the last to arrive: merge the parts in slice order
+                    __threadfence();
+                    const float *P0 = a.partial + ((size_t)r * NH + h) * a.max_splits * (kHeadDim + 2);
+                    float M = -FLT_MAX;
+                    for (int k = 0; k < nparts; ++k) M = fmaxf(M, __ldcg(P0 + (size_t)k * (kHeadDim + 2)));
+#pragma unroll
+                    for (int dd = 0; dd < 2; ++dd) {
+                        const int d = lane + 32 * dd;
+                        float L = 0.0f, O = 0.0f;
+                        for (int k = 0; k < nparts; ++k) {
+                            const float *Pk = P0 + (size_t)k * (kHeadDim + 2);
+                            const float wk = expf(__ldcg(Pk) - M);
+                            L = fmaf(__ldcg(Pk + 1), wk, L);
+                            O = fmaf(__ldcg(Pk + 2 + d), wk, O);
+                        }
+                        a.out[ob + d] = O / L;
+                        put_operand(a.op, ob + d, O / L);
+                    }
+                    __syncwarp();
+                    if (lane == 0) *ctr = 0u;
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------
 // Causal attention of a prompt (prefill): the per-query loop of prefill()
 // (main.c:1759-1763 over attn_scores_1q, attn_softmax_1q, attn_out_1q,
 // math.cl:388-476) for all query rows of one slot in one launch.
@@ -1526,6 +1887,38 @@ static void launch_attn_stream(const AttnArgs<KT> &a, int nrows, const CUtensorM
     launch_pdl(attn_stream_kernel<KT, MMA>, dim3((unsigned)G), dim3(kAsThreads), smem, st, a, nrows, mk, mv);
 }
 
+// One warp-per-run attention launch (fp16 caches): as many CTAs as fit at once, wmax =
+// their warps (per device, with the shared-memory limit raised once per device).
+static void launch_attn_warp(const AttnArgs<__half> &a, int nrows, const CUtensorMap &mk, const CUtensorMap &mv,
+                             cudaStream_t st) {
+    static unsigned long long attr_set = 0;
+    static int per_sm[64];
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const size_t smem = attn_warp_smem();
+    if (dev >= 64 || !(__atomic_load_n(&attr_set, __ATOMIC_ACQUIRE) >> dev & 1ull)) {
+        cudaFuncSetAttribute(attn_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        int n = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_warp_kernel, kAwWarps * 32, smem);
+        if (dev < 64) {
+            per_sm[dev] = n > 0 ? n : 1;
+            __atomic_fetch_or(&attr_set, 1ull << dev, __ATOMIC_RELEASE);
+        }
+    }
+    const int G = sms * (dev < 64 ? per_sm[dev] : 1);
+    launch_pdl(attn_warp_kernel, dim3((unsigned)G), dim3(kAwWarps * 32), smem, st, a, nrows, G * kAwWarps, mk, mv);
+}
+
+// G2_ATTN_STREAM=1: fp16 decode attention by the streamed kernel instead of the warp-per-run one.
+static bool attn_stream_forced() {
+    static const int v = [] {
+        const char *e = getenv("G2_ATTN_STREAM");
+        return e && atoi(e) > 0 ? 1 : 0;
+    }();
+    return v != 0;
+}
+
 template <typename KT>
 void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int layer, Rows rows, int nrows,
                       float *out, int out_stride, float *partial, unsigned *counters, int max_pos_hint,
@@ -1551,6 +1944,14 @@ void launch_attention(const float *qkv, int qkv_stride, const KVLayout &kv, int 
         // decode rows with c_attn's partials: the streamed kernel, as many CTAs as fit at once
         // (fp16 caches with their tensor maps: the tensor-core instantiation)
         a.max_splits = (kv.max_seq + as_chunk<KT>() - 1) / as_chunk<KT>();   // partial slots per (row, head)
+        if constexpr (sizeof(KT) == 2) {
+            if (qp.kmap && qp.vmap && !attn_stream_forced()) {
+                a.max_splits = (kv.max_seq + kAwChunk - 1) / kAwChunk;
+                launch_attn_warp(a, nrows, *static_cast<const CUtensorMap *>(qp.kmap),
+                                 *static_cast<const CUtensorMap *>(qp.vmap), st);
+                return;
+            }
+        }
         if (sizeof(KT) == 2 && qp.kmap && qp.vmap)
             launch_attn_stream<KT, sizeof(KT) == 2>(a, nrows, *static_cast<const CUtensorMap *>(qp.kmap),
                                                      *static_cast<const CUtensorMap *>(qp.vmap), st);
