@@ -495,47 +495,112 @@ __device__ __forceinline__ float4 split_sum(const float *part, int splits, long 
 // per thread (N % 4 == 0); used when a GEMM ran with split-K.
 template <typename WT>
 __global__ void tc_reduce_kernel(const float *part, SplitInfo si, int R, int N, Epi<WT> e, OperandOut op) {
-    pdl_wait();
-    pdl_launch();
     const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
     const long long total = (long long)R * N;
-    if (i >= total) return;
-    const int r = (int)(i / N), n = (int)(i % N);
+    const bool in = i < total;
+    const int r = in ? (int)(i / N) : 0, n = in ? (int)(i % N) : 0;
+    // the bias is not written by the previous kernels: read it before the wait
+    float bv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (in && (e.epi & EPI_BIAS))
+#pragma unroll
+        for (int j = 0; j < 4; ++j) bv[j] = tof(e.bias[n + j]);
+    pdl_wait();
+    pdl_launch();
+    if (!in) return;
+    Epi<WT> en = e;   // the rest of the epilogue, with the bias added here
+    en.epi &= ~EPI_BIAS;
     const float4 acc = split_sum(part, si.at(n), total, i);
-    put_operand(op, (size_t)i, e.apply(r, n, acc.x));
-    put_operand(op, (size_t)i + 1, e.apply(r, n + 1, acc.y));
-    put_operand(op, (size_t)i + 2, e.apply(r, n + 2, acc.z));
-    put_operand(op, (size_t)i + 3, e.apply(r, n + 3, acc.w));
+    put_operand(op, (size_t)i, en.apply(r, n, acc.x + bv[0]));
+    put_operand(op, (size_t)i + 1, en.apply(r, n + 1, acc.y + bv[1]));
+    put_operand(op, (size_t)i + 2, en.apply(r, n + 2, acc.z + bv[2]));
+    put_operand(op, (size_t)i + 3, en.apply(r, n + 3, acc.w + bv[3]));
 }
 
 // The same for a GEMM whose output rows (the residual stream) feed a
 // LayerNorm: one CTA per row sums the splits, applies the epilogue (out =
-// the residual stream), then takes the row's LayerNorm (math.cl:283-311:
-// mean, then the mean square deviation, eps 1e-5) and writes the normalised
-// row, times gamma plus beta, as the next GEMM's operand.  N % 4 == 0,
-// N <= 2048.
+// the residual stream; no K/V append), then takes the row's LayerNorm
+// (math.cl:283-311: mean, then the mean square deviation, eps 1e-5) and writes
+// the normalised row, times gamma plus beta, as the next GEMM's operand.
+// N % 4 == 0, N <= 2048.  The bias, gamma and beta (not written by the
+// previous kernels) are read before the wait for the previous kernel; after it,
+// the partials of both of a thread's column groups and the residual are all
+// requested before any is summed, so the row costs one memory round trip.
 template <typename WT>
 __global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, SplitInfo si, int R, int N, Epi<WT> e,
                                                            const WT *g, const WT *b, OperandOut op) {
-    pdl_wait();
-    pdl_launch();
     __shared__ float sh[8];
     const int r = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const long long total = (long long)R * N;
+    int nn[2];
+    bool in[2];
+    float wb[8], wg[8], wbe[8];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        nn[k] = (t + k * 256) * 4;
+        in[k] = nn[k] < N;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            wb[4 * k + j] = in[k] && (e.epi & EPI_BIAS) ? tof(e.bias[nn[k] + j]) : 0.0f;
+            wg[4 * k + j] = in[k] ? tof(g[nn[k] + j]) : 0.0f;
+            wbe[4 * k + j] = in[k] ? tof(b[nn[k] + j]) : 0.0f;
+        }
+    }
+    pdl_wait();
+    pdl_launch();
+    float4 res[2], acc[2];
+    int ns[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        res[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        ns[k] = in[k] ? si.at(nn[k]) : 0;
+        if (in[k] && (e.epi & EPI_RESID))
+            res[k] = *reinterpret_cast<const float4 *>(e.resid + (size_t)r * N + nn[k]);
+    }
+    const int nsm = ns[0] > ns[1] ? ns[0] : ns[1];
+    for (int s0 = 0; s0 < nsm; s0 += kSumBatch) {   // in split order, as split_sum
+        float4 p[2][kSumBatch];
+#pragma unroll
+        for (int k = 0; k < kSumBatch; ++k)
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+                if (s0 + k < ns[c])
+                    p[c][k] = *reinterpret_cast<const float4 *>(part + (size_t)(s0 + k) * total + (size_t)r * N + nn[c]);
+#pragma unroll
+        for (int k = 0; k < kSumBatch; ++k)
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+                if (s0 + k < ns[c]) {
+                    if (s0 + k == 0) {
+                        acc[c] = p[c][0];
+                    } else {
+                        acc[c].x += p[c][k].x;
+                        acc[c].y += p[c][k].y;
+                        acc[c].z += p[c][k].z;
+                        acc[c].w += p[c][k].w;
+                    }
+                }
+    }
+    // the epilogue (Epi::apply without the K/V append): + bias, GELU, residual + v, stored
     float v[8];
     float s = 0.0f;
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-        const int n = (t + k * 256) * 4;
-        if (n < N) {
-            const long long i = (long long)r * N + n;
-            const float4 acc = split_sum(part, si.at(n), total, i);
-            v[4 * k] = e.apply(r, n, acc.x);
-            v[4 * k + 1] = e.apply(r, n + 1, acc.y);
-            v[4 * k + 2] = e.apply(r, n + 2, acc.z);
-            v[4 * k + 3] = e.apply(r, n + 3, acc.w);
-            s += (v[4 * k] + v[4 * k + 1]) + (v[4 * k + 2] + v[4 * k + 3]);
+        if (!in[k]) continue;
+        const float a4[4] = {acc[k].x, acc[k].y, acc[k].z, acc[k].w};
+        const float r4[4] = {res[k].x, res[k].y, res[k].z, res[k].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float x = a4[j];
+            if (e.epi & EPI_BIAS) x += wb[4 * k + j];
+            if (e.epi & EPI_GELU) x = gelu_f(x);
+            if (e.epi & EPI_RESID) x = r4[j] + x;
+            v[4 * k + j] = x;
         }
+        if (!(e.epi & EPI_NOSTORE))
+            *reinterpret_cast<float4 *>(e.out + (size_t)r * N + nn[k]) =
+                make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        s += (v[4 * k] + v[4 * k + 1]) + (v[4 * k + 2] + v[4 * k + 3]);
     }
     auto block_sum = [&](float x) {
 #pragma unroll
@@ -552,7 +617,7 @@ __global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, Sp
     float q = 0.0f;
 #pragma unroll
     for (int k = 0; k < 2; ++k)
-        if ((t + k * 256) * 4 < N)
+        if (in[k])
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const float d = v[4 * k + j] - mean;
@@ -560,13 +625,11 @@ __global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, Sp
             }
     const float rstd = 1.0f / sqrtf(block_sum(q) / (float)N + 1e-5f);
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const int n = (t + k * 256) * 4;
-        if (n < N)
+    for (int k = 0; k < 2; ++k)
+        if (in[k])
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-                put_operand(op, (size_t)r * N + n + j, (v[4 * k + j] - mean) * rstd * tof(g[n + j]) + tof(b[n + j]));
-    }
+                put_operand(op, (size_t)r * N + nn[k] + j, (v[4 * k + j] - mean) * rstd * wg[4 * k + j] + wbe[4 * k + j]);
 }
 
 // x -> (hi, lo) tf32 pair, or x -> fp16.
@@ -978,7 +1041,7 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
     if (si_out) *si_out = a.si;
     if (!a.si.split()) return 1;   // the GEMM applied the epilogue itself
     if (defer_reduce) return 1;    // the consumer sums the partials
-    if (ln_g && w.N <= 2048 && (w.N % 4) == 0) {   // sum the splits, epilogue and the next LayerNorm in one kernel
+    if (ln_g && w.N <= 2048 && (w.N % 4) == 0 && !(a.e.epi & EPI_KV)) {   // splits, epilogue and the next LayerNorm
         launch_pdl(tc_reduce_ln_kernel<WT>, dim3((unsigned)R), dim3(256), 0, st, (const float *)partial, a.si, R, w.N,
                    a.e, ln_g, ln_b, ln_op);
         if (ln_done) *ln_done = true;
