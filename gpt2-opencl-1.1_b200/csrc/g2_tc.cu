@@ -525,17 +525,20 @@ __global__ void tc_reduce_kernel(const float *part, SplitInfo si, int R, int N, 
 // previous kernels) are read before the wait for the previous kernel; after it,
 // the partials of both of a thread's column groups and the residual are all
 // requested before any is summed, so the row costs one memory round trip.
-template <typename WT>
-__global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, SplitInfo si, int R, int N, Epi<WT> e,
-                                                           const WT *g, const WT *b, OperandOut op) {
+// NG: groups of 1024 columns a CTA covers (N <= 1024 NG); the one-group instantiation
+// (small and medium widths) keeps two CTAs per SM for many-row prefill passes.
+template <typename WT, int NG>
+__global__ void __launch_bounds__(256, NG == 1 ? 2 : 1)
+    tc_reduce_ln_kernel(const float *part, SplitInfo si, int R, int N, Epi<WT> e, const WT *g, const WT *b,
+                        OperandOut op) {
     __shared__ float sh[8];
     const int r = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const long long total = (long long)R * N;
-    int nn[2];
-    bool in[2];
-    float wb[8], wg[8], wbe[8];
+    int nn[NG];
+    bool in[NG];
+    float wb[4 * NG], wg[4 * NG], wbe[4 * NG];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < NG; ++k) {
         nn[k] = (t + k * 256) * 4;
         in[k] = nn[k] < N;
 #pragma unroll
@@ -547,29 +550,31 @@ __global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, Sp
     }
     pdl_wait();
     pdl_launch();
-    float4 res[2], acc[2];
-    int ns[2];
+    float4 res[NG], acc[NG];
+    int ns[NG];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < NG; ++k) {
         res[k] = make_float4(0.f, 0.f, 0.f, 0.f);
         acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
         ns[k] = in[k] ? si.at(nn[k]) : 0;
         if (in[k] && (e.epi & EPI_RESID))
             res[k] = *reinterpret_cast<const float4 *>(e.resid + (size_t)r * N + nn[k]);
     }
-    const int nsm = ns[0] > ns[1] ? ns[0] : ns[1];
+    int nsm = 0;
+#pragma unroll
+    for (int k = 0; k < NG; ++k) nsm = ns[k] > nsm ? ns[k] : nsm;
     for (int s0 = 0; s0 < nsm; s0 += kSumBatch) {   // in split order, as split_sum
-        float4 p[2][kSumBatch];
+        float4 p[NG][kSumBatch];
 #pragma unroll
         for (int k = 0; k < kSumBatch; ++k)
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+            for (int c = 0; c < NG; ++c)
                 if (s0 + k < ns[c])
                     p[c][k] = *reinterpret_cast<const float4 *>(part + (size_t)(s0 + k) * total + (size_t)r * N + nn[c]);
 #pragma unroll
         for (int k = 0; k < kSumBatch; ++k)
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+            for (int c = 0; c < NG; ++c)
                 if (s0 + k < ns[c]) {
                     if (s0 + k == 0) {
                         acc[c] = p[c][0];
@@ -582,10 +587,10 @@ __global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, Sp
                 }
     }
     // the epilogue (Epi::apply without the K/V append): + bias, GELU, residual + v, stored
-    float v[8];
+    float v[4 * NG];
     float s = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < NG; ++k) {
         if (!in[k]) continue;
         const float a4[4] = {acc[k].x, acc[k].y, acc[k].z, acc[k].w};
         const float r4[4] = {res[k].x, res[k].y, res[k].z, res[k].w};
@@ -616,7 +621,7 @@ __global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, Sp
     const float mean = block_sum(s) / (float)N;
     float q = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 2; ++k)
+    for (int k = 0; k < NG; ++k)
         if (in[k])
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -625,7 +630,7 @@ __global__ void __launch_bounds__(256) tc_reduce_ln_kernel(const float *part, Sp
             }
     const float rstd = 1.0f / sqrtf(block_sum(q) / (float)N + 1e-5f);
 #pragma unroll
-    for (int k = 0; k < 2; ++k)
+    for (int k = 0; k < NG; ++k)
         if (in[k])
 #pragma unroll
             for (int j = 0; j < 4; ++j)
@@ -1042,8 +1047,12 @@ int launch_tc_gemm(int kind, const TcWeights &w, const TcRowsOperand &x, int R, 
     if (!a.si.split()) return 1;   // the GEMM applied the epilogue itself
     if (defer_reduce) return 1;    // the consumer sums the partials
     if (ln_g && w.N <= 2048 && (w.N % 4) == 0 && !(a.e.epi & EPI_KV)) {   // splits, epilogue and the next LayerNorm
-        launch_pdl(tc_reduce_ln_kernel<WT>, dim3((unsigned)R), dim3(256), 0, st, (const float *)partial, a.si, R, w.N,
-                   a.e, ln_g, ln_b, ln_op);
+        if (w.N <= 1024)
+            launch_pdl(tc_reduce_ln_kernel<WT, 1>, dim3((unsigned)R), dim3(256), 0, st, (const float *)partial, a.si, R,
+                       w.N, a.e, ln_g, ln_b, ln_op);
+        else
+            launch_pdl(tc_reduce_ln_kernel<WT, 2>, dim3((unsigned)R), dim3(256), 0, st, (const float *)partial, a.si, R,
+                       w.N, a.e, ln_g, ln_b, ln_op);
         if (ln_done) *ln_done = true;
         return 2;
     }
