@@ -1693,30 +1693,33 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmArgs<WT> a) {
 }
 
 // Argmax per row of logits [rows][Vp] (one CTA per row).
-__global__ void __launch_bounds__(256) argmax_rows_kernel(const float *logits, int V, int Vp, int forbid_eos,
-                                                          int *tokens, float *values, int *tok_next, int *pos_next,
-                                                          int *out_tokens, int out_stride, const int *step_ptr) {
+constexpr int kArgThreads = 1024;   // a row of GPT-2's 50,257 logits in two rounds of loads
+constexpr int kArgLoads = 8;        // float4 chunks in flight per thread and round
+__global__ void __launch_bounds__(kArgThreads) argmax_rows_kernel(const float *logits, int V, int Vp, int forbid_eos,
+                                                                  int *tokens, float *values, int *tok_next,
+                                                                  int *pos_next, int *out_tokens, int out_stride,
+                                                                  const int *step_ptr) {
     pdl_wait();
     pdl_launch();
-    __shared__ float wv[8];
-    __shared__ int wi[8];
+    __shared__ float wv[kArgThreads / 32];
+    __shared__ int wi[kArgThreads / 32];
     const int r = blockIdx.x, tid = threadIdx.x;
     const float *L = logits + (size_t)r * Vp;
     float best = -FLT_MAX;
     int besti = INT_MAX;
-    // float4 chunks (rows are Vp = multiple of 4 floats, 16-byte aligned), four in flight per thread
+    // float4 chunks (rows are Vp = multiple of 4 floats, 16-byte aligned), kArgLoads in flight per thread
     const float4 *L4 = reinterpret_cast<const float4 *>(L);
     const int n4 = (V + 3) / 4;
-    for (int c0 = tid; c0 < n4; c0 += 4 * 256) {
-        float4 q[4];
+    for (int c0 = tid; c0 < n4; c0 += kArgLoads * kArgThreads) {
+        float4 q[kArgLoads];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int c = c0 + u * 256;
+        for (int u = 0; u < kArgLoads; ++u) {
+            const int c = c0 + u * kArgThreads;
             q[u] = c < n4 ? L4[c] : make_float4(-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX);
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int c = c0 + u * 256;
+        for (int u = 0; u < kArgLoads; ++u) {
+            const int c = c0 + u * kArgThreads;
             const float vals[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -1743,12 +1746,20 @@ __global__ void __launch_bounds__(256) argmax_rows_kernel(const float *logits, i
         wi[tid >> 5] = besti;
     }
     __syncthreads();
-    if (tid == 0) {
-        for (int w = 1; w < 8; ++w)
-            if (better(wv[w], wi[w], best, besti)) {
-                best = wv[w];
-                besti = wi[w];
+    if (tid < 32) {   // the warps' bests; the first-maximum order makes any reduction order give the same
+        best = wv[tid];
+        besti = wi[tid];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+            if (better(ov, oi, best, besti)) {
+                best = ov;
+                besti = oi;
             }
+        }
+    }
+    if (tid == 0) {
         if (besti == INT_MAX) besti = 0;   // every logit NaN
         if (tokens) tokens[r] = besti;
         if (values) values[r] = best;
@@ -2034,7 +2045,7 @@ void launch_lm_head_rows(const float *x, const WT *wte, float *logits, int E, in
 void launch_argmax_rows(const float *logits, int V, int Vp, int nrows, int forbid_eos, int *tokens, float *values,
                         int *tok_next, int *pos_next, int *out_tokens, int out_stride, const int *step_ptr,
                         cudaStream_t st) {
-    launch_pdl(argmax_rows_kernel, dim3(nrows), dim3(256), 0, st, logits, V, Vp, forbid_eos, tokens, values, tok_next, pos_next,
+    launch_pdl(argmax_rows_kernel, dim3(nrows), dim3(kArgThreads), 0, st, logits, V, Vp, forbid_eos, tokens, values, tok_next, pos_next,
                                               out_tokens, out_stride, step_ptr);
 }
 
