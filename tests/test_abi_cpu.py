@@ -212,6 +212,19 @@ def test_open_bad_args(tiny_model):
     assert g2.lib.g2_open(tiny_model.encode(), 0, 1, 7, C.byref(h)) == -1
 
 
+def test_topk_argument_checks_without_device():
+    """g2_topk and g2k_topk reject bad arguments on the host before any device work
+    (every call below fails a check that precedes the launch)."""
+    vals, ids = (C.c_float * 4)(), (C.c_int * 4)()
+    assert g2.lib.g2_topk(None, 0, 1, vals, ids) == -1                        # null engine
+    assert g2.lib.g2k_topk(None, 100, 1, C.cast(vals, C.c_void_p), C.cast(ids, C.c_void_p), None) == -1
+    buf = (C.c_float * 100)()
+    for n, k in ((100, 0), (100, 101), (1000, 257), (0, 1), (-5, 1)):        # k in [1, min(256, n)]
+        assert g2.lib.g2k_topk(C.cast(buf, C.c_void_p), n, k, C.cast(vals, C.c_void_p),
+                               C.cast(ids, C.c_void_p), None) == -6, (n, k)
+    assert "g2k_topk" in g2.lib.g2_last_error().decode()
+
+
 def test_linear_layout_model_validates(tmp_path):
     """nn.Linear [out,in] files are accepted (transposed at load, main.c:1252-1300)."""
     d = synth.make_model(str(tmp_path / "lin"), synth.TINY, seed=3, layout="linear")
