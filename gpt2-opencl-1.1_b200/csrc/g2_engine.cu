@@ -98,6 +98,7 @@ struct g2_engine {
     float *logits = nullptr, *logits_rows = nullptr;
     float *gemv_partial = nullptr, *attn_partial = nullptr, *lm_partial = nullptr;
     unsigned *gemv_ctr = nullptr, *attn_ctr = nullptr, *lm_ctr = nullptr;
+    size_t gemv_ctr_n = 0, attn_ctr_n = 0;   // counters in each array (zeroed again after an expired wait)
     int *rows_tok = nullptr, *rows_pos = nullptr, *rows_slot = nullptr;
     int *result = nullptr, *argmax_out = nullptr, *batch_step = nullptr, *out_tokens = nullptr;
     StepState *state = nullptr;
@@ -645,8 +646,10 @@ extern "C" int g2_open(const char *model_dir, int device, int max_batch, int dty
     }
     TRY(dalloc(e, &e->gemv_partial, gp));
     TRY(dalloc(e, &e->gemv_ctr, gt));
+    e->gemv_ctr_n = gt;
     TRY(dalloc(e, &e->attn_partial, attn_partial_floats(R, NH, S)));
     TRY(dalloc(e, &e->attn_ctr, attn_counter_count(R, NH)));
+    e->attn_ctr_n = attn_counter_count(R, NH);
     TRY(dalloc(e, &e->lm_partial, (size_t)2 * lm_head_blocks()));
     TRY(dalloc(e, &e->lm_ctr, 1));
     TRY(dalloc(e, &e->rows_tok, R));
@@ -1214,6 +1217,17 @@ int check_flags() {
 // any kernel.  The two error words are copied to pinned memory behind the
 // caller's own copies on the stream, so one synchronisation serves both (a
 // token of the host loop pays one host round trip, not three).
+// After an expired wait: a kernel that gave up may have left a cross-CTA (or
+// cross-warp) arrival counter part-way, so every counter array is zeroed on the
+// stream before the next kernel.
+static int reset_counters(g2_engine *e) {
+    if (e->gemv_ctr) CK(cudaMemsetAsync(e->gemv_ctr, 0, e->gemv_ctr_n * sizeof(unsigned), e->st));
+    if (e->attn_ctr) CK(cudaMemsetAsync(e->attn_ctr, 0, e->attn_ctr_n * sizeof(unsigned), e->st));
+    if (e->lm_ctr) CK(cudaMemsetAsync(e->lm_ctr, 0, sizeof(unsigned), e->st));
+    if (e->tc_ctr) CK(cudaMemsetAsync(e->tc_ctr, 0, (size_t)kTcMaxTiles * sizeof(unsigned), e->st));
+    return G2_OK;
+}
+
 static int sync_and_check(g2_engine *e) {
     int *h = e->h_small + 4 * (size_t)e->max_batch;   // the two spare ints
     h[0] = h[1] = 0;
@@ -1224,10 +1238,13 @@ static int sync_and_check(g2_engine *e) {
         return set_err(G2_ERR_RANGE, "bounds check failed in a kernel (site %d, G2_CHECK build)", site);
     if (h[0]) {
         CK(cudaMemsetAsync(e->tc_err, 0, sizeof(int), e->st));   // ordered before the stream's next kernels
-        return set_err(G2_ERR_TIMEOUT, "tensor-core GEMM: a bounded device-side wait expired");
+        if (const int rc = reset_counters(e)) return rc;
+        return set_err(G2_ERR_TIMEOUT, "tensor-core GEMM or batched attention: a bounded device-side wait expired");
     }
     if (const int code = h[1]) {
         CK(cudaMemsetAsync(e->d_err, 0, sizeof(int), e->st));
+        if (code != kErrClamp)
+            if (const int rc = reset_counters(e)) return rc;
         if (code == kErrClamp)
             return set_err(G2_ERR_RANGE, "decode kernel: an accumulator contribution exceeded +-2^21 and was clamped");
         return set_err(G2_ERR_TIMEOUT, "decode kernel: a bounded device-side wait expired (site %d)", code);
