@@ -1048,15 +1048,18 @@ __global__ void __launch_bounds__(kAsThreads, 3)
 //     TMA into its own three-stage ring, the first stages before the wait for
 //     the previous kernel (the cached rows before each step's position were
 //     written by earlier steps);
-//   * sums q from c_attn's split-K partials at a run's start, and at a run's last
-//     chunk the new K and V rows, which it appends to the cache (split_kv,
-//     math.cl:367-383) and patches into the staged tiles;
-//   * computes the chunk's scores (K tile x q) and P.V (P x V tile, V read
-//     transposed by ldmatrix) with m16n8k16 tensor-core operations, fp16 operands
-//     (q and the probabilities rounded to fp16, as the fp16 engine's GEMM operands
-//     are) and fp32 accumulation, and keeps the run's online softmax -- running
-//     maximum, sum and the 64 outputs, the latter in the MMA accumulators --
-//     in registers;
+//   * sums q from c_attn's split-K partials at a run's start, together with the
+//     new K and V rows when its share holds the run's last chunk; it appends
+//     those to the cache (split_kv, math.cl:367-383) and patches them into the
+//     staged tile at the step's position;
+//   * computes the chunk's scores (K tile x q: the keys on the MMA's m, q as
+//     column 0 of B) and P.V as V^T P (the dims on m, the V tile read transposed
+//     by ldmatrix as the A operand, P as column 0 of B) with m16n8k16 tensor-core
+//     operations -- 32 a chunk, each using one column of its 8, which is why
+//     the time of a chunk follows their count -- fp16 operands (q and the
+//     probabilities rounded to fp16, as the fp16 engine's GEMM operands are) and
+//     fp32 accumulation, and keeps the run's online softmax -- running maximum,
+//     sum and the 64 outputs, the latter in the MMA accumulators -- in registers;
 //   * at the end of its share of a run writes the output (and the next GEMM's
 //     operand), or hands in a partial that the last warp of the run to arrive
 //     merges in slice order.
